@@ -1,0 +1,698 @@
+// Decode-step kernels: one lockstep position for batch <= 16 rows per launch
+// (larger batches are split into chunks of 16 by the entry points).
+//
+// Every weight matrix is streamed from HBM exactly once per step: a warp owns
+// a pair of output rows, keeps the (normalised) activations of all rows of
+// the batch in shared memory, and reduces its per-lane partial sums with a
+// transpose-reduction so that lane l ends up owning (row, batch) = (l / B, l % B).
+#include <math.h>
+
+#include "common.cuh"
+
+namespace dh {
+namespace {
+
+constexpr int kGemvWarps = 8;
+constexpr int kMaxRows = 16;  // rows of the batch handled per launch
+constexpr float kNormEps = 1.1920928955078125e-07f;  // fp32 machine epsilon (torch RMSNorm, eps=None)
+
+// After this, lane l holds the warp-wide sum of v[l % NV] (NV a power of two <= 32).
+template <int NV>
+__device__ __forceinline__ float transpose_reduce(float (&v)[NV]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int n = NV; n > 1; n >>= 1) {
+    const int o = n >> 1;
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = upper ? v[i] : v[i + n / 2];
+      const float keep = upper ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  float r = v[0];
+#pragma unroll
+  for (int o = NV; o < 32; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+  return r;
+}
+
+struct GemvIn {
+  const void* x;                 // (batch, K): fp32 when x_f32, else bf16
+  int x_f32;
+  const __nv_bfloat16* norm_w;   // nullable: RMSNorm weight applied to x
+  int K;
+  int batch;
+};
+
+// ---- epilogues: rows(u) names the two weight rows of work unit u;
+//      store() receives, in each lane, the dot product of row `row` of unit u
+//      with batch row b, and the partner row's value for the same b.
+struct EpiMixerIn {  // W3 = [W_in; W1x; W1s], adjacent row pairs
+  const __nv_bfloat16* w;
+  int d, K, max_len;
+  __nv_bfloat16 *v0, *a, *bh;
+  const int64_t* t_buf;
+  __device__ int units() const { return 3 * d / 2; }
+  __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
+    r0 = w + (size_t)(2 * u) * K;
+    r1 = r0 + K;
+    return true;
+  }
+  __device__ void store(int u, int b, int row, float v, float, bool) const {
+    const int n = 2 * u + row, seg = n / d, c = n % d;
+    if (seg == 0) v0[(size_t)b * d + c] = f2bf(v);
+    else if (seg == 1) a[(size_t)b * d + c] = f2bf(v);
+    else bh[((size_t)b * max_len + *t_buf) * d + c] = f2bf(v);
+  }
+};
+
+struct EpiResidual {  // x[b, n] += v
+  const __nv_bfloat16* w;
+  int N, K;
+  float* x;
+  __device__ int units() const { return N / 2; }
+  __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
+    r0 = w + (size_t)(2 * u) * K;
+    r1 = r0 + K;
+    return true;
+  }
+  __device__ void store(int u, int b, int row, float v, float, bool) const {
+    x[(size_t)b * N + 2 * u + row] += v;
+  }
+};
+
+struct EpiSwiglu {  // unit j = (gate row j, up row j) -> silu(g) * u
+  const __nv_bfloat16 *wg, *wu;
+  int ff, K;
+  __nv_bfloat16* out;
+  __device__ int units() const { return ff; }
+  __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
+    r0 = wg + (size_t)u * K;
+    r1 = wu + (size_t)u * K;
+    return true;
+  }
+  __device__ void store(int u, int b, int row, float v, float other, bool) const {
+    if (row != 0) return;
+    const float g = v, up = other;
+    out[(size_t)b * ff + u] = f2bf(g / (1.0f + expf(-g)) * up);
+  }
+};
+
+struct EpiQkvRope {  // [Wq; Wk; Wv], row pairs (2j, 2j+1) rotated for q and k
+  const __nv_bfloat16* w;
+  int d, K, hd, max_len;
+  const float *cosT, *sinT;
+  __nv_bfloat16 *q, *kc, *vc;
+  const int64_t* t_buf;
+  __device__ int units() const { return 3 * d / 2; }
+  __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
+    r0 = w + (size_t)(2 * u) * K;
+    r1 = r0 + K;
+    return true;
+  }
+  __device__ void store(int u, int b, int row, float v, float other, bool) const {
+    const int n = 2 * u + row, seg = n / d, c = n % d;
+    const int64_t t = *t_buf;
+    float out = v;
+    if (seg < 2) {
+      const int j = (c % hd) >> 1;
+      const float cs = cosT[t * (hd / 2) + j], sn = sinT[t * (hd / 2) + j];
+      const float x1 = row == 0 ? v : other, x2 = row == 0 ? other : v;
+      out = row == 0 ? (x1 * cs - x2 * sn) : (x1 * sn + x2 * cs);
+    }
+    if (seg == 0) q[(size_t)b * d + c] = f2bf(out);
+    else if (seg == 1) kc[((size_t)b * max_len + t) * d + c] = f2bf(out);
+    else vc[((size_t)b * max_len + t) * d + c] = f2bf(out);
+  }
+};
+
+struct EpiLogits {  // rows of E, odd vocab handled by a half-empty last unit
+  const __nv_bfloat16* w;
+  int V, K;
+  __nv_bfloat16* out;
+  __device__ int units() const { return (V + 1) / 2; }
+  __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
+    r0 = w + (size_t)(2 * u) * K;
+    const bool has1 = 2 * u + 1 < V;
+    r1 = has1 ? r0 + K : r0;
+    return has1;
+  }
+  __device__ void store(int u, int b, int row, float v, float, bool has1) const {
+    if (row == 1 && !has1) return;
+    out[(size_t)b * V + 2 * u + row] = f2bf(v);
+  }
+};
+
+template <int MAXB, class Epi>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvIn in, Epi epi) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [batch][K]
+  __shared__ float s_rstd[MAXB];
+  const int K = in.K, batch = in.batch;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nunits = epi.units();
+  const int gw = blockIdx.x * kGemvWarps + warp;
+  const int wstride = gridDim.x * kGemvWarps;
+
+  // weights do not depend on x: start pulling this warp's first rows into L2
+  if (gw < nunits) {
+    const __nv_bfloat16 *r0, *r1;
+    epi.rows(gw, r0, r1);
+    for (int k = lane * 64; k < K; k += 32 * 64) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(r0 + k));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(r1 + k));
+    }
+  }
+
+  if (in.x_f32) {
+    const float* x = static_cast<const float*>(in.x);
+    if (in.norm_w) {
+      for (int b = warp; b < batch; b += kGemvWarps) {
+        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)b * K);
+        float ss = 0.f;
+        for (int i = lane; i < K / 4; i += 32) {
+          const float4 v = xr[i];
+          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) s_rstd[b] = rsqrtf(ss / (float)K + kNormEps);
+      }
+      __syncthreads();
+    }
+    const int k4 = K / 4;
+    for (int i = threadIdx.x; i < batch * k4; i += blockDim.x) {
+      const int b = i / k4, k = (i - b * k4) * 4;
+      float4 v = reinterpret_cast<const float4*>(x + (size_t)b * K)[k / 4];
+      if (in.norm_w) {
+        const float r = s_rstd[b];
+        v.x = v.x * r * bf2f(in.norm_w[k]);
+        v.y = v.y * r * bf2f(in.norm_w[k + 1]);
+        v.z = v.z * r * bf2f(in.norm_w[k + 2]);
+        v.w = v.w * r * bf2f(in.norm_w[k + 3]);
+      }
+      uint2 pk;
+      pk.x = pack2(v.x, v.y);
+      pk.y = pack2(v.z, v.w);
+      *reinterpret_cast<uint2*>(xs + (size_t)b * K + k) = pk;
+    }
+  } else {
+    const uint4* x = static_cast<const uint4*>(in.x);
+    for (int i = threadIdx.x; i < batch * K / 8; i += blockDim.x)
+      reinterpret_cast<uint4*>(xs)[i] = x[i];
+  }
+  __syncthreads();
+
+  for (int u = gw; u < nunits; u += wstride) {
+    const __nv_bfloat16 *r0, *r1;
+    const bool has1 = epi.rows(u, r0, r1);
+    float acc[2 * MAXB];
+#pragma unroll
+    for (int i = 0; i < 2 * MAXB; ++i) acc[i] = 0.f;
+#pragma unroll 2
+    for (int k = lane * 8; k < K; k += 256) {
+      float fa[8], fb[8];
+      unpack8(ld_stream16(r0 + k), fa);
+      unpack8(ld_stream16(r1 + k), fb);
+#pragma unroll
+      for (int b = 0; b < MAXB; ++b) {
+        if (b < batch) {
+          float fx[8];
+          unpack8(*reinterpret_cast<const uint4*>(xs + (size_t)b * K + k), fx);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            acc[b] = fmaf(fa[j], fx[j], acc[b]);
+            acc[MAXB + b] = fmaf(fb[j], fx[j], acc[MAXB + b]);
+          }
+        }
+      }
+    }
+    const float r = transpose_reduce<2 * MAXB>(acc);
+    const float other = __shfl_xor_sync(0xffffffffu, r, MAXB);
+    const int b = lane % MAXB, row = (lane / MAXB) & 1;
+    if (lane < 2 * MAXB && b < batch) epi.store(u, b, row, r, other, has1);
+  }
+}
+
+template <int MAXB, class Epi>
+int launch_gemv_b(const GemvIn& in, const Epi& epi, int nunits, cudaStream_t st) {
+  const size_t smem = (size_t)MAXB * in.K * sizeof(__nv_bfloat16);
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaFuncSetAttribute(gemv_kernel<MAXB, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kMaxRows * 2816 * 2 + 8192);
+    configured_dev = dev;
+  }
+  int grid = (nunits + kGemvWarps - 1) / kGemvWarps;
+  const int cap = sm_count() * 16;
+  if (grid > cap) grid = cap;
+  gemv_kernel<MAXB, Epi><<<grid, kGemvWarps * 32, smem, st>>>(in, epi);
+  return check_launch("gemv_kernel");
+}
+
+template <class Epi>
+int launch_gemv(GemvIn in, const Epi& epi, int nunits, cudaStream_t st) {
+  if (in.K % 8 != 0 || in.K > 2816 * 2)
+    return set_error(DH_ERR_SHAPE, "gemv: K=%d must be a multiple of 8 and <= 5632", in.K);
+  if (in.batch <= 0 || in.batch > kMaxRows)
+    return set_error(DH_ERR_SHAPE, "gemv: batch chunk %d outside [1, 16]", in.batch);
+  if ((size_t)in.batch * in.K * 2 > (size_t)kMaxRows * 2816 * 2 + 8192)
+    return set_error(DH_ERR_SHAPE, "gemv: batch*K too large for shared memory");
+  if (in.batch == 1) return launch_gemv_b<1>(in, epi, nunits, st);
+  if (in.batch == 2) return launch_gemv_b<2>(in, epi, nunits, st);
+  if (in.batch <= 4) return launch_gemv_b<4>(in, epi, nunits, st);
+  if (in.batch <= 8) return launch_gemv_b<8>(in, epi, nunits, st);
+  return launch_gemv_b<16>(in, epi, nunits, st);
+}
+
+// ---------------------------------------------------------------- tree step
+struct TreeStepParams {
+  const __nv_bfloat16 *a, *bh, *wi, *wf, *wr;
+  const float *bi, *bf, *br;
+  const int64_t* t_buf;
+  float *ig, *fg;
+  __nv_bfloat16* rg;
+  const __nv_bfloat16* v0;
+  __nv_bfloat16* ring;
+  __nv_bfloat16* y;
+  int* counters;
+  int batch, max_len, L, H, hd, gh, S;
+};
+
+// grid (L, H): block (level l, head h) forms the three gate readouts of head h
+// at level l for every row, then the last of the L blocks of head h to finish
+// runs the level recurrence of head h (no block ever waits on another).
+template <int MAXB>
+__global__ void __launch_bounds__(128) tree_step_kernel(TreeStepParams p) {
+  const int l = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int L = p.L, H = p.H, gh = p.gh, d = H * p.hd;
+  const long long t = *p.t_buf;
+  const long long src = t - (1ll << l);
+  const bool ok = src >= 0;
+  const long long srcc = ok ? src : 0;
+
+  float acc[MAXB][3];
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) acc[b][0] = acc[b][1] = acc[b][2] = 0.f;
+  const size_t wrow = ((size_t)l * H + h) * gh;
+  for (int k = tid * 8; k < gh; k += 128 * 8) {
+    float fi[8], ff[8], fr[8];
+    unpack8(ld_stream16(p.wi + wrow + k), fi);
+    unpack8(ld_stream16(p.wf + wrow + k), ff);
+    unpack8(ld_stream16(p.wr + wrow + k), fr);
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b) {
+      if (b < p.batch) {
+        float fa[8], fs[8];
+        unpack8(*reinterpret_cast<const uint4*>(p.a + (size_t)b * gh + k), fa);
+        if (ok) {
+          unpack8(*reinterpret_cast<const uint4*>(p.bh + ((size_t)b * p.max_len + srcc) * gh + k),
+                  fs);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) fs[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float hv = fmaxf(fa[j] + fs[j], 0.f);
+          hv *= hv;  // relu squared
+          acc[b][0] = fmaf(fi[j], hv, acc[b][0]);
+          acc[b][1] = fmaf(ff[j], hv, acc[b][1]);
+          acc[b][2] = fmaf(fr[j], hv, acc[b][2]);
+        }
+      }
+    }
+  }
+  __shared__ float red[4][MAXB * 3];
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) {
+#pragma unroll
+    for (int g = 0; g < 3; ++g) {
+      const float v = warp_sum(acc[b][g]);
+      if (lane == 0) red[warp][b * 3 + g] = v;
+    }
+  }
+  __syncthreads();
+  if (tid < p.batch) {
+    const int b = tid;
+    float pre[3];
+#pragma unroll
+    for (int g = 0; g < 3; ++g) pre[g] = red[0][b * 3 + g] + red[1][b * 3 + g] + red[2][b * 3 + g] + red[3][b * 3 + g];
+    const int lh = l * H + h;
+    const float okf = ok ? 1.f : 0.f;
+    const float ig = sigmoidf_(pre[0] + p.bi[lh]) * okf;
+    const float fg = sigmoidf_(pre[1] + p.bf[lh]) * okf + (1.f - okf);
+    const float rg = sigmoidf_(pre[2] + p.br[lh]);
+    p.ig[((size_t)b * L + l) * H + h] = ig;
+    p.fg[((size_t)b * L + l) * H + h] = fg;
+    p.rg[(((size_t)b * p.max_len + t) * L + l) * H + h] = f2bf(rg);
+    __threadfence();
+  }
+  __syncthreads();
+  __shared__ int s_last;
+  if (tid == 0) s_last = (atomicAdd(&p.counters[h], 1) == L - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  // level recurrence for head h (fused_step.py:62-88 semantics, fp32 state)
+  const int groups = p.hd / 8;
+  for (int idx = tid; idx < p.batch * groups; idx += blockDim.x) {
+    const int b = idx / groups;
+    const int c0 = h * p.hd + (idx - b * groups) * 8;
+    __nv_bfloat16* ringb = p.ring + (size_t)b * p.S * d;
+    float V[8];
+    const uint4 v0 = *reinterpret_cast<const uint4*>(p.v0 + (size_t)b * d + c0);
+    unpack8(v0, V);
+    *reinterpret_cast<uint4*>(ringb + (size_t)(t & 1) * d + c0) = v0;  // ring 0 at t
+    for (int lv = 0; lv < L; ++lv) {
+      const long long s = t - (1ll << lv);
+      const float fgv = __ldcg(p.fg + ((size_t)b * L + lv) * H + h);
+      if (s >= 0) {
+        const float igv = __ldcg(p.ig + ((size_t)b * L + lv) * H + h);
+        const float rgv = bf2f(p.rg[(((size_t)b * p.max_len + s) * L + lv) * H + h]);
+        const long long slot = ((2ll << lv) - 2) + (s & ((2ll << lv) - 1));
+        float vs[8];
+        unpack8(*reinterpret_cast<const uint4*>(ringb + (size_t)slot * d + c0), vs);
+        const float coef = igv * rgv;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) V[j] = fgv * V[j] + coef * vs[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) V[j] = fgv * V[j];
+      }
+      if (lv + 1 < L) {
+        const long long slot = ((2ll << (lv + 1)) - 2) + (t & ((2ll << (lv + 1)) - 1));
+        *reinterpret_cast<uint4*>(ringb + (size_t)slot * d + c0) = pack8(V);
+      }
+    }
+    *reinterpret_cast<uint4*>(p.y + (size_t)b * d + c0) = pack8(V);
+  }
+  if (tid == 0) p.counters[h] = 0;
+}
+
+// ---------------------------------------------------------------- attention
+struct AttnParams {
+  const __nv_bfloat16 *q, *k, *v;
+  __nv_bfloat16* y;
+  const int64_t* t_buf;
+  float* part;
+  int* counters;
+  int max_len, H, window, chunk_cap;
+};
+
+__device__ __forceinline__ float block_reduce_128(float v, float* sred, bool is_max) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = is_max ? warp_max(v) : warp_sum(v);
+  __syncthreads();
+  if (lane == 0) sred[warp] = v;
+  __syncthreads();
+  float r = sred[0];
+#pragma unroll
+  for (int w = 1; w < 4; ++w) r = is_max ? fmaxf(r, sred[w]) : r + sred[w];
+  return r;
+}
+
+// grid (H, batch, nsplit), 128 threads, hd = 64.
+__global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
+  constexpr int HD = 64;
+  extern __shared__ float sc[];  // [chunk_cap]
+  __shared__ float sq[HD];
+  __shared__ float sred[4];
+  __shared__ float sacc[4][HD];
+  __shared__ int s_last;
+  const int h = blockIdx.x, b = blockIdx.y, split = blockIdx.z, nsplit = gridDim.z;
+  const int tid = threadIdx.x;
+  const int H = p.H, d = H * HD;
+  const long long t = *p.t_buf;
+  const long long lo = p.window > 0 ? (t + 1 - p.window > 0 ? t + 1 - p.window : 0) : 0;
+  const long long n = t + 1 - lo;
+  const long long chunk = (n + nsplit - 1) / nsplit;
+  const long long s0 = lo + split * chunk;
+  long long s1 = s0 + chunk;
+  if (s1 > t + 1) s1 = t + 1;
+  const int cnt = s1 > s0 ? (int)(s1 - s0) : 0;
+  if (tid < HD) sq[tid] = bf2f(p.q[(size_t)b * d + h * HD + tid]);
+  __syncthreads();
+  const float scale = rsqrtf((float)HD);
+
+  float mloc = -INFINITY;
+  for (int i = tid; i < cnt; i += 128) {
+    const __nv_bfloat16* kr = p.k + ((size_t)b * p.max_len + s0 + i) * d + h * HD;
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      float f[8];
+      unpack8(reinterpret_cast<const uint4*>(kr)[j], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(f[e], sq[j * 8 + e], s);
+    }
+    s *= scale;
+    sc[i] = s;
+    mloc = fmaxf(mloc, s);
+  }
+  const float M = block_reduce_128(mloc, sred, true);
+  float lsum = 0.f;
+  for (int i = tid; i < cnt; i += 128) {
+    const float e = expf(sc[i] - M);
+    sc[i] = e;
+    lsum += e;
+  }
+  const float Lsum = block_reduce_128(lsum, sred, false);  // includes a barrier after sc writes
+  const int c2 = (tid & 31) * 2, prow = tid >> 5;
+  float a0 = 0.f, a1 = 0.f;
+  for (int i = prow; i < cnt; i += 4) {
+    const __nv_bfloat162 vv = *reinterpret_cast<const __nv_bfloat162*>(
+        p.v + ((size_t)b * p.max_len + s0 + i) * d + h * HD + c2);
+    const float2 f = __bfloat1622float2(vv);
+    a0 = fmaf(sc[i], f.x, a0);
+    a1 = fmaf(sc[i], f.y, a1);
+  }
+  sacc[prow][c2] = a0;
+  sacc[prow][c2 + 1] = a1;
+  __syncthreads();
+  if (nsplit == 1) {
+    if (tid < HD) {
+      const float o = sacc[0][tid] + sacc[1][tid] + sacc[2][tid] + sacc[3][tid];
+      p.y[(size_t)b * d + h * HD + tid] = f2bf(cnt > 0 ? o / Lsum : 0.f);
+    }
+    return;
+  }
+  float* mine = p.part + (((size_t)b * H + h) * nsplit + split) * (HD + 2);
+  if (tid < HD) mine[2 + tid] = sacc[0][tid] + sacc[1][tid] + sacc[2][tid] + sacc[3][tid];
+  if (tid == 0) {
+    mine[0] = cnt > 0 ? M : -INFINITY;
+    mine[1] = cnt > 0 ? Lsum : 0.f;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = (atomicAdd(&p.counters[b * H + h], 1) == nsplit - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float* all = p.part + ((size_t)b * H + h) * nsplit * (HD + 2);
+  float Mx = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) Mx = fmaxf(Mx, __ldcg(all + s * (HD + 2)));
+  if (tid < HD) {
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float ms = __ldcg(all + s * (HD + 2));
+      if (ms == -INFINITY) continue;
+      const float w = expf(ms - Mx);
+      den += w * __ldcg(all + s * (HD + 2) + 1);
+      num += w * __ldcg(all + s * (HD + 2) + 2 + tid);
+    }
+    p.y[(size_t)b * d + h * HD + tid] = f2bf(den > 0.f ? num / den : 0.f);
+  }
+  if (tid == 0) p.counters[b * H + h] = 0;
+}
+
+// ---------------------------------------------------------------- small ones
+__global__ void embed_kernel(const int64_t* tokens, const __nv_bfloat16* emb, float* x, int d,
+                             int vocab, int* status) {
+  const int b = blockIdx.x;
+  long long tok = tokens[b];
+  if (tok < 0 || tok >= vocab) {
+    if (status && threadIdx.x == 0) atomicExch(status, 1);
+    tok = tok < 0 ? 0 : vocab - 1;
+  }
+  for (int c = threadIdx.x * 8; c < d; c += blockDim.x * 8) {
+    float f[8];
+    unpack8(*reinterpret_cast<const uint4*>(emb + (size_t)tok * d + c), f);
+    float4* xo = reinterpret_cast<float4*>(x + (size_t)b * d + c);
+    xo[0] = make_float4(f[0], f[1], f[2], f[3]);
+    xo[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
+__global__ void advance_kernel(int64_t* t) { t[0] += 1; }
+
+}  // namespace
+}  // namespace dh
+
+using namespace dh;
+
+#define BF(p) reinterpret_cast<const __nv_bfloat16*>(p)
+#define BFM(p) reinterpret_cast<__nv_bfloat16*>(p)
+#define STREAM(s) reinterpret_cast<cudaStream_t>(s)
+
+extern "C" int dh_decode_embed(const int64_t* tokens, const void* emb, float* x, int batch, int d,
+                               int vocab, int* status, void* stream) {
+  DH_REQUIRE(tokens && emb && x, DH_ERR_ARG, "dh_decode_embed: null pointer");
+  DH_REQUIRE(batch > 0 && d % 8 == 0 && vocab > 0, DH_ERR_SHAPE, "dh_decode_embed: bad sizes");
+  embed_kernel<<<batch, 128, 0, STREAM(stream)>>>(tokens, BF(emb), x, d, vocab, status);
+  return check_launch("embed_kernel");
+}
+
+extern "C" int dh_decode_mixer_in(const float* x, const void* norm_w, const void* w3, void* v0,
+                                  void* a_out, void* b_hist, const int64_t* t_buf, int max_len,
+                                  int batch, int d, void* stream) {
+  DH_REQUIRE(x && norm_w && w3 && v0 && a_out && b_hist && t_buf, DH_ERR_ARG,
+             "dh_decode_mixer_in: null pointer");
+  DH_REQUIRE(d % 8 == 0 && max_len > 0, DH_ERR_SHAPE, "dh_decode_mixer_in: bad sizes");
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb};
+    EpiMixerIn e{BF(w3), d, d, max_len, BFM(v0) + (size_t)b0 * d, BFM(a_out) + (size_t)b0 * d,
+                 BFM(b_hist) + (size_t)b0 * max_len * d, t_buf};
+    int rc = launch_gemv(in, e, 3 * d / 2, STREAM(stream));
+    if (rc) return rc;
+  }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_tree_step(const void* a_in, const void* b_hist, const void* wi,
+                                   const void* wf, const void* wr, const float* bi,
+                                   const float* bf, const float* br, const int64_t* t_buf,
+                                   float* ig, float* fg, void* rg_hist, const void* v0,
+                                   void* v_ring, void* y, int* counters, int batch, int max_len,
+                                   int L, int H, int hd, int gh, void* stream) {
+  DH_REQUIRE(a_in && b_hist && wi && wf && wr && bi && bf && br && t_buf && ig && fg && rg_hist &&
+                 v0 && v_ring && y && counters,
+             DH_ERR_ARG, "dh_decode_tree_step: null pointer");
+  DH_REQUIRE(L >= 1 && L <= 30 && H >= 1 && hd % 8 == 0 && gh % 8 == 0 && batch > 0,
+             DH_ERR_SHAPE, "dh_decode_tree_step: bad sizes (L=%d H=%d hd=%d gh=%d)", L, H, hd, gh);
+  const int d = H * hd, S = (1 << (L + 1)) - 2;
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    TreeStepParams p{BF(a_in) + (size_t)b0 * gh,
+                     BF(b_hist) + (size_t)b0 * max_len * gh,
+                     BF(wi), BF(wf), BF(wr), bi, bf, br, t_buf,
+                     ig + (size_t)b0 * L * H, fg + (size_t)b0 * L * H,
+                     BFM(rg_hist) + (size_t)b0 * max_len * L * H,
+                     BF(v0) + (size_t)b0 * d,
+                     BFM(v_ring) + (size_t)b0 * S * d,
+                     BFM(y) + (size_t)b0 * d,
+                     counters, nb, max_len, L, H, hd, gh, S};
+    dim3 grid(L, H);
+    if (nb == 1) tree_step_kernel<1><<<grid, 128, 0, STREAM(stream)>>>(p);
+    else if (nb <= 4) tree_step_kernel<4><<<grid, 128, 0, STREAM(stream)>>>(p);
+    else tree_step_kernel<16><<<grid, 128, 0, STREAM(stream)>>>(p);
+    int rc = check_launch("tree_step_kernel");
+    if (rc) return rc;
+  }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_linear_residual(const void* y, const void* w, float* x, int batch, int k,
+                                         int d_out, void* stream) {
+  DH_REQUIRE(y && w && x, DH_ERR_ARG, "dh_decode_linear_residual: null pointer");
+  DH_REQUIRE(d_out % 2 == 0, DH_ERR_SHAPE, "dh_decode_linear_residual: odd output width");
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    GemvIn in{BF(y) + (size_t)b0 * k, 0, nullptr, k, nb};
+    EpiResidual e{BF(w), d_out, k, x + (size_t)b0 * d_out};
+    int rc = launch_gemv(in, e, d_out / 2, STREAM(stream));
+    if (rc) return rc;
+  }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_ffn_in(const float* x, const void* norm_w, const void* w_gate,
+                                const void* w_up, void* u, int batch, int d, int ff,
+                                void* stream) {
+  DH_REQUIRE(x && norm_w && w_gate && w_up && u, DH_ERR_ARG, "dh_decode_ffn_in: null pointer");
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb};
+    EpiSwiglu e{BF(w_gate), BF(w_up), ff, d, BFM(u) + (size_t)b0 * ff};
+    int rc = launch_gemv(in, e, ff, STREAM(stream));
+    if (rc) return rc;
+  }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_attn_in(const float* x, const void* norm_w, const void* wqkv,
+                                 const float* rope_cos, const float* rope_sin, void* q,
+                                 void* k_cache, void* v_cache, const int64_t* t_buf, int max_len,
+                                 int batch, int d, int H, void* stream) {
+  DH_REQUIRE(x && norm_w && wqkv && rope_cos && rope_sin && q && k_cache && v_cache && t_buf,
+             DH_ERR_ARG, "dh_decode_attn_in: null pointer");
+  DH_REQUIRE(H > 0 && d % H == 0 && (d / H) % 2 == 0, DH_ERR_SHAPE, "dh_decode_attn_in: bad heads");
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb};
+    EpiQkvRope e{BF(wqkv), d, d, d / H, max_len, rope_cos, rope_sin,
+                 BFM(q) + (size_t)b0 * d, BFM(k_cache) + (size_t)b0 * max_len * d,
+                 BFM(v_cache) + (size_t)b0 * max_len * d, t_buf};
+    int rc = launch_gemv(in, e, 3 * d / 2, STREAM(stream));
+    if (rc) return rc;
+  }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_attn(const void* q, const void* k_cache, const void* v_cache, void* y,
+                              const int64_t* t_buf, float* part, int* counters, int nsplit,
+                              int batch, int max_len, int H, int hd, int window, void* stream) {
+  DH_REQUIRE(q && k_cache && v_cache && y && t_buf, DH_ERR_ARG, "dh_decode_attn: null pointer");
+  DH_REQUIRE(hd == 64, DH_ERR_SHAPE, "dh_decode_attn: head_dim %d unsupported (64 only)", hd);
+  DH_REQUIRE(nsplit >= 1 && nsplit <= 64, DH_ERR_SHAPE, "dh_decode_attn: nsplit %d", nsplit);
+  DH_REQUIRE(nsplit == 1 || (part && counters), DH_ERR_ARG,
+             "dh_decode_attn: nsplit > 1 needs part and counters scratch");
+  const int span = (window > 0 && window < max_len) ? window : max_len;
+  const int cap = (span + nsplit - 1) / nsplit;
+  DH_REQUIRE(cap <= 12288, DH_ERR_SHAPE, "dh_decode_attn: window chunk %d too large", cap);
+  const size_t smem = (size_t)cap * sizeof(float);
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         12288 * 4);
+    configured_dev = dev;
+  }
+  const int d = H * hd;
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    AttnParams p{BF(q) + (size_t)b0 * d, BF(k_cache) + (size_t)b0 * max_len * d,
+                 BF(v_cache) + (size_t)b0 * max_len * d, BFM(y) + (size_t)b0 * d, t_buf,
+                 part ? part + (size_t)b0 * H * nsplit * (hd + 2) : nullptr,
+                 counters ? counters + (size_t)b0 * H : nullptr, max_len, H, window, cap};
+    attn_decode_kernel<<<dim3(H, nb, nsplit), 128, smem, STREAM(stream)>>>(p);
+    int rc = check_launch("attn_decode_kernel");
+    if (rc) return rc;
+  }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_logits(const float* x, const void* norm_w, const void* emb, void* logits,
+                                int batch, int d, int vocab, void* stream) {
+  DH_REQUIRE(x && norm_w && emb && logits, DH_ERR_ARG, "dh_decode_logits: null pointer");
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb};
+    EpiLogits e{BF(emb), vocab, d, BFM(logits) + (size_t)b0 * vocab};
+    int rc = launch_gemv(in, e, (vocab + 1) / 2, STREAM(stream));
+    if (rc) return rc;
+  }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_advance(int64_t* t_buf, void* stream) {
+  DH_REQUIRE(t_buf, DH_ERR_ARG, "dh_decode_advance: null pointer");
+  advance_kernel<<<1, 1, 0, STREAM(stream)>>>(t_buf);
+  return check_launch("advance_kernel");
+}

@@ -1,0 +1,237 @@
+"""B200 incremental decoder: the drop-in for the reference's
+`FusedGraphedHybridDecoder` (dispatcher_hybrid/decoding.py:446-488).
+
+Same public surface as the reference decoders (decoding.py:101-338):
+
+    dec = FusedGraphedHybridDecoder(model)      # model in bfloat16 on CUDA
+    logits = dec.prefill(ids)                   # ids (T,) or (B, T)
+    logits = dec.step(tokens)                   # scalar / (1,) / (B,)
+    dec.t, dec.max_len, dec.batch, dec.caches
+
+and the same cache layouts (B_hist, rg_hist, V_ring with ring offsets and
+masks; k/v with RoPE'd keys), so cache contents and slot positions compare
+element for element with the reference's eager decoder.
+
+One step is the sequence of C-ABI calls recorded by `_record_step` and
+captured once into a CUDA graph; the position lives on the device in
+`t_buf` and is advanced inside the graph.  Every kernel of the step is a
+hand-written sm_100a kernel of `libdispatcher_b200.so`; there is no other
+compute path (construction fails without CUDA or the library).
+"""
+
+import math
+
+import torch
+
+from . import _lib
+from .packing import PackedModel, config_of
+
+
+def _ptr(t):
+    return ctypes_void(t.data_ptr()) if t is not None else None
+
+
+def ctypes_void(p):
+    import ctypes
+    return ctypes.c_void_p(p)
+
+
+class TreeLayerCache:
+    """Reference `_TreeLayerCache` layout (decoding.py:50-76)."""
+
+    def __init__(self, batch, max_len, gh, L, H, hd, device, dtype):
+        self.L, self.H, self.hd = L, H, hd
+        d = H * hd
+        self.B_hist = torch.zeros(batch, max_len, gh, device=device, dtype=dtype)
+        self.rg_hist = torch.zeros(batch, max_len, L, H, device=device, dtype=dtype)
+        self.S = 2 ** (L + 1) - 2
+        self.V_ring = torch.zeros(batch, self.S, d, device=device, dtype=dtype)
+        self.offsets = torch.tensor([2 ** (j + 1) - 2 for j in range(L)], device=device)
+        self.masks = torch.tensor([2 ** (j + 1) - 1 for j in range(L)], device=device)
+
+
+class AttnCache:
+    """Reference `_AttnCache` layout (decoding.py:79-86); RoPE tables in fp32."""
+
+    def __init__(self, batch, max_len, H, hd, device, dtype):
+        self.k = torch.zeros(batch, max_len, H, hd, device=device, dtype=dtype)
+        self.v = torch.zeros_like(self.k)
+        theta = 10000.0 ** (-torch.arange(0, hd, 2, dtype=torch.float32) / hd)
+        ang = torch.arange(max_len, dtype=torch.float32)[:, None] * theta[None, :]
+        self.rope_cos = ang.cos().to(device).contiguous()
+        self.rope_sin = ang.sin().to(device).contiguous()
+
+
+def check_single_document(cfg, ids):
+    """decoding.py:89-98: the decoders implement the wrap mask only."""
+    if getattr(cfg, "doc_reset", False) and bool((ids == cfg.eot_token).any()):
+        raise ValueError(
+            f"prompt contains the document separator (token {cfg.eot_token}) and this "
+            f"model was trained with doc_reset=True; the incremental decoders assume a "
+            f"single document. Remove the separator, or use model.generate().")
+
+
+class FusedGraphedHybridDecoder:
+    """Exact per-token decoder on B200 kernels, one CUDA-graph replay per token."""
+
+    def __init__(self, model, max_len=None, dtype=None):
+        if not torch.cuda.is_available():
+            raise RuntimeError("FusedGraphedHybridDecoder requires CUDA")
+        param_dtype = next(model.parameters()).dtype
+        if dtype is not None and dtype != param_dtype:            # decoding.py:119-122
+            raise ValueError(
+                f"decoder dtype {dtype} != model dtype {param_dtype}; cast the "
+                f"model first, e.g. model.to(torch.bfloat16)")
+        _lib.load()                                               # fail now, not mid-step
+        self.m = model
+        self.cfg = config_of(model)
+        self.max_len = max_len or self.cfg.max_len
+        if self.max_len > self.cfg.max_len or self.max_len & (self.max_len - 1):
+            raise ValueError(f"max_len {self.max_len} must be a power of two <= "
+                             f"{self.cfg.max_len}")
+        self.dtype = param_dtype
+        self.w = PackedModel(model)
+        self.device = self.w.device
+        self.caches = None
+        self.batch = None
+        self.graph = None
+        self.t = 0
+        self._squeeze = False
+
+    # ------------------------------------------------------------ buffers
+    def _alloc(self, batch):
+        if self.caches is not None and self.batch == batch:
+            for c in self.caches:          # a new prompt starts from empty caches
+                for name in ("B_hist", "rg_hist", "V_ring", "k", "v"):
+                    if hasattr(c, name):
+                        getattr(c, name).zero_()
+            return
+        cfg, dev, dt = self.cfg, self.device, self.dtype
+        H, d = cfg.num_heads, cfg.d_model
+        hd, L = d // H, cfg.levels
+        self.batch = batch
+        slots = cfg.attn_slots()
+        self.caches = [AttnCache(batch, self.max_len, H, hd, dev, dt) if i in slots else
+                       TreeLayerCache(batch, self.max_len, d, L, H, hd, dev, dt)
+                       for i in range(cfg.num_layers)]
+        f32, bf = torch.float32, torch.bfloat16
+        ff = cfg.dim_feedforward
+        self.token_buf = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.t_buf = torch.zeros(1, dtype=torch.long, device=dev)
+        self.logits_out = torch.zeros(batch, cfg.vocab_size, device=dev, dtype=bf)
+        self.x = torch.zeros(batch, d, device=dev, dtype=f32)
+        self.v0 = torch.zeros(batch, d, device=dev, dtype=bf)
+        self.a = torch.zeros(batch, d, device=dev, dtype=bf)
+        self.y = torch.zeros(batch, d, device=dev, dtype=bf)
+        self.q = torch.zeros(batch, d, device=dev, dtype=bf)
+        self.u = torch.zeros(batch, ff, device=dev, dtype=bf)
+        self.ig = torch.zeros(batch, L, H, device=dev, dtype=f32)
+        self.fg = torch.zeros(batch, L, H, device=dev, dtype=f32)
+        sm = torch.cuda.get_device_properties(dev).multi_processor_count
+        self.nsplit = max(1, min(16, math.ceil(2 * sm / max(1, min(batch, 16) * H))))
+        self.part = torch.zeros(batch, H, self.nsplit, hd + 2, device=dev, dtype=f32)
+        self.counters = torch.zeros(H + batch * H, device=dev, dtype=torch.int32)
+        self.status = torch.zeros(1, device=dev, dtype=torch.int32)
+        self.graph = None
+
+    # ------------------------------------------------------------ one step
+    def _record_step(self, stream):
+        """Issue every kernel of one decode step on `stream` (captured once)."""
+        cfg, W, B = self.cfg, self.w, self.batch
+        d, H, L, ff = cfg.d_model, cfg.num_heads, cfg.levels, cfg.dim_feedforward
+        hd = d // H
+        V = cfg.vocab_size
+        s = ctypes_void(stream)
+        P = _ptr
+        call = _lib.call
+        call("dh_decode_embed", P(self.token_buf), P(W.emb), P(self.x), B, d, V,
+             P(self.status), s)
+        tree_ctr = self.counters[:H]
+        attn_ctr = self.counters[H:]
+        for lay, cache in zip(W.layers, self.caches):
+            if lay["kind"] == "tree":
+                call("dh_decode_mixer_in", P(self.x), P(lay["norm1"]), P(lay["w3"]), P(self.v0),
+                     P(self.a), P(cache.B_hist), P(self.t_buf), self.max_len, B, d, s)
+                call("dh_decode_tree_step", P(self.a), P(cache.B_hist), P(lay["wi"]),
+                     P(lay["wf"]), P(lay["wr"]), P(lay["bi"]), P(lay["bf"]), P(lay["br"]),
+                     P(self.t_buf), P(self.ig), P(self.fg), P(cache.rg_hist), P(self.v0),
+                     P(cache.V_ring), P(self.y), P(tree_ctr), B, self.max_len, L, H, hd, d, s)
+            else:
+                call("dh_decode_attn_in", P(self.x), P(lay["norm1"]), P(lay["wqkv"]),
+                     P(cache.rope_cos), P(cache.rope_sin), P(self.q), P(cache.k), P(cache.v),
+                     P(self.t_buf), self.max_len, B, d, H, s)
+                call("dh_decode_attn", P(self.q), P(cache.k), P(cache.v), P(self.y),
+                     P(self.t_buf), P(self.part), P(attn_ctr), self.nsplit, B, self.max_len,
+                     H, hd, cfg.attn_window, s)
+            call("dh_decode_linear_residual", P(self.y), P(lay["w_out"]), P(self.x), B, d, d, s)
+            call("dh_decode_ffn_in", P(self.x), P(lay["norm2"]), P(lay["w_gate"]),
+                 P(lay["w_up"]), P(self.u), B, d, ff, s)
+            call("dh_decode_linear_residual", P(self.u), P(lay["w_down"]), P(self.x), B, ff, d, s)
+        call("dh_decode_logits", P(self.x), P(W.norm_out), P(W.lm_head), P(self.logits_out),
+             B, d, V, s)
+        call("dh_decode_advance", P(self.t_buf), s)
+
+    def _capture(self):
+        """decoding.py:317-328: warm up on a side stream, then capture one step."""
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        saved_t = int(self.t)
+        with torch.cuda.stream(side):
+            self._record_step(side.cuda_stream)   # warm-up: binds lazy attributes
+        torch.cuda.current_stream().wait_stream(side)
+        with torch.cuda.graph(g):
+            self._record_step(torch.cuda.current_stream().cuda_stream)
+        self.t_buf.fill_(saved_t)
+        self.graph = g
+
+    # ------------------------------------------------------------ public
+    @torch.no_grad()
+    def prefill(self, idx):
+        """idx: (T,) or (B, T) token ids -> (T, vocab) / (B, T, vocab) logits.
+
+        The prompt runs through the captured step one position at a time,
+        which fills every cache exactly as the step will later read it."""
+        self._squeeze = idx.dim() == 1
+        ids = idx.view(1, -1) if self._squeeze else idx
+        check_single_document(self.cfg, ids)
+        T = ids.shape[1]
+        if T > self.max_len:
+            raise ValueError(f"prompt of {T} exceeds max_len {self.max_len}")
+        if T < 1:
+            raise ValueError("empty prompt")
+        ids = ids.to(self.device)
+        self._alloc(ids.shape[0])
+        self.t = 0
+        self.t_buf.zero_()
+        if self.graph is None:
+            self._capture()
+        out = torch.empty(self.batch, T, self.cfg.vocab_size, device=self.device,
+                          dtype=self.logits_out.dtype)
+        for p in range(T):
+            self.token_buf.copy_(ids[:, p])
+            self.graph.replay()
+            out[:, p].copy_(self.logits_out)
+        self.t = T
+        return out[0] if self._squeeze else out
+
+    @torch.no_grad()
+    def step(self, tokens):
+        """tokens: scalar / (1,) / (B,) -> (vocab,) or (B, vocab)."""
+        if self.graph is None:
+            raise RuntimeError("call prefill() before step()")
+        if self.t >= self.max_len:                                 # decoding.py:289-290
+            raise ValueError(f"context exhausted at max_len {self.max_len}")
+        toks = tokens.view(-1)
+        if toks.shape[0] != self.batch:
+            raise ValueError(f"got {toks.shape[0]} tokens for batch {self.batch}")
+        self.token_buf.copy_(toks)
+        self.graph.replay()
+        self.t += 1
+        out = self.logits_out.clone()
+        return out[0] if self._squeeze else out
+
+
+# the reference's name for the graphed decoder without fused kernels maps to
+# the same implementation: on B200 every decoder runs the fused step
+GraphedHybridDecoder = FusedGraphedHybridDecoder

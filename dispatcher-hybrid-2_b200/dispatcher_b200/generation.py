@@ -1,0 +1,58 @@
+"""`fast_generate` on the B200 decoder (modeling_dispatcher.py:379-442).
+
+Identical sampling semantics: temperature floor 1e-6, top-k by k-th value,
+multinomial or argmax, eos freezing, stop at max_len.  The decoder names
+of the reference ("auto", "eager", "graphed", "fused") are accepted; all of
+them run the B200 decoder, since that is the only compute path here.
+"""
+
+import torch
+import torch.nn.functional as F
+
+from .decoding import FusedGraphedHybridDecoder
+
+DECODERS = {"fused": FusedGraphedHybridDecoder, "graphed": FusedGraphedHybridDecoder,
+            "eager": FusedGraphedHybridDecoder, "b200": FusedGraphedHybridDecoder}
+
+
+@torch.no_grad()
+def fast_generate(model, input_ids, max_new_tokens=50, do_sample=False, temperature=1.0,
+                  top_k=None, eos_token_id=None, num_return_sequences=1, decoder="auto"):
+    ids = input_ids.view(1, -1) if input_ids.dim() == 1 else input_ids
+    if num_return_sequences > 1:
+        if ids.shape[0] != 1:
+            raise ValueError("num_return_sequences needs a single prompt")
+        if not do_sample:
+            raise ValueError("num_return_sequences without sampling would "
+                             "return identical rows")
+        ids = ids.expand(num_return_sequences, -1)
+    if decoder == "auto":
+        dec = FusedGraphedHybridDecoder(model)
+    elif isinstance(decoder, str):
+        if decoder not in DECODERS:
+            raise KeyError(decoder)
+        dec = DECODERS[decoder](model)
+    else:
+        dec = decoder
+    Bb = ids.shape[0]
+    logits = dec.prefill(ids)[:, -1]
+    finished = torch.zeros(Bb, dtype=torch.bool, device=ids.device)
+    out = [ids]
+    for _ in range(max_new_tokens):
+        logits = logits.float() / max(temperature, 1e-6)
+        if top_k is not None:
+            kth = torch.topk(logits, top_k, dim=-1).values[:, -1:]
+            logits = logits.masked_fill(logits < kth, float("-inf"))
+        nxt = (torch.multinomial(F.softmax(logits, dim=-1), 1)[:, 0] if do_sample
+               else logits.argmax(-1))
+        nxt = nxt.to(ids.device)
+        if eos_token_id is not None:
+            nxt = torch.where(finished, torch.full_like(nxt, eos_token_id), nxt)
+            finished = finished | (nxt == eos_token_id)
+        out.append(nxt.unsqueeze(1))
+        if eos_token_id is not None and bool(finished.all()):
+            break
+        if dec.t >= dec.max_len:
+            break
+        logits = dec.step(nxt)
+    return torch.cat(out, dim=1)

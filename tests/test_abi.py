@@ -1,0 +1,62 @@
+"""CPU-side checks of the C ABI and the host logic (no GPU needed)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from dispatcher_b200 import _lib, build
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    decl = _lib.parse_header()
+    assert len(decl) >= 10
+    for name in decl:
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+    assert b"sm_100a" in lib.dh_version()
+
+
+def test_header_declarations_cover_all_exports():
+    """Every exported dh_* symbol is declared in the public header."""
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.lib_path()],
+                         capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\bT (dh_\w+)", out))
+    assert exported == set(_lib.parse_header()), exported ^ set(_lib.parse_header())
+
+
+def test_errors_are_reported_not_trapped():
+    """Argument validation fails with a status and a message, on the host."""
+    with pytest.raises(_lib.DispatcherB200Error, match="null pointer"):
+        _lib.call("dh_decode_advance", None, None)
+    lib = _lib.load()
+    rc = lib.dh_decode_attn(None, None, None, None, None, None, None, 1, 1, 16, 2, 64, 0, None)
+    assert rc == 2 and b"null" in lib.dh_last_error()
+
+
+def test_library_is_built_for_sm100a_only():
+    assert build.ARCH_FLAGS == ["-gencode", "arch=compute_100a,code=sm_100a"]
+    assert os.path.exists(build.LIB_PATH)
+
+
+def test_decoder_refuses_without_cuda():
+    if torch.cuda.is_available():
+        pytest.skip("CUDA present")
+    from dispatcher_b200 import FusedGraphedHybridDecoder, DispatcherHybridForCausalLM, small_config
+    m = DispatcherHybridForCausalLM(small_config())
+    with pytest.raises(RuntimeError, match="requires CUDA"):
+        FusedGraphedHybridDecoder(m)
+
+
+def test_ring_layout_constants():
+    """Ring j: 2^(j+1) slots at offset 2^(j+1)-2; S = 2^(L+1)-2 (8190 at L=12)."""
+    import oracle
+    L = 12
+    offs = oracle.RING_OFFSETS(L)
+    assert offs[-1] + 2 ** L == 2 ** (L + 1) - 2 == 8190
+    for j in range(L):
+        slots = {oracle.ring_slot(j, t) for t in range(5000, 5000 + 2 ** (j + 1))}
+        assert slots == set(range(offs[j], offs[j] + 2 ** (j + 1)))

@@ -1,0 +1,197 @@
+"""Parity of the B200 decoder with the oracle (the reference's eager decoder
+restated), on seeded random-init weights.  Mirrors the reference's
+tests/test_decoding.py contract: decoder vs parallel forward, caches and
+ring slot positions, batched vs solo rows, error behaviour."""
+
+import pytest
+import torch
+
+import oracle
+from dispatcher_b200 import (DispatcherHybridForCausalLM, FusedGraphedHybridDecoder,
+                             DispatcherConfig, small_config, make_state_dict)
+from tests.helpers import bf16_bound, cast_sd, decisive_argmax_ok, max_err
+
+pytestmark = pytest.mark.gpu
+
+
+def build(cfg, seed, nondeg):
+    sd32 = make_state_dict(cfg, seed=seed, nondegenerate=nondeg)
+    model = DispatcherHybridForCausalLM(cfg, seed=seed, nondegenerate=nondeg)
+    model = model.to("cuda", torch.bfloat16).eval()
+    return model, sd32
+
+
+@pytest.fixture(scope="module")
+def small_nd():
+    return (small_config(),) + build(small_config(), 1, True)
+
+
+@pytest.fixture(scope="module")
+def small_s0():
+    return (small_config(),) + build(small_config(), 0, False)
+
+
+def _compare(cfg, model, sd32, prompt=48, steps=12, seed=0, batch=1):
+    """Reference `_compare` (tests/test_decoding.py:33-44): decoder logits at
+    positions prompt.. vs the parallel forward's, here against the fp32
+    oracle with the bf16 bound measured from the oracle's own bf16 run."""
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, cfg.vocab_size - 1, (batch, prompt + steps), generator=g)
+    ref32 = oracle.forward(sd32, cfg, ids)[:, prompt - 1:]
+    ref16 = oracle.forward(cast_sd(sd32, torch.bfloat16), cfg, ids)[:, prompt - 1:].float()
+    dec = FusedGraphedHybridDecoder(model)
+    pre = dec.prefill(ids[:, :prompt].cuda())
+    got = [pre[:, -1].float()]
+    for t in range(prompt, prompt + steps):
+        got.append(dec.step(ids[:, t].cuda()).float())
+    got = torch.stack(got, 1)[:, :-1].cpu()
+    ref32, ref16 = ref32[:, :-1], ref16[:, :-1]
+    err = max_err(got, ref32)
+    bound = bf16_bound(ref32, ref16)
+    assert err < bound, f"max|dlogit| {err:.4f} vs fp32 exceeds bf16 bound {bound:.4f}"
+    ok, agree = decisive_argmax_ok(got, ref32, err)
+    assert ok, f"decisive argmax flip (agreement {agree:.3f})"
+    return dec, ids, err, bound
+
+
+def test_decoder_matches_forward_small_nondegenerate(small_nd):
+    _compare(*small_nd)
+
+
+def test_decoder_matches_forward_small_seed0(small_s0):
+    _compare(*small_s0)
+
+
+def test_decoder_batched(small_nd):
+    _compare(*small_nd, batch=3, seed=5)
+
+
+def test_prefill_logits_match_forward(small_nd):
+    cfg, model, sd32 = small_nd
+    g = torch.Generator().manual_seed(11)
+    ids = torch.randint(0, cfg.vocab_size - 1, (2, 70), generator=g)
+    ref32 = oracle.forward(sd32, cfg, ids)
+    ref16 = oracle.forward(cast_sd(sd32, torch.bfloat16), cfg, ids).float()
+    got = FusedGraphedHybridDecoder(model).prefill(ids.cuda()).float().cpu()
+    assert max_err(got, ref32) < bf16_bound(ref32, ref16)
+
+
+def test_caches_and_ring_slots_match_oracle(small_nd):
+    """Ring contents, B/rg histories and KV caches after prefill + steps; the
+    set of written ring slots must be identical (slot indexing is exact)."""
+    cfg, model, sd32 = small_nd
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, cfg.vocab_size - 1, (2, 37), generator=g)
+    nexts = torch.randint(0, cfg.vocab_size - 1, (2, 9), generator=g)
+    ref = oracle.OracleDecoder(sd32, cfg)
+    ref.prefill(prompt)
+    dec = FusedGraphedHybridDecoder(model)
+    dec.prefill(prompt.cuda())
+    for j in range(9):
+        ref.step(nexts[:, j])
+        dec.step(nexts[:, j].cuda())
+    T = 37 + 9
+    for i, (rc, mc) in enumerate(zip(ref.caches, dec.caches)):
+        if hasattr(rc, "V_ring"):
+            r_ring, m_ring = rc.V_ring, mc.V_ring.float().cpu()
+            assert torch.equal(r_ring != 0, m_ring != 0), f"layer {i}: ring slot pattern differs"
+            assert max_err(m_ring, r_ring) < 0.05 * r_ring.abs().max().item() + 1e-2
+            assert max_err(mc.B_hist[:, :T].float().cpu(), rc.B_hist[:, :T]) < 0.02 * rc.B_hist.abs().max().item() + 1e-3
+            assert max_err(mc.rg_hist[:, :T].float().cpu(), rc.rg_hist[:, :T]) < 0.02
+            assert not mc.B_hist[:, T:].any() and not mc.rg_hist[:, T:].any()
+        else:
+            assert max_err(mc.k[:, :T].float().cpu(), rc.k[:, :T]) < 0.02 * rc.k.abs().max().item() + 1e-3
+            assert max_err(mc.v[:, :T].float().cpu(), rc.v[:, :T]) < 0.02 * rc.v.abs().max().item() + 1e-3
+            assert not mc.k[:, T:].any()
+
+
+def test_ring_slot_positions_are_bit_exact(small_nd):
+    """After t positions, ring j holds exactly the slots of positions
+    max(0, t-2^(j+1)) .. t-1 (decoding.py:63-76); every other slot is zero."""
+    cfg, model, _ = small_nd
+    L = cfg.levels
+    for T in (1, 2, 3, 7, 64, 129):
+        ids = torch.randint(0, cfg.vocab_size - 1, (1, T))
+        dec = FusedGraphedHybridDecoder(model)
+        dec.prefill(ids.cuda())
+        ring = dec.caches[0].V_ring[0].float().cpu()
+        written = ring.abs().sum(-1) != 0
+        expect = torch.zeros_like(written)
+        for j in range(L):
+            for p in range(max(0, T - 2 ** (j + 1)), T):
+                expect[oracle.ring_slot(j, p)] = True
+        assert torch.equal(written, expect), f"T={T}: ring slots differ"
+
+
+def test_batched_equals_solo(small_nd):
+    cfg, model, _ = small_nd
+    g = torch.Generator().manual_seed(0)
+    prompts = torch.randint(0, cfg.vocab_size - 1, (3, 40), generator=g).cuda()
+    nexts = torch.randint(0, cfg.vocab_size - 1, (3, 8), generator=g).cuda()
+    dec = FusedGraphedHybridDecoder(model)
+    batched = [dec.prefill(prompts)[:, -1]]
+    batched += [dec.step(nexts[:, j]) for j in range(8)]
+    batched = torch.stack(batched, 1).float()
+    for b in range(3):
+        solo = FusedGraphedHybridDecoder(model)
+        s = [solo.prefill(prompts[b])[-1]] + [solo.step(nexts[b, j]) for j in range(8)]
+        gap = max_err(torch.stack(s).float(), batched[b])
+        assert gap < 0.02, f"row {b}: batched vs solo {gap:.3e}"
+
+
+def test_errors_match_reference_behaviour(small_nd):
+    cfg, model, _ = small_nd
+    dec = FusedGraphedHybridDecoder(model, max_len=64)
+    bad = torch.tensor([3, 4, cfg.eot_token, 5]).cuda()
+    with pytest.raises(ValueError, match="document separator"):
+        dec.prefill(bad)
+    with pytest.raises(ValueError, match="exceeds max_len"):
+        dec.prefill(torch.ones(65, dtype=torch.long).cuda())
+    dec.prefill(torch.ones(63, dtype=torch.long).cuda())
+    dec.step(torch.tensor([1]).cuda())
+    with pytest.raises(ValueError, match="context exhausted"):
+        dec.step(torch.tensor([1]).cuda())
+    with pytest.raises(ValueError, match="dtype"):
+        FusedGraphedHybridDecoder(model, dtype=torch.float32)
+    with pytest.raises(ValueError, match="tokens for batch"):
+        d2 = FusedGraphedHybridDecoder(model)
+        d2.prefill(torch.ones(2, 5, dtype=torch.long).cuda())
+        d2.step(torch.ones(3, dtype=torch.long).cuda())
+
+
+def test_fast_generate_greedy_tracks_oracle(small_nd):
+    cfg, model, sd32 = small_nd
+    ids = torch.tensor([[464, 118, 286, 262]])
+    got = model.fast_generate(ids.cuda(), max_new_tokens=10).cpu()
+    # teacher-forced check: each generated token is the fp32 argmax unless
+    # the fp32 top-2 margin is inside the bf16 noise
+    logits = oracle.forward(sd32, cfg, got[:, :-1])[0, 3:]
+    top2 = torch.topk(logits, 2, -1).values
+    decisive = (top2[:, 0] - top2[:, 1]) > 0.05
+    agree = logits.argmax(-1) == got[0, 4:]
+    assert bool((agree | ~decisive).all())
+    assert got.shape == (1, 14) and torch.equal(got[:, :4], ids)
+
+
+def test_fast_generate_sampling_and_eos(small_nd):
+    cfg, model, _ = small_nd
+    torch.manual_seed(0)
+    ids = torch.tensor([[464, 118, 286, 262]]).cuda()
+    out = model.fast_generate(ids, max_new_tokens=6, do_sample=True, temperature=0.8, top_k=50,
+                              num_return_sequences=3)
+    assert out.shape == (3, 10) and (out[:, :4] == ids).all()
+    two = torch.randint(0, cfg.vocab_size - 1, (2, 8)).cuda()
+    first = int(model.fast_generate(two[:1], max_new_tokens=1)[0, -1])
+    out = model.fast_generate(two, max_new_tokens=6, eos_token_id=first)
+    assert int(out[0, 8]) == first and (out[0, 8:] == first).all()
+
+
+@pytest.mark.slow
+def test_full_config_decode_vs_oracle():
+    """Default 292M config: prefill 48 + 4 steps against the fp32 oracle."""
+    cfg = DispatcherConfig()
+    model, sd32 = build(cfg, 0, False)
+    _compare(cfg, model, sd32, prompt=48, steps=4)
+    del model
+    model, sd32 = build(cfg, 1, True)
+    _compare(cfg, model, sd32, prompt=48, steps=4, seed=1)
