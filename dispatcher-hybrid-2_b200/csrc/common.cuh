@@ -248,4 +248,21 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);   // M / 16
 }
 
+// ---------------------------------------------------------------------------
+// programmatic dependent launch + bulk L2 prefetch
+// ---------------------------------------------------------------------------
+// Let the next kernel in the stream start its prologue (it still waits for
+// this grid's completion before touching our outputs).
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Block until the preceding grid has completed and its writes are visible
+// (a no-op when the kernel was launched without the programmatic attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Fire-and-forget prefetch of [p, p+bytes) into L2 (bytes % 16 == 0).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 }  // namespace dh

@@ -16,6 +16,24 @@ constexpr int kGemvWarps = 8;
 constexpr int kMaxRows = 16;  // rows of the batch handled per launch
 constexpr float kNormEps = 1.1920928955078125e-07f;  // fp32 machine epsilon (torch RMSNorm, eps=None)
 
+// Launch with programmatic stream serialization: the kernel may begin while
+// its predecessor drains; every kernel here calls pdl_wait() before touching
+// data that a predecessor writes.
+template <typename Kern, typename... Args>
+int launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess ? 0 : 1;
+}
+
 // After this, lane l holds the warp-wide sum of v[l % NV] (NV a power of two <= 32).
 template <int NV>
 __device__ __forceinline__ float transpose_reduce(float (&v)[NV]) {
@@ -149,21 +167,26 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvIn in, Epi ep
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [batch][K]
   __shared__ float s_rstd[MAXB];
+  pdl_trigger();
   const int K = in.K, batch = in.batch;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nunits = epi.units();
-  const int gw = blockIdx.x * kGemvWarps + warp;
-  const int wstride = gridDim.x * kGemvWarps;
+  // each CTA owns a contiguous run of units, so its weight rows are contiguous
+  const int upc = (nunits + gridDim.x - 1) / gridDim.x;
+  const int u_begin = blockIdx.x * upc;
+  const int u_end = min(nunits, u_begin + upc);
 
-  // weights do not depend on x: start pulling this warp's first rows into L2
-  if (gw < nunits) {
-    const __nv_bfloat16 *r0, *r1;
-    epi.rows(gw, r0, r1);
-    for (int k = lane * 64; k < K; k += 32 * 64) {
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(r0 + k));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(r1 + k));
+  // weights do not depend on the previous kernel: pull this warp's rows
+  // into L2 while the producer of x is still running
+  if (lane == 0) {
+    for (int u = u_begin + warp; u < u_end; u += kGemvWarps) {
+      const __nv_bfloat16 *r0, *r1;
+      const bool has1 = epi.rows(u, r0, r1);
+      prefetch_l2(r0, (uint32_t)K * 2);
+      if (has1) prefetch_l2(r1, (uint32_t)K * 2);
     }
   }
+  pdl_wait();
 
   if (in.x_f32) {
     const float* x = static_cast<const float*>(in.x);
@@ -203,7 +226,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvIn in, Epi ep
   }
   __syncthreads();
 
-  for (int u = gw; u < nunits; u += wstride) {
+  for (int u = u_begin + warp; u < u_end; u += kGemvWarps) {
     const __nv_bfloat16 *r0, *r1;
     const bool has1 = epi.rows(u, r0, r1);
     float acc[2 * MAXB];
@@ -246,10 +269,11 @@ int launch_gemv_b(const GemvIn& in, const Epi& epi, int nunits, cudaStream_t st)
     configured_dev = dev;
   }
   int grid = (nunits + kGemvWarps - 1) / kGemvWarps;
-  const int cap = sm_count() * 16;
+  const int cap = sm_count() * 8;  // one resident wave of 256-thread CTAs
   if (grid > cap) grid = cap;
-  gemv_kernel<MAXB, Epi><<<grid, kGemvWarps * 32, smem, st>>>(in, epi);
-  return check_launch("gemv_kernel");
+  return launch_pdl(gemv_kernel<MAXB, Epi>, dim3(grid), dim3(kGemvWarps * 32), smem, st, in, epi)
+             ? set_error(DH_ERR_CUDA, "gemv_kernel launch: %s", cudaGetErrorString(cudaGetLastError()))
+             : DH_OK;
 }
 
 template <class Epi>
@@ -286,18 +310,34 @@ struct TreeStepParams {
 // runs the level recurrence of head h (no block ever waits on another).
 template <int MAXB>
 __global__ void __launch_bounds__(128) tree_step_kernel(TreeStepParams p) {
+  constexpr int LMAX = 16;
   const int l = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int L = p.L, H = p.H, gh = p.gh, d = H * p.hd;
+  pdl_trigger();
+  // t_buf is only advanced by the last kernel of a step, and the history rows
+  // at positions < t were written by earlier steps: both are safe to read
+  // before waiting on the producer of A / v0.
   const long long t = *p.t_buf;
   const long long src = t - (1ll << l);
   const bool ok = src >= 0;
   const long long srcc = ok ? src : 0;
+  const size_t wrow = ((size_t)l * H + h) * gh;
+  if (tid == 0) {
+    prefetch_l2(p.wi + wrow, gh * 2);
+    prefetch_l2(p.wf + wrow, gh * 2);
+    prefetch_l2(p.wr + wrow, gh * 2);
+  } else if (ok && tid <= p.batch) {
+    const int b = tid - 1;
+    prefetch_l2(p.bh + ((size_t)b * p.max_len + srcc) * gh, gh * 2);
+    const long long slot = ((2ll << l) - 2) + (srcc & ((2ll << l) - 1));
+    prefetch_l2(p.ring + ((size_t)b * p.S + slot) * d + h * p.hd, p.hd * 2);
+  }
+  pdl_wait();
 
   float acc[MAXB][3];
 #pragma unroll
   for (int b = 0; b < MAXB; ++b) acc[b][0] = acc[b][1] = acc[b][2] = 0.f;
-  const size_t wrow = ((size_t)l * H + h) * gh;
   for (int k = tid * 8; k < gh; k += 128 * 8) {
     float fi[8], ff[8], fr[8];
     unpack8(ld_stream16(p.wi + wrow + k), fi);
@@ -358,35 +398,47 @@ __global__ void __launch_bounds__(128) tree_step_kernel(TreeStepParams p) {
   if (!s_last) return;
   __threadfence();
 
-  // level recurrence for head h (fused_step.py:62-88 semantics, fp32 state)
+  // level recurrence for head h (fused_step.py:62-88 semantics, fp32 state).
+  // Every level's inputs are read before the serial chain: the ring slots
+  // read (positions t - 2^l) never coincide with the slots written (t).
   const int groups = p.hd / 8;
   for (int idx = tid; idx < p.batch * groups; idx += blockDim.x) {
     const int b = idx / groups;
     const int c0 = h * p.hd + (idx - b * groups) * 8;
     __nv_bfloat16* ringb = p.ring + (size_t)b * p.S * d;
+    uint4 vsrc[LMAX];
+    float coef[LMAX], fgv[LMAX];
+#pragma unroll
+    for (int lv = 0; lv < LMAX; ++lv) {
+      if (lv < L) {
+        const long long s = t - (1ll << lv);
+        fgv[lv] = __ldcg(p.fg + ((size_t)b * L + lv) * H + h);
+        coef[lv] = 0.f;
+        vsrc[lv] = make_uint4(0, 0, 0, 0);
+        if (s >= 0) {
+          const float igv = __ldcg(p.ig + ((size_t)b * L + lv) * H + h);
+          const float rgv = bf2f(p.rg[(((size_t)b * p.max_len + s) * L + lv) * H + h]);
+          coef[lv] = igv * rgv;
+          const long long slot = ((2ll << lv) - 2) + (s & ((2ll << lv) - 1));
+          vsrc[lv] = *reinterpret_cast<const uint4*>(ringb + (size_t)slot * d + c0);
+        }
+      }
+    }
     float V[8];
     const uint4 v0 = *reinterpret_cast<const uint4*>(p.v0 + (size_t)b * d + c0);
     unpack8(v0, V);
     *reinterpret_cast<uint4*>(ringb + (size_t)(t & 1) * d + c0) = v0;  // ring 0 at t
-    for (int lv = 0; lv < L; ++lv) {
-      const long long s = t - (1ll << lv);
-      const float fgv = __ldcg(p.fg + ((size_t)b * L + lv) * H + h);
-      if (s >= 0) {
-        const float igv = __ldcg(p.ig + ((size_t)b * L + lv) * H + h);
-        const float rgv = bf2f(p.rg[(((size_t)b * p.max_len + s) * L + lv) * H + h]);
-        const long long slot = ((2ll << lv) - 2) + (s & ((2ll << lv) - 1));
+#pragma unroll
+    for (int lv = 0; lv < LMAX; ++lv) {
+      if (lv < L) {
         float vs[8];
-        unpack8(*reinterpret_cast<const uint4*>(ringb + (size_t)slot * d + c0), vs);
-        const float coef = igv * rgv;
+        unpack8(vsrc[lv], vs);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) V[j] = fgv * V[j] + coef * vs[j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) V[j] = fgv * V[j];
-      }
-      if (lv + 1 < L) {
-        const long long slot = ((2ll << (lv + 1)) - 2) + (t & ((2ll << (lv + 1)) - 1));
-        *reinterpret_cast<uint4*>(ringb + (size_t)slot * d + c0) = pack8(V);
+        for (int j = 0; j < 8; ++j) V[j] = fgv[lv] * V[j] + coef[lv] * vs[j];
+        if (lv + 1 < L) {
+          const long long slot = ((2ll << (lv + 1)) - 2) + (t & ((2ll << (lv + 1)) - 1));
+          *reinterpret_cast<uint4*>(ringb + (size_t)slot * d + c0) = pack8(V);
+        }
       }
     }
     *reinterpret_cast<uint4*>(p.y + (size_t)b * d + c0) = pack8(V);
@@ -427,6 +479,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
   const int h = blockIdx.x, b = blockIdx.y, split = blockIdx.z, nsplit = gridDim.z;
   const int tid = threadIdx.x;
   const int H = p.H, d = H * HD;
+  pdl_trigger();
   const long long t = *p.t_buf;
   const long long lo = p.window > 0 ? (t + 1 - p.window > 0 ? t + 1 - p.window : 0) : 0;
   const long long n = t + 1 - lo;
@@ -435,6 +488,14 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
   long long s1 = s0 + chunk;
   if (s1 > t + 1) s1 = t + 1;
   const int cnt = s1 > s0 ? (int)(s1 - s0) : 0;
+  // cache rows before t were written by earlier steps: warm them into L2
+  for (int i = tid; i < cnt; i += 128) {
+    if (s0 + i < t) {
+      prefetch_l2(p.k + ((size_t)b * p.max_len + s0 + i) * d + h * HD, HD * 2);
+      prefetch_l2(p.v + ((size_t)b * p.max_len + s0 + i) * d + h * HD, HD * 2);
+    }
+  }
+  pdl_wait();
   if (tid < HD) sq[tid] = bf2f(p.q[(size_t)b * d + h * HD + tid]);
   __syncthreads();
   const float scale = rsqrtf((float)HD);
@@ -513,6 +574,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
 // ---------------------------------------------------------------- small ones
 __global__ void embed_kernel(const int64_t* tokens, const __nv_bfloat16* emb, float* x, int d,
                              int vocab, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x;
   long long tok = tokens[b];
   if (tok < 0 || tok >= vocab) {
@@ -528,7 +591,11 @@ __global__ void embed_kernel(const int64_t* tokens, const __nv_bfloat16* emb, fl
   }
 }
 
-__global__ void advance_kernel(int64_t* t) { t[0] += 1; }
+__global__ void advance_kernel(int64_t* t) {
+  pdl_trigger();
+  pdl_wait();
+  t[0] += 1;
+}
 
 }  // namespace
 }  // namespace dh
@@ -543,8 +610,10 @@ extern "C" int dh_decode_embed(const int64_t* tokens, const void* emb, float* x,
                                int vocab, int* status, void* stream) {
   DH_REQUIRE(tokens && emb && x, DH_ERR_ARG, "dh_decode_embed: null pointer");
   DH_REQUIRE(batch > 0 && d % 8 == 0 && vocab > 0, DH_ERR_SHAPE, "dh_decode_embed: bad sizes");
-  embed_kernel<<<batch, 128, 0, STREAM(stream)>>>(tokens, BF(emb), x, d, vocab, status);
-  return check_launch("embed_kernel");
+  if (launch_pdl(embed_kernel, dim3(batch), dim3(128), 0, STREAM(stream), tokens, BF(emb), x, d,
+                 vocab, status))
+    return check_launch("embed_kernel");
+  return DH_OK;
 }
 
 extern "C" int dh_decode_mixer_in(const float* x, const void* norm_w, const void* w3, void* v0,
@@ -573,7 +642,7 @@ extern "C" int dh_decode_tree_step(const void* a_in, const void* b_hist, const v
   DH_REQUIRE(a_in && b_hist && wi && wf && wr && bi && bf && br && t_buf && ig && fg && rg_hist &&
                  v0 && v_ring && y && counters,
              DH_ERR_ARG, "dh_decode_tree_step: null pointer");
-  DH_REQUIRE(L >= 1 && L <= 30 && H >= 1 && hd % 8 == 0 && gh % 8 == 0 && batch > 0,
+  DH_REQUIRE(L >= 1 && L <= 16 && H >= 1 && hd % 8 == 0 && gh % 8 == 0 && batch > 0,
              DH_ERR_SHAPE, "dh_decode_tree_step: bad sizes (L=%d H=%d hd=%d gh=%d)", L, H, hd, gh);
   const int d = H * hd, S = (1 << (L + 1)) - 2;
   for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
@@ -588,11 +657,10 @@ extern "C" int dh_decode_tree_step(const void* a_in, const void* b_hist, const v
                      BFM(y) + (size_t)b0 * d,
                      counters, nb, max_len, L, H, hd, gh, S};
     dim3 grid(L, H);
-    if (nb == 1) tree_step_kernel<1><<<grid, 128, 0, STREAM(stream)>>>(p);
-    else if (nb <= 4) tree_step_kernel<4><<<grid, 128, 0, STREAM(stream)>>>(p);
-    else tree_step_kernel<16><<<grid, 128, 0, STREAM(stream)>>>(p);
-    int rc = check_launch("tree_step_kernel");
-    if (rc) return rc;
+    const int bad = nb == 1   ? launch_pdl(tree_step_kernel<1>, grid, dim3(128), 0, STREAM(stream), p)
+                    : nb <= 4 ? launch_pdl(tree_step_kernel<4>, grid, dim3(128), 0, STREAM(stream), p)
+                              : launch_pdl(tree_step_kernel<16>, grid, dim3(128), 0, STREAM(stream), p);
+    if (bad) return check_launch("tree_step_kernel");
   }
   return DH_OK;
 }
@@ -671,9 +739,8 @@ extern "C" int dh_decode_attn(const void* q, const void* k_cache, const void* v_
                  BF(v_cache) + (size_t)b0 * max_len * d, BFM(y) + (size_t)b0 * d, t_buf,
                  part ? part + (size_t)b0 * H * nsplit * (hd + 2) : nullptr,
                  counters ? counters + (size_t)b0 * H : nullptr, max_len, H, window, cap};
-    attn_decode_kernel<<<dim3(H, nb, nsplit), 128, smem, STREAM(stream)>>>(p);
-    int rc = check_launch("attn_decode_kernel");
-    if (rc) return rc;
+    if (launch_pdl(attn_decode_kernel, dim3(H, nb, nsplit), dim3(128), smem, STREAM(stream), p))
+      return check_launch("attn_decode_kernel");
   }
   return DH_OK;
 }
@@ -693,6 +760,7 @@ extern "C" int dh_decode_logits(const float* x, const void* norm_w, const void* 
 
 extern "C" int dh_decode_advance(int64_t* t_buf, void* stream) {
   DH_REQUIRE(t_buf, DH_ERR_ARG, "dh_decode_advance: null pointer");
-  advance_kernel<<<1, 1, 0, STREAM(stream)>>>(t_buf);
-  return check_launch("advance_kernel");
+  if (launch_pdl(advance_kernel, dim3(1), dim3(1), 0, STREAM(stream), t_buf))
+    return check_launch("advance_kernel");
+  return DH_OK;
 }

@@ -1,0 +1,529 @@
+// Parallel-forward mixer: tree mask, gate readout on the tensor cores, and
+// the dyadic level sweep.
+//
+// Gate readout (replaces fused_gates.py:38-93 and the einsums of
+// modeling_dispatcher.py:100-109).  One CTA owns 128 positions of one
+// sequence.  For every 64-wide slice k of the gate-hidden width and every
+// level l, four builder warps form the hidden tile
+//      H[t, k] = relu(A[t, k] + m(t, l) * B[t - 2^l, k])^2          (bf16)
+// directly in shared memory in the tcgen05 operand layout, and one thread
+// issues tcgen05.mma H x W_l^T into a per-level fp32 accumulator in TMEM
+// (W_l: the 3H gate rows of level l, padded to NP rows).  The (T, L, gh)
+// hidden tensor never exists in HBM.  Shifted B rows come straight from TMA:
+// rows t - 2^l < 0 are out of bounds and arrive as zeros, which is exactly
+// the wrap mask.  The epilogue adds the bias, applies sigmoid and the
+// wrap/doc masks, and writes
+//   mode 0: gates (B, H, L, 3, T) bf16 — admit*m, forget*m + (1-m), transmit
+//   mode 1: pre-activations (B, T, n_lv, H) x 3 bf16 (the reference op)
+// and optionally the transmit gates of every level into a decoder rg_hist.
+//
+// Level sweep (modeling_dispatcher.py:116-120): one CTA per (sequence, head,
+// 8-channel slice) keeps the slice of V for all positions, fp32 in registers,
+// and exchanges bf16 copies through shared memory once per level.
+#include "common.cuh"
+#include "tma.cuh"
+
+namespace dh {
+namespace {
+
+// ------------------------------------------------------------------ mask
+// mask[b, t, l] = (2^l < T) && t >= 2^l && (!doc_reset || doc(t) == doc(t - 2^l)),
+// doc(t) = number of EOT tokens strictly before t (modeling_dispatcher.py:282-323).
+__global__ void __launch_bounds__(1024) tree_mask_kernel(const int64_t* ids, int T, int L,
+                                                         int64_t eot, int doc_reset,
+                                                         uint8_t* mask) {
+  extern __shared__ int sdoc[];  // [T]
+  __shared__ int warp_tot[32];
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (T + 1023) / 1024;
+  const int s0 = tid * per;
+  int cnt = 0;
+  for (int i = 0; i < per; ++i) {
+    const int t = s0 + i;
+    if (t < T && doc_reset && ids[(size_t)b * T + t] == eot) ++cnt;
+  }
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int v = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    warp_tot[lane] = v;  // inclusive over warps
+  }
+  __syncthreads();
+  int run = incl - cnt + (warp > 0 ? warp_tot[warp - 1] : 0);  // exclusive prefix
+  for (int i = 0; i < per; ++i) {
+    const int t = s0 + i;
+    if (t < T) {
+      sdoc[t] = run;
+      if (doc_reset && ids[(size_t)b * T + t] == eot) ++run;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < T * L; i += blockDim.x) {
+    const int t = i / L, l = i - t * L;
+    const int s = 1 << l;
+    uint8_t m = (s < T && t >= s) ? 1 : 0;
+    if (m && doc_reset) m = sdoc[t] == sdoc[t - s];
+    mask[(size_t)b * T * L + i] = m;
+  }
+}
+
+// ------------------------------------------------------------------ gates
+constexpr int kStagesBW = 4;
+constexpr int kTileT = 128;
+constexpr int kSlice = 64;  // gate-hidden columns per step (128 B of bf16)
+constexpr int kSBytes = kTileT * kSlice * 2;  // 16 KB operand tile
+constexpr int kWBytes = 8192;                 // W slot (NP <= 64 rows of 128 B)
+
+struct GateArgs {
+  int B, T, H, L, NP, gh;
+  int n_lv, n_calc, group;
+  const float* bias;  // (L, NP)
+  const uint8_t* mask;
+  int mask_L;
+  int mode;
+  __nv_bfloat16* gates;
+  __nv_bfloat16 *pre_i, *pre_f, *pre_r;
+  __nv_bfloat16* rg_hist;
+  int rg_T;
+  int* err;
+};
+
+constexpr int kGateSmem = 1024 + 2 * kSBytes + kStagesBW * (kSBytes + kWBytes) + 2 * kSBytes + 256;
+
+__global__ void __launch_bounds__(192, 1)
+    gate_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmW, GateArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;                                   // 2 x 16 KB
+  uint8_t* sBW = sA + 2 * kSBytes;                      // stages x (16 KB B + 8 KB W)
+  uint8_t* sH = sBW + kStagesBW * (kSBytes + kWBytes);  // 2 x 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sH + 2 * kSBytes);
+  uint64_t* a_full = bars;
+  uint64_t* a_empty = bars + 2;
+  uint64_t* bw_full = bars + 4;
+  uint64_t* bw_empty = bw_full + kStagesBW;
+  uint64_t* h_full = bw_empty + kStagesBW;
+  uint64_t* h_empty = h_full + 2;
+  uint64_t* d_full = h_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * kTileT, b = blockIdx.y;
+  const int nk = g.gh / kSlice;
+  const int ngroups = (g.n_calc + g.group - 1) / g.group;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 4);
+      mbar_init(&h_full[i], 4);
+      mbar_init(&h_empty[i], 1);
+    }
+    for (int s = 0; s < kStagesBW; ++s) {
+      mbar_init(&bw_full[s], 1);
+      mbar_init(&bw_empty[s], 1);
+    }
+    mbar_init(d_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmW);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------- TMA producer
+      int as = 0, s = 0;
+      uint32_t aph = 0, ph = 0;
+      long fills_a = 0, fills_bw = 0;
+      bool ok = true;
+      for (int grp = 0; grp < ngroups && ok; ++grp) {
+        const int l0 = grp * g.group;
+        const int l1 = min(l0 + g.group, g.n_calc);
+        for (int kc = 0; kc < nk && ok; ++kc) {
+          if (!mbar_wait(&a_empty[as], aph ^ 1, g.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&a_full[as], kSBytes);
+          tma_load_3d(&tmA, &a_full[as], sA + as * kSBytes, kc * kSlice, t0, b);
+          ++fills_a;
+          if (++as == 2) { as = 0; aph ^= 1; }
+          for (int l = l0; l < l1; ++l) {
+            if (!mbar_wait(&bw_empty[s], ph ^ 1, g.err)) { ok = false; break; }
+            uint8_t* slot = sBW + s * (kSBytes + kWBytes);
+            mbar_arrive_expect_tx(&bw_full[s], kSBytes + g.NP * 128);
+            tma_load_3d(&tmB, &bw_full[s], slot, kc * kSlice, t0 - (1 << l), b);
+            tma_load_2d(&tmW, &bw_full[s], slot + kSBytes, kc * kSlice, l * g.NP);
+            ++fills_bw;
+            if (++s == kStagesBW) { s = 0; ph ^= 1; }
+          }
+        }
+      }
+      for (int i = 0; i < 2; ++i) {
+        const long n = fills_a / 2 + (i < fills_a % 2 ? 1 : 0);
+        if (n > 0) mbar_wait(&a_full[i], (uint32_t)((n - 1) & 1), nullptr, 1u << 20);
+      }
+      for (int i = 0; i < kStagesBW; ++i) {
+        const long n = fills_bw / kStagesBW + (i < fills_bw % kStagesBW ? 1 : 0);
+        if (n > 0) mbar_wait(&bw_full[i], (uint32_t)((n - 1) & 1), nullptr, 1u << 20);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---------------- MMA issuer
+      const uint32_t idesc = idesc_bf16(kTileT, g.NP);
+      int s = 0, hs = 0;
+      uint32_t ph = 0, hph = 0;
+      bool ok = true;
+      for (int grp = 0; grp < ngroups && ok; ++grp) {
+        const int l0 = grp * g.group;
+        const int l1 = min(l0 + g.group, g.n_calc);
+        for (int kc = 0; kc < nk && ok; ++kc) {
+          for (int l = l0; l < l1; ++l) {
+            if (!mbar_wait(&bw_full[s], ph, g.err) || !mbar_wait(&h_full[hs], hph, g.err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t hA = smem_u32(sH + hs * kSBytes);
+            const uint32_t wB = smem_u32(sBW + s * (kSBytes + kWBytes) + kSBytes);
+            const uint32_t d = tmem_base + (uint32_t)((l - l0) * g.NP);
+#pragma unroll
+            for (int k = 0; k < kSlice / 16; ++k)
+              umma_bf16(d, sw128_desc(hA + k * 32), sw128_desc(wB + k * 32), idesc,
+                        (kc | k) != 0);
+            umma_commit(&bw_empty[s]);
+            umma_commit(&h_empty[hs]);
+            if (++s == kStagesBW) { s = 0; ph ^= 1; }
+            if (++hs == 2) { hs = 0; hph ^= 1; }
+          }
+        }
+        if (ok) umma_commit(d_full);
+      }
+    }
+  } else {  // ---------------- builders + epilogue (warps 2..5)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // row of the tile == TMEM lane
+    const int t = t0 + r;
+    const bool row_ok = t < g.T;
+    int as = 0, s = 0, hs = 0;
+    uint32_t aph = 0, ph = 0, hph = 0, dph = 0;
+    bool ok = true;
+    for (int grp = 0; grp < ngroups && ok; ++grp) {
+      const int l0 = grp * g.group;
+      const int l1 = min(l0 + g.group, g.n_calc);
+      for (int kc = 0; kc < nk && ok; ++kc) {
+        if (!mbar_wait(&a_full[as], aph, g.err)) { ok = false; break; }
+        const uint8_t* arow = sA + as * kSBytes + r * 128;
+        for (int l = l0; l < l1; ++l) {
+          if (!mbar_wait(&bw_full[s], ph, g.err) || !mbar_wait(&h_empty[hs], hph ^ 1, g.err)) {
+            ok = false;
+            break;
+          }
+          float m = 1.f;
+          if (g.mask) m = (row_ok && g.mask[((size_t)b * g.T + t) * g.mask_L + l]) ? 1.f : 0.f;
+          const uint8_t* brow = sBW + s * (kSBytes + kWBytes) + r * 128;
+          uint8_t* hrow = sH + hs * kSBytes + r * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int off = ((j ^ (r & 7)) << 4);
+            float fa[8], fb[8], fh[8];
+            unpack8(*reinterpret_cast<const uint4*>(arow + off), fa);
+            unpack8(*reinterpret_cast<const uint4*>(brow + off), fb);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              // reference rounding: A + B in the model dtype, then relu^2 in bf16
+              float x = bf2f(f2bf(fa[e] + m * fb[e]));
+              x = fmaxf(x, 0.f);
+              fh[e] = x * x;
+            }
+            *reinterpret_cast<uint4*>(hrow + off) = pack8(fh);
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&h_full[hs]);
+          if (++s == kStagesBW) { s = 0; ph ^= 1; }
+          if (++hs == 2) { hs = 0; hph ^= 1; }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_empty[as]);
+        if (++as == 2) { as = 0; aph ^= 1; }
+      }
+      if (!ok) break;
+      // ---- epilogue of this level group
+      if (!mbar_wait(d_full, dph, g.err)) break;
+      dph ^= 1;
+      tc_fence_after();
+      const int H = g.H;
+      for (int l = l0; l < l1; ++l) {
+        float pre[64];
+        const uint32_t base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((l - l0) * g.NP);
+        for (int c = 0; c < g.NP; c += 16) {
+          uint32_t v[16];
+          tmem_ld16(base + c, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (c + e < 64) pre[c + e] = __uint_as_float(v[e]);
+        }
+        if (!row_ok) continue;
+        const float* bias = g.bias + (size_t)l * g.NP;
+        float m = (t >= (1 << l)) ? 1.f : 0.f;
+        if (g.mask) m = g.mask[((size_t)b * g.T + t) * g.mask_L + l] ? 1.f : 0.f;
+        if (l < g.n_lv) {
+          if (g.mode == 0) {
+            for (int h = 0; h < H; ++h) {
+              const float a = sigmoidf_(pre[h] + bias[h]) * m;
+              const float f = sigmoidf_(pre[H + h] + bias[H + h]) * m + (1.f - m);
+              const float rr = sigmoidf_(pre[2 * H + h] + bias[2 * H + h]);
+              __nv_bfloat16* gp = g.gates + ((((size_t)b * H + h) * g.L + l) * 3) * g.T + t;
+              gp[0] = f2bf(a);
+              gp[g.T] = f2bf(f);
+              gp[2 * (size_t)g.T] = f2bf(rr);
+            }
+          } else {
+            const size_t o = (((size_t)b * g.T + t) * g.n_lv + l) * H;
+            for (int h = 0; h < H; ++h) {
+              g.pre_i[o + h] = f2bf(pre[h] + bias[h]);
+              g.pre_f[o + h] = f2bf(pre[H + h] + bias[H + h]);
+              g.pre_r[o + h] = f2bf(pre[2 * H + h] + bias[2 * H + h]);
+            }
+          }
+        }
+        if (g.rg_hist) {
+          __nv_bfloat16* rp = g.rg_hist + (((size_t)b * g.rg_T + t) * g.L + l) * H;
+          for (int h = 0; h < H; ++h) rp[h] = f2bf(sigmoidf_(pre[2 * H + h] + bias[2 * H + h]));
+        }
+      }
+      tc_fence_before();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ------------------------------------------------------------------ scan
+constexpr int kScanThreads = 512;
+constexpr int kScanPer = 8;  // positions per thread (T <= 4096)
+
+struct ScanArgs {
+  const __nv_bfloat16* v0;
+  int ld_v0;
+  const __nv_bfloat16* gates;  // (B, H, L, 3, T)
+  __nv_bfloat16* out;
+  int ld_out;
+  int B, T, H, hd, L, n_lv;
+  __nv_bfloat16* ring;  // (B, S, d) or null
+  int S;
+};
+
+__global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
+  extern __shared__ uint4 sx[];  // [T] x 8 bf16
+  const int slices = a.hd / 8;
+  const int cc = blockIdx.x % slices;
+  const int h = (blockIdx.x / slices) % a.H;
+  const int b = blockIdx.x / (slices * a.H);
+  const int d = a.H * a.hd;
+  const int col = h * a.hd + cc * 8;
+  const int tid = threadIdx.x;
+  const int T = a.T;
+  float V[kScanPer][8];
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int t = tid + i * kScanThreads;
+    if (t < T) unpack8(*reinterpret_cast<const uint4*>(a.v0 + ((size_t)b * T + t) * a.ld_v0 + col), V[i]);
+  }
+  auto write_ring = [&](int j) {
+    const int lo = T - (2 << j);
+#pragma unroll
+    for (int i = 0; i < kScanPer; ++i) {
+      const int t = tid + i * kScanThreads;
+      if (t < T && t >= lo) {
+        const int slot = ((2 << j) - 2) + (t & ((2 << j) - 1));
+        *reinterpret_cast<uint4*>(a.ring + ((size_t)b * a.S + slot) * d + col) = pack8(V[i]);
+      }
+    }
+  };
+  if (a.ring) write_ring(0);
+  const __nv_bfloat16* gbase = a.gates + (((size_t)b * a.H + h) * a.L) * 3 * (size_t)T;
+  for (int l = 0; l < a.n_lv; ++l) {
+    const int s = 1 << l;
+    if (s > T) break;
+#pragma unroll
+    for (int i = 0; i < kScanPer; ++i) {
+      const int t = tid + i * kScanThreads;
+      if (t < T) sx[t] = pack8(V[i]);
+    }
+    __syncthreads();
+    const __nv_bfloat16* ga = gbase + (size_t)l * 3 * T;
+#pragma unroll
+    for (int i = 0; i < kScanPer; ++i) {
+      const int t = tid + i * kScanThreads;
+      if (t >= T) continue;
+      const float f = bf2f(ga[T + t]);
+      if (t >= s) {
+        const float coef = bf2f(ga[t]) * bf2f(ga[2 * T + t - s]);
+        float vs[8];
+        unpack8(sx[t - s], vs);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) V[i][e] = f * V[i][e] + coef * vs[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) V[i][e] = f * V[i][e];
+      }
+    }
+    if (a.ring && l + 1 < a.L) write_ring(l + 1);
+    __syncthreads();
+  }
+  if (a.ring)
+    for (int j = a.n_lv + 1; j < a.L; ++j) write_ring(j);
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int t = tid + i * kScanThreads;
+    if (t < T) *reinterpret_cast<uint4*>(a.out + ((size_t)b * T + t) * a.ld_out + col) = pack8(V[i]);
+  }
+}
+
+}  // namespace
+}  // namespace dh
+
+using namespace dh;
+
+extern "C" int dh_tree_mask(const int64_t* ids, int batch, int T, int L, int64_t eot,
+                            int doc_reset, uint8_t* mask, void* stream) {
+  DH_REQUIRE(ids && mask, DH_ERR_ARG, "dh_tree_mask: null pointer");
+  DH_REQUIRE(batch > 0 && T > 0 && T <= 16384 && L > 0 && L < 31, DH_ERR_SHAPE,
+             "dh_tree_mask: bad sizes");
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaFuncSetAttribute(tree_mask_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 16384 * 4);
+    configured_dev = dev;
+  }
+  tree_mask_kernel<<<batch, 1024, (size_t)T * sizeof(int), reinterpret_cast<cudaStream_t>(stream)>>>(
+      ids, T, L, eot, doc_reset, mask);
+  return check_launch("tree_mask_kernel");
+}
+
+static int launch_gates(const void* a, int lda, const void* bsrc, int ldb, const void* wg,
+                        GateArgs g, cudaStream_t st) {
+  DH_REQUIRE(a && bsrc && wg && g.bias, DH_ERR_ARG, "mixer gates: null pointer");
+  DH_REQUIRE(g.gh % kSlice == 0 && g.NP % 16 == 0 && g.NP <= 64 && 3 * g.H <= g.NP,
+             DH_ERR_SHAPE, "mixer gates: gh=%d NP=%d H=%d unsupported", g.gh, g.NP, g.H);
+  DH_REQUIRE(g.n_calc >= 1 && g.n_calc <= g.L && g.n_lv <= g.n_calc && g.L <= 30, DH_ERR_SHAPE,
+             "mixer gates: level counts n_lv=%d n_calc=%d L=%d", g.n_lv, g.n_calc, g.L);
+  DH_REQUIRE(lda % 8 == 0 && ldb % 8 == 0, DH_ERR_SHAPE, "mixer gates: row strides must be multiples of 8");
+  g.group = 512 / g.NP;
+  if (g.group > g.n_calc) g.group = g.n_calc;
+  {  // balance the groups
+    const int ng = (g.n_calc + g.group - 1) / g.group;
+    g.group = (g.n_calc + ng - 1) / ng;
+  }
+  CUtensorMap ta, tb, tw;
+  const uint64_t da[3] = {(uint64_t)g.gh, (uint64_t)g.T, (uint64_t)g.B};
+  const uint64_t sa[2] = {(uint64_t)lda * 2, (uint64_t)lda * 2 * g.T};
+  const uint64_t sb[2] = {(uint64_t)ldb * 2, (uint64_t)ldb * 2 * g.T};
+  const uint32_t box3[3] = {kSlice, kTileT, 1};
+  int rc = make_tmap_bf16(&ta, a, 3, da, sa, box3, true);
+  if (rc) return rc;
+  rc = make_tmap_bf16(&tb, bsrc, 3, da, sb, box3, true);
+  if (rc) return rc;
+  const uint64_t dw[2] = {(uint64_t)g.gh, (uint64_t)g.L * g.NP};
+  const uint64_t sw[1] = {(uint64_t)g.gh * 2};
+  const uint32_t bw[2] = {kSlice, (uint32_t)g.NP};
+  rc = make_tmap_bf16(&tw, wg, 2, dw, sw, bw, true);
+  if (rc) return rc;
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaFuncSetAttribute(gate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGateSmem);
+    configured_dev = dev;
+  }
+  dim3 grid((g.T + kTileT - 1) / kTileT, g.B);
+  gate_kernel<<<grid, 192, kGateSmem, st>>>(ta, tb, tw, g);
+  return check_launch("gate_kernel");
+}
+
+extern "C" int dh_mixer_gates(const void* a, int lda, const void* bsrc, int ldb, const void* wg,
+                              const float* bias, const uint8_t* mask, int batch, int T, int H,
+                              int L, int NP, int gh, int n_lv, void* gates, void* rg_hist,
+                              int rg_T, int* status, void* stream) {
+  DH_REQUIRE(gates, DH_ERR_ARG, "dh_mixer_gates: null gates output");
+  GateArgs g{};
+  g.B = batch; g.T = T; g.H = H; g.L = L; g.NP = NP; g.gh = gh;
+  g.n_lv = n_lv;
+  g.n_calc = rg_hist ? L : n_lv;
+  g.bias = bias; g.mask = mask; g.mask_L = L; g.mode = 0;
+  g.gates = reinterpret_cast<__nv_bfloat16*>(gates);
+  g.rg_hist = reinterpret_cast<__nv_bfloat16*>(rg_hist);
+  g.rg_T = rg_T;
+  g.err = status;
+  return launch_gates(a, lda, bsrc, ldb, wg, g, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dh_gate_preacts_fwd(const void* a, int lda, const void* bsrc, int ldb,
+                                   const void* wg, const float* bias, const uint8_t* mask,
+                                   int mask_L, int batch, int T, int H, int L, int NP, int gh,
+                                   int n_lv, void* pre_i, void* pre_f, void* pre_r, int* status,
+                                   void* stream) {
+  DH_REQUIRE(pre_i && pre_f && pre_r, DH_ERR_ARG, "dh_gate_preacts_fwd: null output");
+  GateArgs g{};
+  g.B = batch; g.T = T; g.H = H; g.L = L; g.NP = NP; g.gh = gh;
+  g.n_lv = n_lv; g.n_calc = n_lv;
+  g.bias = bias; g.mask = mask; g.mask_L = mask_L; g.mode = 1;
+  g.pre_i = reinterpret_cast<__nv_bfloat16*>(pre_i);
+  g.pre_f = reinterpret_cast<__nv_bfloat16*>(pre_f);
+  g.pre_r = reinterpret_cast<__nv_bfloat16*>(pre_r);
+  g.err = status;
+  return launch_gates(a, lda, bsrc, ldb, wg, g, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dh_level_scan(const void* v0, int ld_v0, const void* gates, void* out, int ld_out,
+                             int batch, int T, int H, int hd, int L, int n_lv, void* ring,
+                             void* stream) {
+  DH_REQUIRE(v0 && gates && out, DH_ERR_ARG, "dh_level_scan: null pointer");
+  DH_REQUIRE(T > 0 && T <= kScanThreads * kScanPer, DH_ERR_SHAPE,
+             "dh_level_scan: T=%d exceeds %d", T, kScanThreads * kScanPer);
+  DH_REQUIRE(hd % 8 == 0 && ld_v0 % 8 == 0 && ld_out % 8 == 0 && n_lv <= L, DH_ERR_SHAPE,
+             "dh_level_scan: bad sizes");
+  ScanArgs a{reinterpret_cast<const __nv_bfloat16*>(v0), ld_v0,
+             reinterpret_cast<const __nv_bfloat16*>(gates),
+             reinterpret_cast<__nv_bfloat16*>(out), ld_out, batch, T, H, hd, L, n_lv,
+             reinterpret_cast<__nv_bfloat16*>(ring), (1 << (L + 1)) - 2};
+  const int blocks = batch * H * (hd / 8);
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kScanThreads * kScanPer * 16);
+    configured_dev = dev;
+  }
+  scan_kernel<<<blocks, kScanThreads, (size_t)T * 16, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("scan_kernel");
+}

@@ -74,7 +74,7 @@ def small_config(**overrides):
     """A reduced shape used by the parity tests: every kernel path (tree and
     attention blocks, level masking, window clipping, vocab tails) is live,
     at sizes the CPU oracle finishes in well under a second."""
-    kw = dict(vocab_size=515, d_model=128, num_heads=2, dim_feedforward=352,
+    kw = dict(vocab_size=515, d_model=128, num_heads=2, dim_feedforward=384,
               num_layers=4, max_len=256, attn_layers=(2,), attn_window=64,
               eot_token=514, bos_token_id=514, eos_token_id=514)
     kw.update(overrides)

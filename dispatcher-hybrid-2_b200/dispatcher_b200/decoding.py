@@ -95,6 +95,7 @@ class FusedGraphedHybridDecoder:
         self.caches = None
         self.batch = None
         self.graph = None
+        self._engine = None
         self.t = 0
         self._squeeze = False
 
@@ -186,12 +187,7 @@ class FusedGraphedHybridDecoder:
         self.graph = g
 
     # ------------------------------------------------------------ public
-    @torch.no_grad()
-    def prefill(self, idx):
-        """idx: (T,) or (B, T) token ids -> (T, vocab) / (B, T, vocab) logits.
-
-        The prompt runs through the captured step one position at a time,
-        which fills every cache exactly as the step will later read it."""
+    def _prepare_prompt(self, idx):
         self._squeeze = idx.dim() == 1
         ids = idx.view(1, -1) if self._squeeze else idx
         check_single_document(self.cfg, ids)
@@ -202,6 +198,36 @@ class FusedGraphedHybridDecoder:
             raise ValueError("empty prompt")
         ids = ids.to(self.device)
         self._alloc(ids.shape[0])
+        return ids, T
+
+    @torch.no_grad()
+    def prefill(self, idx):
+        """idx: (T,) or (B, T) token ids -> (T, vocab) / (B, T, vocab) logits.
+
+        Runs the parallel forward on the B200 prefill engine, which also fills
+        B_hist, rg_hist (all levels), every level's ring slab and the
+        attention caches (decoding.py:143-185, 225-245), then captures the
+        step graph at position T."""
+        ids, T = self._prepare_prompt(idx)
+        if self.graph is None:
+            # the capture's warm-up step writes position 0, which the
+            # prefill below overwrites; no cache slot keeps a stray value
+            self.t = 0
+            self.t_buf.zero_()
+            self._capture()
+        if self._engine is None:
+            from .engine import PrefillEngine
+            self._engine = PrefillEngine(self.m, packed=self.w)
+        out = self._engine.forward(ids, caches=self.caches)
+        self.t = T
+        self.t_buf.fill_(T)
+        return out[0] if self._squeeze else out
+
+    @torch.no_grad()
+    def prefill_stepwise(self, idx):
+        """Same contract as prefill(), but the prompt runs through the captured
+        step one position at a time (an independent route to the same caches)."""
+        ids, T = self._prepare_prompt(idx)
         self.t = 0
         self.t_buf.zero_()
         if self.graph is None:

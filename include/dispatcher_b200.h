@@ -108,6 +108,94 @@ DH_API int dh_decode_logits(const float* x, const void* norm_w, const void* emb,
 /* t_buf[0] += 1 (decoding.py:443). */
 DH_API int dh_decode_advance(int64_t* t_buf, void* stream);
 
+/* --------------------------------------------------------------- prefill */
+
+/* C = A . W^T on the tensor cores (tcgen05, TMA, fp32 accumulation): the
+ * dense projections of the parallel forward (nn.Linear calls at
+ * modeling_dispatcher.py:70-74, 122-123, 171-173, 185, 197, 351).
+ * A: M x K bf16 (row stride lda), W: N x K bf16 (row stride ldw), K % 64 == 0.
+ * epilogue 0: C = A W^T (bf16, row stride ldc)
+ *          1: C = R + A W^T (R bf16, row stride ldr; R may equal C)
+ *          2: SwiGLU: W holds gate/up rows interleaved in blocks of 128
+ *             (rows [256j, 256j+128) = gate features [128j, 128j+128),
+ *             the next 128 = the matching up features); C (M x N/2) =
+ *             silu(A Wg^T) * (A Wu^T)  (modeling_dispatcher.py:196-197).
+ * status (nullable): set to DH_ERR_TIMEOUT if a bounded pipeline wait gave up. */
+DH_API int dh_gemm_bf16(const void* A, int lda, const void* W, int ldw, void* C, int ldc,
+                        const void* R, int ldr, int M, int N, int K, int epilogue, int* status,
+                        void* stream);
+
+/* Tree mask (modeling_dispatcher.py:282-297, 311-323): mask[b,t,l] = 1 iff
+ * 2^l < T, t >= 2^l and (no doc reset, or t and t-2^l lie in the same
+ * document, doc = count of `eot` tokens strictly before the position).
+ * ids int64 (batch, T); mask uint8 (batch, T, L). */
+DH_API int dh_tree_mask(const int64_t* ids, int batch, int T, int L, int64_t eot, int doc_reset,
+                        uint8_t* mask, void* stream);
+
+/* Mixer gates for the parallel forward, on the tensor cores; replaces the
+ * gate pipeline of fused_gates.py:38-93 / modeling_dispatcher.py:100-114.
+ * a, bsrc: A = W1x.x and B = W1s.x, bf16 rows (batch*T, gh), row strides
+ * lda/ldb (views into one projection output are fine).  wg: bf16
+ * (L*NP, gh), level l rows [l*NP + g*H + h] = gate g (admit, forget,
+ * transmit) of head h, rows 3H..NP-1 zero (NP % 16 == 0, NP <= 64).
+ * bias fp32 (L, NP) in the same order.  mask: uint8 (batch, T, L) from
+ * dh_tree_mask, or NULL for the wrap mask alone.  Levels 0..n_lv-1 go to
+ * gates bf16 (batch, H, L, 3, T): admit*m, forget*m + 1-m, transmit.  When
+ * rg_hist is not NULL the transmit gates of all L levels are also written
+ * to rg_hist bf16 (batch, rg_T, L, H) (decoder cache, decoding.py:164-174). */
+DH_API int dh_mixer_gates(const void* a, int lda, const void* bsrc, int ldb, const void* wg,
+                          const float* bias, const uint8_t* mask, int batch, int T, int H, int L,
+                          int NP, int gh, int n_lv, void* gates, void* rg_hist, int rg_T,
+                          int* status, void* stream);
+
+/* The reference custom op dispatcher::gate_preacts_fwd (fused_gates.py:
+ * 186-214, 307-314): pre_i/pre_f/pre_r bf16 (batch, T, n_lv, H) =
+ * W_x[l] . relu(A + m*roll(B, 2^l))^2 + b_x, no sigmoid.  Weights and bias
+ * packed as for dh_mixer_gates; mask uint8 (batch, T, mask_L) or NULL. */
+DH_API int dh_gate_preacts_fwd(const void* a, int lda, const void* bsrc, int ldb, const void* wg,
+                               const float* bias, const uint8_t* mask, int mask_L, int batch,
+                               int T, int H, int L, int NP, int gh, int n_lv, void* pre_i,
+                               void* pre_f, void* pre_r, int* status, void* stream);
+
+/* Dyadic level sweep (modeling_dispatcher.py:116-120): for l < n_lv,
+ * V(t) <- f_l(t) V(t) + a_l(t) r_l(t-2^l) V(t-2^l).  v0 bf16 (batch*T, hd*H)
+ * with row stride ld_v0 (heads are contiguous 64-channel groups, the
+ * reference's transpose at :70-71); gates from dh_mixer_gates; out bf16
+ * with row stride ld_out.  ring (nullable): decoder V_ring (batch, 2^(L+1)-2,
+ * H*hd) filled with the last 2^(j+1) positions of each level j
+ * (decoding.py:68-76, 154, 179-183).  T <= 4096. */
+DH_API int dh_level_scan(const void* v0, int ld_v0, const void* gates, void* out, int ld_out,
+                         int batch, int T, int H, int hd, int L, int n_lv, void* ring,
+                         void* stream);
+
+/* y = RMSNorm(x) * w over rows of width D, bf16 in/out, fp32 math with the
+ * fp32 machine epsilon (torch.nn.RMSNorm, eps=None). */
+DH_API int dh_rmsnorm_bf16(const void* x, int ldx, const void* w, void* y, int ldy, int M, int D,
+                           void* stream);
+
+/* x[m,:] = E[ids[m],:] (bf16).  Out-of-range ids are clamped and flagged in
+ * *status (nullable). */
+DH_API int dh_embed_bf16(const int64_t* ids, const void* emb, void* x, int M, int D, int V,
+                         int* status, void* stream);
+
+/* In-place RoPE on the q and k thirds of a (M, ld) qkv projection, position
+ * m % T, pairs (2j, 2j+1), fp32 tables (max_len, hd/2)
+ * (modeling_dispatcher.py:144-166). */
+DH_API int dh_rope_qk(void* p, int ld, int M, int T, int d, int hd, const float* rope_cos,
+                      const float* rope_sin, void* stream);
+
+/* dst[b, t, 0:n] = src[b*T + t, 0:n] (bf16): fills decoder caches (B_hist,
+ * k, v) from prefill activations. */
+DH_API int dh_copy_rows(const void* src, int ld_src, void* dst, int ld_dst,
+                        long long batch_stride_dst, int batch, int T, int n, void* stream);
+
+/* Sliding-window causal attention over a (batch*T, ld) qkv projection with
+ * q, k already rotated: keys s with t - window < s <= t (all s <= t when
+ * window <= 0 or window >= T), scale 1/sqrt(hd), hd = 64; out bf16
+ * (batch*T, ldo) (modeling_dispatcher.py:168-185). */
+DH_API int dh_window_attn_prefill(const void* qkv, int ld, void* out, int ldo, int batch, int T,
+                                  int H, int hd, int window, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
