@@ -62,10 +62,27 @@ __device__ __forceinline__ void tile_coords(int tile, int m_blocks, int n_blocks
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
+// Residual chunk of the coalesced store pattern below (lane -> 16 B of row
+// chunk>>2, part chunk&3), issued before the accumulator is read so the
+// global-load latency overlaps the TMEM load and staging.
+__device__ __forceinline__ void load_residual(uint4 (&res)[4], int lane, int row0, int col0,
+                                              const GemmArgs& g) {
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int chunk = it * 32 + lane;
+    const int row = row0 + (chunk >> 2), col = col0 + (chunk & 3) * 8;
+    res[it] = make_uint4(0, 0, 0, 0);
+    if (row < g.M && col + 8 <= g.n_out)
+      res[it] = *reinterpret_cast<const uint4*>(g.R + (size_t)row * g.ldr + col);
+  }
+}
+
 // write this lane's 32 values (its row) to staging, then store the warp's
-// 32 x 32 block with each lane writing 16 B in row-contiguous order
+// 32 x 32 block: 16-byte row-contiguous stores when the output rows are
+// 16-byte aligned, otherwise one coalesced 64-byte row segment per store
 __device__ __forceinline__ void stage_and_store(const float (&v)[32], uint8_t* stg, int lane,
-                                                int row0, int col0, const GemmArgs& g) {
+                                                int row0, int col0, const GemmArgs& g,
+                                                const uint4 (&res)[4]) {
   uint4* dst = reinterpret_cast<uint4*>(stg + lane * kStgRow);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -76,31 +93,44 @@ __device__ __forceinline__ void stage_and_store(const float (&v)[32], uint8_t* s
   }
   __syncwarp();
   const bool vec = (g.ldc % 8 == 0) && (g.epi != EPI_RESIDUAL || g.ldr % 8 == 0);
+  if (vec) {
 #pragma unroll
-  for (int it = 0; it < 4; ++it) {
-    const int chunk = it * 32 + lane;
-    const int r = chunk >> 2, part = chunk & 3;
-    const int row = row0 + r, col = col0 + part * 8;
-    if (row >= g.M || col >= g.n_out) continue;
-    uint4 val = *reinterpret_cast<const uint4*>(stg + r * kStgRow + part * 16);
-    __nv_bfloat16* out = g.C + (size_t)row * g.ldc + col;
-    if (vec && col + 8 <= g.n_out) {
-      if (g.epi == EPI_RESIDUAL) {
-        float a[8], b[8];
-        unpack8(val, a);
-        unpack8(*reinterpret_cast<const uint4*>(g.R + (size_t)row * g.ldr + col), b);
+    for (int it = 0; it < 4; ++it) {
+      const int chunk = it * 32 + lane;
+      const int r = chunk >> 2, part = chunk & 3;
+      const int row = row0 + r, col = col0 + part * 8;
+      if (row >= g.M || col >= g.n_out) continue;
+      uint4 val = *reinterpret_cast<const uint4*>(stg + r * kStgRow + part * 16);
+      __nv_bfloat16* out = g.C + (size_t)row * g.ldc + col;
+      if (col + 8 <= g.n_out) {
+        if (g.epi == EPI_RESIDUAL) {
+          float a[8], b[8];
+          unpack8(val, a);
+          unpack8(res[it], b);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) a[e] += b[e];
-        val = pack8(a);
+          for (int e = 0; e < 8; ++e) a[e] += b[e];
+          val = pack8(a);
+        }
+        *reinterpret_cast<uint4*>(out) = val;
+      } else {
+        const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&val);
+        for (int e = 0; e < 8 && col + e < g.n_out; ++e) {
+          float x = bf2f(hv[e]);
+          if (g.epi == EPI_RESIDUAL) x += bf2f(g.R[(size_t)row * g.ldr + col + e]);
+          out[e] = f2bf(x);
+        }
       }
-      *reinterpret_cast<uint4*>(out) = val;
-    } else {
-      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&val);
-      for (int e = 0; e < 8 && col + e < g.n_out; ++e) {
-        float x = bf2f(h[e]);
-        if (g.epi == EPI_RESIDUAL) x += bf2f(g.R[(size_t)row * g.ldr + col + e]);
-        out[e] = f2bf(x);
-      }
+    }
+  } else {
+    const int col = col0 + lane;
+    const bool col_ok = col < g.n_out;
+    for (int r = 0; r < 32; ++r) {
+      const int row = row0 + r;
+      if (row >= g.M) break;
+      if (!col_ok) continue;
+      float x = bf2f(reinterpret_cast<const __nv_bfloat16*>(stg + r * kStgRow)[lane]);
+      if (g.epi == EPI_RESIDUAL) x += bf2f(g.R[(size_t)row * g.ldr + col]);
+      g.C[(size_t)row * g.ldc + col] = f2bf(x);
     }
   }
   __syncwarp();
@@ -219,6 +249,7 @@ __global__ void __launch_bounds__(192, 1)
       const int row0 = mb * BM + q * 32;
       const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       if (g.epi == EPI_SWIGLU) {
+        const uint4 nores[4] = {};
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           uint32_t gv[32], uv[32];
@@ -228,18 +259,23 @@ __global__ void __launch_bounds__(192, 1)
           float v[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = silu(__uint_as_float(gv[e])) * __uint_as_float(uv[e]);
-          stage_and_store(v, stg, lane, row0, nb * (BN / 2) + c, g);
+          stage_and_store(v, stg, lane, row0, nb * (BN / 2) + c, g, nores);
         }
       } else {
+        const bool resid = g.epi == EPI_RESIDUAL && (g.ldr % 8 == 0);
+        uint4 res[4] = {};
+        if (resid) load_residual(res, lane, row0, nb * BN, g);
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t rv[32];
           tmem_ld32(trow + c, rv);
+          uint4 cur[4] = {res[0], res[1], res[2], res[3]};
+          if (resid && c + 32 < BN) load_residual(res, lane, row0, nb * BN + c + 32, g);
           tmem_ld_wait();
           float v[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(rv[e]);
-          stage_and_store(v, stg, lane, row0, nb * BN + c, g);
+          stage_and_store(v, stg, lane, row0, nb * BN + c, g, cur);
         }
       }
       tc_fence_before();

@@ -84,6 +84,10 @@ constexpr int kTileT = 128;
 constexpr int kSlice = 64;  // gate-hidden columns per step (128 B of bf16)
 constexpr int kSBytes = kTileT * kSlice * 2;  // 16 KB operand tile
 constexpr int kWBytes = 8192;                 // W slot (NP <= 64 rows of 128 B)
+constexpr int kBuilderWarps = 8;              // 2 threads per tile row
+constexpr int kGateThreads = 64 + kBuilderWarps * 32;
+constexpr int kHBufs = 4;                     // hidden tiles in flight (MMA latency)
+constexpr int kBiasMax = 16 * 64;             // L * NP floats
 
 struct GateArgs {
   int B, T, H, L, NP, gh;
@@ -99,9 +103,10 @@ struct GateArgs {
   int* err;
 };
 
-constexpr int kGateSmem = 1024 + 2 * kSBytes + kStagesBW * (kSBytes + kWBytes) + 2 * kSBytes + 256;
+constexpr int kGateSmem =
+    1024 + 2 * kSBytes + kStagesBW * (kSBytes + kWBytes) + kHBufs * kSBytes + kBiasMax * 4 + 256;
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGateThreads, 1)
     gate_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmW, GateArgs g) {
   extern __shared__ uint8_t smem_raw[];
@@ -109,15 +114,16 @@ __global__ void __launch_bounds__(192, 1)
                                              ~uintptr_t(1023));
   uint8_t* sA = smem;                                   // 2 x 16 KB
   uint8_t* sBW = sA + 2 * kSBytes;                      // stages x (16 KB B + 8 KB W)
-  uint8_t* sH = sBW + kStagesBW * (kSBytes + kWBytes);  // 2 x 16 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sH + 2 * kSBytes);
+  uint8_t* sH = sBW + kStagesBW * (kSBytes + kWBytes);  // kHBufs x 16 KB
+  float* sBias = reinterpret_cast<float*>(sH + kHBufs * kSBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sBias + kBiasMax);
   uint64_t* a_full = bars;
   uint64_t* a_empty = bars + 2;
   uint64_t* bw_full = bars + 4;
   uint64_t* bw_empty = bw_full + kStagesBW;
   uint64_t* h_full = bw_empty + kStagesBW;
-  uint64_t* h_empty = h_full + 2;
-  uint64_t* d_full = h_empty + 2;
+  uint64_t* h_empty = h_full + kHBufs;
+  uint64_t* d_full = h_empty + kHBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -128,8 +134,10 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&a_full[i], 1);
-      mbar_init(&a_empty[i], 4);
-      mbar_init(&h_full[i], 4);
+      mbar_init(&a_empty[i], kBuilderWarps);
+    }
+    for (int i = 0; i < kHBufs; ++i) {
+      mbar_init(&h_full[i], kBuilderWarps);
       mbar_init(&h_empty[i], 1);
     }
     for (int s = 0; s < kStagesBW; ++s) {
@@ -148,6 +156,7 @@ __global__ void __launch_bounds__(192, 1)
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmW);
   }
+  for (int i = threadIdx.x; i < g.L * g.NP; i += blockDim.x) sBias[i] = g.bias[i];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -214,45 +223,60 @@ __global__ void __launch_bounds__(192, 1)
             umma_commit(&bw_empty[s]);
             umma_commit(&h_empty[hs]);
             if (++s == kStagesBW) { s = 0; ph ^= 1; }
-            if (++hs == 2) { hs = 0; hph ^= 1; }
+            if (++hs == kHBufs) { hs = 0; hph ^= 1; }
           }
         }
         if (ok) umma_commit(d_full);
       }
     }
-  } else {  // ---------------- builders + epilogue (warps 2..5)
-    const int q = warp & 3;
-    const int r = q * 32 + lane;  // row of the tile == TMEM lane
+  } else {  // ---------------- builders + epilogue (warps 2..9)
+    const int q = warp & 3;               // TMEM lane quadrant of this warp
+    const int half = (warp - 2) >> 2;     // which 32 columns of a slice / which levels
+    const int r = q * 32 + lane;          // tile row == TMEM lane
     const int t = t0 + r;
     const bool row_ok = t < g.T;
+    // per-level mask bits of this row, read once (wrap + doc reset)
+    uint32_t mbits = 0;
+    for (int l = 0; l < g.n_calc; ++l) {
+      bool m = t >= (1 << l);
+      if (g.mask) m = row_ok && g.mask[((size_t)b * g.T + t) * g.mask_L + l] != 0;
+      mbits |= (m ? 1u : 0u) << l;
+    }
     int as = 0, s = 0, hs = 0;
     uint32_t aph = 0, ph = 0, hph = 0, dph = 0;
     bool ok = true;
+    const int coff = half * 4;  // first of this thread's four 16-byte chunks
     for (int grp = 0; grp < ngroups && ok; ++grp) {
       const int l0 = grp * g.group;
       const int l1 = min(l0 + g.group, g.n_calc);
       for (int kc = 0; kc < nk && ok; ++kc) {
         if (!mbar_wait(&a_full[as], aph, g.err)) { ok = false; break; }
         const uint8_t* arow = sA + as * kSBytes + r * 128;
+        float fa[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          unpack8(*reinterpret_cast<const uint4*>(arow + (((coff + j) ^ (r & 7)) << 4)), fa[j]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_empty[as]);
+        if (++as == 2) { as = 0; aph ^= 1; }
         for (int l = l0; l < l1; ++l) {
           if (!mbar_wait(&bw_full[s], ph, g.err) || !mbar_wait(&h_empty[hs], hph ^ 1, g.err)) {
             ok = false;
             break;
           }
-          float m = 1.f;
-          if (g.mask) m = (row_ok && g.mask[((size_t)b * g.T + t) * g.mask_L + l]) ? 1.f : 0.f;
+          // masked rows drop the shifted source (rows with t < 2^l arrive as TMA zeros)
+          const float m = g.mask ? (float)((mbits >> l) & 1u) : 1.f;
           const uint8_t* brow = sBW + s * (kSBytes + kWBytes) + r * 128;
           uint8_t* hrow = sH + hs * kSBytes + r * 128;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int off = ((j ^ (r & 7)) << 4);
-            float fa[8], fb[8], fh[8];
-            unpack8(*reinterpret_cast<const uint4*>(arow + off), fa);
+          for (int j = 0; j < 4; ++j) {
+            const int off = ((coff + j) ^ (r & 7)) << 4;
+            float fb[8], fh[8];
             unpack8(*reinterpret_cast<const uint4*>(brow + off), fb);
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               // reference rounding: A + B in the model dtype, then relu^2 in bf16
-              float x = bf2f(f2bf(fa[e] + m * fb[e]));
+              float x = bf2f(f2bf(fa[j][e] + m * fb[e]));
               x = fmaxf(x, 0.f);
               fh[e] = x * x;
             }
@@ -262,56 +286,45 @@ __global__ void __launch_bounds__(192, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&h_full[hs]);
           if (++s == kStagesBW) { s = 0; ph ^= 1; }
-          if (++hs == 2) { hs = 0; hph ^= 1; }
+          if (++hs == kHBufs) { hs = 0; hph ^= 1; }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_empty[as]);
-        if (++as == 2) { as = 0; aph ^= 1; }
       }
       if (!ok) break;
-      // ---- epilogue of this level group
+      // ---- epilogue of this level group: the two warp halves split the levels
       if (!mbar_wait(d_full, dph, g.err)) break;
       dph ^= 1;
       tc_fence_after();
       const int H = g.H;
-      for (int l = l0; l < l1; ++l) {
-        float pre[64];
+      const int nl = l1 - l0, mid = (nl + 1) / 2;
+      const int la = half ? l0 + mid : l0, lb = half ? l1 : l0 + mid;
+      for (int l = la; l < lb; ++l) {
         const uint32_t base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((l - l0) * g.NP);
-        for (int c = 0; c < g.NP; c += 16) {
+        const float* bias = sBias + l * g.NP;
+        const float m = (float)((mbits >> l) & 1u);
+        for (int c = 0; c < 3 * H; c += 16) {
           uint32_t v[16];
           tmem_ld16(base + c, v);
           tmem_ld_wait();
+          if (!row_ok) continue;
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (c + e < 64) pre[c + e] = __uint_as_float(v[e]);
-        }
-        if (!row_ok) continue;
-        const float* bias = g.bias + (size_t)l * g.NP;
-        float m = (t >= (1 << l)) ? 1.f : 0.f;
-        if (g.mask) m = g.mask[((size_t)b * g.T + t) * g.mask_L + l] ? 1.f : 0.f;
-        if (l < g.n_lv) {
-          if (g.mode == 0) {
-            for (int h = 0; h < H; ++h) {
-              const float a = sigmoidf_(pre[h] + bias[h]) * m;
-              const float f = sigmoidf_(pre[H + h] + bias[H + h]) * m + (1.f - m);
-              const float rr = sigmoidf_(pre[2 * H + h] + bias[2 * H + h]);
-              __nv_bfloat16* gp = g.gates + ((((size_t)b * H + h) * g.L + l) * 3) * g.T + t;
-              gp[0] = f2bf(a);
-              gp[g.T] = f2bf(f);
-              gp[2 * (size_t)g.T] = f2bf(rr);
+          for (int e = 0; e < 16; ++e) {
+            const int col = c + e;
+            if (col >= 3 * H) break;
+            const int gi = col / H, h = col - gi * H;
+            const float pre = __uint_as_float(v[e]) + bias[col];
+            if (l < g.n_lv) {
+              if (g.mode == 0) {
+                const float sg = sigmoidf_(pre);
+                const float val = gi == 0 ? sg * m : (gi == 1 ? sg * m + (1.f - m) : sg);
+                g.gates[((((size_t)b * H + h) * g.L + l) * 3 + gi) * g.T + t] = f2bf(val);
+              } else {
+                __nv_bfloat16* dst = gi == 0 ? g.pre_i : (gi == 1 ? g.pre_f : g.pre_r);
+                dst[(((size_t)b * g.T + t) * g.n_lv + l) * H + h] = f2bf(pre);
+              }
             }
-          } else {
-            const size_t o = (((size_t)b * g.T + t) * g.n_lv + l) * H;
-            for (int h = 0; h < H; ++h) {
-              g.pre_i[o + h] = f2bf(pre[h] + bias[h]);
-              g.pre_f[o + h] = f2bf(pre[H + h] + bias[H + h]);
-              g.pre_r[o + h] = f2bf(pre[2 * H + h] + bias[2 * H + h]);
-            }
+            if (g.rg_hist && gi == 2)
+              g.rg_hist[(((size_t)b * g.rg_T + t) * g.L + l) * H + h] = f2bf(sigmoidf_(pre));
           }
-        }
-        if (g.rg_hist) {
-          __nv_bfloat16* rp = g.rg_hist + (((size_t)b * g.rg_T + t) * g.L + l) * H;
-          for (int h = 0; h < H; ++h) rp[h] = f2bf(sigmoidf_(pre[2 * H + h] + bias[2 * H + h]));
         }
       }
       tc_fence_before();
@@ -326,6 +339,11 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ------------------------------------------------------------------ scan
+// One CTA per (sequence, head, 8-channel slice).  Thread j owns positions
+// j, j+512, j+1024, ... of the slice in fp32 registers; bf16 copies are
+// exchanged through shared memory once per level (consecutive threads touch
+// consecutive 16-byte rows: no bank conflicts).  The gates of level l+1 are
+// already in flight while level l is computed.
 constexpr int kScanThreads = 512;
 constexpr int kScanPer = 8;  // positions per thread (T <= 4096)
 
@@ -339,6 +357,22 @@ struct ScanArgs {
   __nv_bfloat16* ring;  // (B, S, d) or null
   int S;
 };
+
+struct LevelGates {
+  __nv_bfloat16 a[kScanPer], f[kScanPer], r[kScanPer];  // r at the source position t - 2^l
+};
+
+__device__ __forceinline__ void load_level(const __nv_bfloat16* __restrict__ ga, int T, int tid,
+                                           int s, LevelGates& G) {
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int t = tid + i * kScanThreads;
+    const bool in = t < T, src = in && t >= s;
+    G.a[i] = in ? ga[t] : __float2bfloat16_rn(0.f);
+    G.f[i] = in ? ga[T + t] : __float2bfloat16_rn(1.f);
+    G.r[i] = src ? ga[2 * (size_t)T + t - s] : __float2bfloat16_rn(0.f);
+  }
+}
 
 __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
   extern __shared__ uint4 sx[];  // [T] x 8 bf16
@@ -369,23 +403,26 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
   };
   if (a.ring) write_ring(0);
   const __nv_bfloat16* gbase = a.gates + (((size_t)b * a.H + h) * a.L) * 3 * (size_t)T;
-  for (int l = 0; l < a.n_lv; ++l) {
+  int nl = a.n_lv;
+  while (nl > 0 && (1 << (nl - 1)) > T) --nl;   // the reference stops at shift > T
+  LevelGates cur, nxt;
+  if (nl > 0) load_level(gbase, T, tid, 1, cur);
+  for (int l = 0; l < nl; ++l) {
     const int s = 1 << l;
-    if (s > T) break;
+    if (l + 1 < nl) load_level(gbase + (size_t)(l + 1) * 3 * T, T, tid, 2 * s, nxt);
 #pragma unroll
     for (int i = 0; i < kScanPer; ++i) {
       const int t = tid + i * kScanThreads;
       if (t < T) sx[t] = pack8(V[i]);
     }
     __syncthreads();
-    const __nv_bfloat16* ga = gbase + (size_t)l * 3 * T;
 #pragma unroll
     for (int i = 0; i < kScanPer; ++i) {
       const int t = tid + i * kScanThreads;
       if (t >= T) continue;
-      const float f = bf2f(ga[T + t]);
+      const float f = bf2f(cur.f[i]);
       if (t >= s) {
-        const float coef = bf2f(ga[t]) * bf2f(ga[2 * T + t - s]);
+        const float coef = bf2f(cur.a[i]) * bf2f(cur.r[i]);
         float vs[8];
         unpack8(sx[t - s], vs);
 #pragma unroll
@@ -397,6 +434,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
     }
     if (a.ring && l + 1 < a.L) write_ring(l + 1);
     __syncthreads();
+    cur = nxt;
   }
   if (a.ring)
     for (int j = a.n_lv + 1; j < a.L; ++j) write_ring(j);
@@ -434,7 +472,8 @@ static int launch_gates(const void* a, int lda, const void* bsrc, int ldb, const
   DH_REQUIRE(a && bsrc && wg && g.bias, DH_ERR_ARG, "mixer gates: null pointer");
   DH_REQUIRE(g.gh % kSlice == 0 && g.NP % 16 == 0 && g.NP <= 64 && 3 * g.H <= g.NP,
              DH_ERR_SHAPE, "mixer gates: gh=%d NP=%d H=%d unsupported", g.gh, g.NP, g.H);
-  DH_REQUIRE(g.n_calc >= 1 && g.n_calc <= g.L && g.n_lv <= g.n_calc && g.L <= 30, DH_ERR_SHAPE,
+  DH_REQUIRE(g.n_calc >= 1 && g.n_calc <= g.L && g.n_lv <= g.n_calc && g.L * g.NP <= kBiasMax,
+             DH_ERR_SHAPE,
              "mixer gates: level counts n_lv=%d n_calc=%d L=%d", g.n_lv, g.n_calc, g.L);
   DH_REQUIRE(lda % 8 == 0 && ldb % 8 == 0, DH_ERR_SHAPE, "mixer gates: row strides must be multiples of 8");
   g.group = 512 / g.NP;
@@ -465,7 +504,7 @@ static int launch_gates(const void* a, int lda, const void* bsrc, int ldb, const
     configured_dev = dev;
   }
   dim3 grid((g.T + kTileT - 1) / kTileT, g.B);
-  gate_kernel<<<grid, 192, kGateSmem, st>>>(ta, tb, tw, g);
+  gate_kernel<<<grid, kGateThreads, kGateSmem, st>>>(ta, tb, tw, g);
   return check_launch("gate_kernel");
 }
 

@@ -86,20 +86,26 @@ class PrefillEngine:
                 mask=torch.empty(B, T, L, device=dev, dtype=torch.uint8))
         return self._bufs[key]
 
-    def _gemm(self, name, a, w, out, epi=0, residual=None, s=None):
+    def _timed(self, name, flops, fn, *args):
+        """Run one C-ABI call; with `record_events` set (a list), bracket it
+        with CUDA events on the current stream for per-op timing."""
         ev = self.record_events
-        if ev is not None:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
+        if ev is None:
+            return _lib.call(fn, *args)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        _lib.call(fn, *args)
+        e1.record()
+        ev.append((name, flops, e0, e1))
+
+    def _gemm(self, name, a, w, out, epi=0, residual=None, s=None):
         M, K = a.shape
         N = w.shape[0]
-        _lib.call("dh_gemm_bf16", _p(a), a.stride(0), _p(w), w.stride(0), _p(out), out.stride(0),
-                  _p(residual), residual.stride(0) if residual is not None else 0, M, N, K, epi,
-                  _p(self.status), s)
-        if ev is not None:
-            e1.record()
-            ev.append((name, 2.0 * M * N * K, e0, e1))
+        self._timed(name, 2.0 * M * N * K, "dh_gemm_bf16", _p(a), a.stride(0), _p(w), w.stride(0),
+                    _p(out), out.stride(0), _p(residual),
+                    residual.stride(0) if residual is not None else 0, M, N, K, epi,
+                    _p(self.status), s)
 
     @torch.no_grad()
     def forward(self, ids, caches=None, logits_out=None):
@@ -125,19 +131,23 @@ class PrefillEngine:
             call("dh_tree_mask", _p(ids), B, T, L, int(cfg.eot_token), 1, _p(mask), s)
         for i, lay in enumerate(W.layers):
             cache = caches[i] if caches is not None else None
-            call("dh_rmsnorm_bf16", _p(x), d, _p(lay["norm1"]), _p(h), d, M, d, s)
+            self._timed("rmsnorm", 0.0, "dh_rmsnorm_bf16", _p(x), d, _p(lay["norm1"]), _p(h), d,
+                        M, d, s)
             if lay["kind"] == "tree":
                 self._gemm("proj3", h, lay["w3"], P, s=s)
                 A, Bs = P[:, d:2 * d], P[:, 2 * d:]
                 if cache is not None:
                     mlen = cache.B_hist.shape[1]
                     call("dh_copy_rows", _p(Bs), 3 * d, _p(cache.B_hist), d, mlen * d, B, T, d, s)
-                call("dh_mixer_gates", _p(A), 3 * d, _p(Bs), 3 * d, _p(lay["wg"]),
-                     _p(lay["bias_np"]), _p(mask) if use_mask else None, B, T, H, L, self.NP, d,
-                     n_lv, _p(gates), _p(cache.rg_hist) if cache is not None else None,
-                     cache.rg_hist.shape[1] if cache is not None else 0, _p(self.status), s)
-                call("dh_level_scan", _p(P), 3 * d, _p(gates), _p(Vb), d, B, T, H, hd, L, n_lv,
-                     _p(cache.V_ring) if cache is not None else None, s)
+                self._timed("gates", 2.0 * M * (L if cache is not None else n_lv) * 3 * H * d,
+                            "dh_mixer_gates", _p(A), 3 * d, _p(Bs), 3 * d, _p(lay["wg"]),
+                            _p(lay["bias_np"]), _p(mask) if use_mask else None, B, T, H, L,
+                            self.NP, d, n_lv, _p(gates),
+                            _p(cache.rg_hist) if cache is not None else None,
+                            cache.rg_hist.shape[1] if cache is not None else 0,
+                            _p(self.status), s)
+                self._timed("scan", 0.0, "dh_level_scan", _p(P), 3 * d, _p(gates), _p(Vb), d, B,
+                            T, H, hd, L, n_lv, _p(cache.V_ring) if cache is not None else None, s)
             else:
                 self._gemm("qkv", h, lay["wqkv"], P, s=s)
                 call("dh_rope_qk", _p(P), 3 * d, M, T, d, hd, _p(self.rope_cos),
@@ -146,8 +156,8 @@ class PrefillEngine:
                     mlen = cache.k.shape[1]
                     call("dh_copy_rows", _p(P[:, d:2 * d]), 3 * d, _p(cache.k), d, mlen * d, B, T, d, s)
                     call("dh_copy_rows", _p(P[:, 2 * d:]), 3 * d, _p(cache.v), d, mlen * d, B, T, d, s)
-                call("dh_window_attn_prefill", _p(P), 3 * d, _p(Vb), d, B, T, H, hd,
-                     cfg.attn_window, s)
+                self._timed("attn", 0.0, "dh_window_attn_prefill", _p(P), 3 * d, _p(Vb), d, B, T,
+                            H, hd, cfg.attn_window, s)
             self._gemm("out", Vb, lay["w_out"], x, epi=1, residual=x, s=s)
             call("dh_rmsnorm_bf16", _p(x), d, _p(lay["norm2"]), _p(h), d, M, d, s)
             self._gemm("gate_up", h, lay["w_gu"], U, epi=2, s=s)
