@@ -1,26 +1,23 @@
 """Benchmark of the Dispatcher-Hybrid B200 hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload prefill|decode]
 
-Workloads (default 292M config, random-init bf16 weights from seed 0,
-synthetic uniform token ids):
-  prefill  parallel forward of 8 x 4096 tokens per GPU -> logits (configs[1];
-           8 rows per GPU, so N=8 is the 64-sequence sharded prefill)
-  decode   16 lockstep rows per GPU at context 3900 (one shared prompt, seed
-           2), greedy; plus a batch-1 decode line at context 3900 reported in
-           the same JSON under "decode_b1"
+Primary line: parallel-forward prefill of the
+default 292M model (random-init bf16 weights, seed 0) over 8 x 4096 synthetic
+token ids per GPU (uniform over the vocabulary, EOT kept so the doc-reset
+mask is live) -> logits.  N GPUs each prefill their own 8 sequences (weak
+scaling; at N=8 this is the 64-sequence sharded prefill of configs[4]).
+`value` is whole-job tok/s (max over ranks of the device time).  Decode
+results at context 3900 (16 lockstep rows per GPU, and batch 1) are added
+under "decode" in the same JSON line.
 
-One JSON line on rank 0.  `value` is the whole-job aggregate tok/s (max of
-per-rank device times); `e2e` is the same metric through the public API with
-host buffers; `roofline` covers the dominant kernel; `cpu_baseline` is the
-reference algorithm (the CPU oracle, a restatement of the reference's eager
-path) timed on this host's cores on a bounded sample.
+`--impl reference` times the reference algorithm on the host CPU (the
+oracle: an eager restatement of the reference's own PyTorch code) on a
+bounded sample of the same workload.
 """
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -36,15 +33,50 @@ import torch  # noqa: E402
 
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+PREFILL_B, PREFILL_T = 8, 4096
+DECODE_CTX = 3900
+METRIC = "prefill tok/s at T=4096 (8 x 4096 per GPU)"
 
 
 def peaks():
     try:
         with open(PEAKS_FILE) as f:
-            p = json.load(f)
-        return p, "measured"
+            return json.load(f), "measured"
     except Exception:
         return FALLBACK_PEAKS, "fallback"
+
+
+def prefill_flops_per_token(cfg):
+    """Algorithmic FLOPs per prefill token: every dense projection (2 per
+    MAC, tied lm_head included), the gate readouts of every level, and the
+    window attention (average keys per query over T=4096 with window 1024)."""
+    d, H, L, ff, V = cfg.d_model, cfg.num_heads, cfg.levels, cfg.dim_feedforward, cfg.vocab_size
+    n_attn = len(cfg.attn_slots())
+    n_tree = cfg.num_layers - n_attn
+    dense = n_tree * (4 * d * d + 3 * ff * d) + n_attn * (4 * d * d + 3 * ff * d) + V * d
+    gates = n_tree * L * 3 * H * d
+    T, W = PREFILL_T, cfg.attn_window
+    avg_keys = sum(min(t + 1, W) for t in range(T)) / T
+    attn = n_attn * 4 * d * avg_keys
+    return 2 * dense + 2 * gates + attn
+
+
+def decode_bytes_per_step(cfg, batch, ctx):
+    """Algorithmic HBM bytes of one decode step: every weight once (tied
+    lm_head read in full, the embedding one row per token) plus the per-row
+    state the step must read/write (ring slots and histories of every level,
+    the attention window of K and V)."""
+    d, H, L, ff, V = cfg.d_model, cfg.num_heads, cfg.levels, cfg.dim_feedforward, cfg.vocab_size
+    n_attn = len(cfg.attn_slots())
+    n_tree = cfg.num_layers - n_attn
+    w_tree = (4 * d * d + 3 * L * H * d + 3 * ff * d) * 2 + 3 * L * H * 4
+    w_attn = (4 * d * d + 3 * ff * d) * 2
+    weights = n_tree * w_tree + n_attn * w_attn + V * d * 2 + (2 * cfg.num_layers + 1) * d * 2
+    tree_row = (d * 2) * (1 + L) + (d * 2) * (2 * L) + L * H * 2 * 2
+    win = min(ctx + 1, cfg.attn_window if cfg.attn_window > 0 else ctx + 1)
+    attn_row = 2 * win * d * 2 + 2 * d * 2
+    state = batch * (n_tree * tree_row + n_attn * attn_row + d * 2)
+    return weights + state
 
 
 # ----------------------------------------------------------------- clocks
@@ -56,9 +88,7 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index):
-        self.dev = device_index
-        self.proc = None
-        self.lines = []
+        self.dev, self.proc, self.lines = device_index, None, []
 
     def start(self):
         try:
@@ -66,8 +96,7 @@ class ClockSampler:
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100", "-i", str(self.dev)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
+            threading.Thread(target=self._read, daemon=True).start()
         except Exception:
             self.proc = None
 
@@ -86,7 +115,7 @@ class ClockSampler:
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
+            parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
             try:
@@ -129,170 +158,239 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
-# ----------------------------------------------------------------- data
-def prompt_ids(n_rows, T, seed, vocab=50257, eot=50256, share=False):
-    """Uniform ids; EOT re-drawn from [0, eot) so decode prompts stay one document."""
+def prompt_ids(n_rows, T, seed, vocab=50257, eot=50256, keep_eot=False):
+    """Uniform ids; unless keep_eot, EOT is re-drawn from [0, eot) so decode
+    prompts stay a single document (the decoders reject separators)."""
     g = torch.Generator().manual_seed(seed)
-    rows = 1 if share else n_rows
-    ids = torch.randint(0, vocab, (rows, T), generator=g)
-    bad = ids == eot
-    while bad.any():
-        ids[bad] = torch.randint(0, eot, (int(bad.sum()),), generator=g)
+    ids = torch.randint(0, vocab, (n_rows, T), generator=g)
+    if not keep_eot:
         bad = ids == eot
-    return ids.expand(n_rows, T).contiguous() if share else ids
-
-
-def decode_bytes_per_step(cfg, batch, ctx):
-    """Algorithmic HBM bytes of one decode step: every weight once (tied
-    lm_head read in full, embedding one row per token) + per-row state."""
-    d, H, L, ff, V = cfg.d_model, cfg.num_heads, cfg.levels, cfg.dim_feedforward, cfg.vocab_size
-    n_attn = len(cfg.attn_slots())
-    n_tree = cfg.num_layers - n_attn
-    w_tree = (4 * d * d + 3 * L * H * d + 3 * ff * d) * 2 + 3 * L * H * 4
-    w_attn = (4 * d * d + 3 * ff * d) * 2
-    weights = n_tree * w_tree + n_attn * w_attn + V * d * 2 + (2 * cfg.num_layers + 1) * d * 2
-    # per row: tree: B_hist write + 12 reads, ring 12 reads + 12 writes, rg r/w
-    tree_row = (d * 2) * (1 + L) + (d * 2) * (2 * L) + L * H * 2 * 2
-    win = min(ctx + 1, cfg.attn_window if cfg.attn_window > 0 else ctx + 1)
-    attn_row = 2 * win * d * 2 + 2 * d * 2
-    state = batch * (n_tree * tree_row + n_attn * attn_row + d * 2)
-    return weights + state, weights, state
+        while bad.any():
+            ids[bad] = torch.randint(0, eot, (int(bad.sum()),), generator=g)
+            bad = ids == eot
+    return ids
 
 
 # ----------------------------------------------------------------- b200 arm
-def run_decode(model, cfg, batch, ctx, steps, warmup, seed, world):
-    from dispatcher_b200 import FusedGraphedHybridDecoder
-    ids = prompt_ids(batch, ctx, seed, cfg.vocab_size, cfg.eot_token, share=True).cuda()
-    dec = FusedGraphedHybridDecoder(model)
-    logits = dec.prefill(ids)[:, -1]
-    nxt = logits.argmax(-1)
-    steps = min(steps, cfg.max_len - ctx - warmup)
+def run_prefill(engine, ids, steps, warmup, world, logits_buf):
+    """Device-timed prefill steps; every GEMM launch inside the timed region
+    is also bracketed with CUDA events for the roofline of the dominant kernel."""
     for _ in range(warmup):
-        nxt = dec.step(nxt).argmax(-1)
+        engine.forward(ids, logits_out=logits_buf)
+    torch.cuda.synchronize()
+    barrier(world)
+    engine.record_events = []
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        engine.forward(ids, logits_out=logits_buf)
+    e.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    events, engine.record_events = engine.record_events, None
+    ms = max_over_ranks(s.elapsed_time(e), world) / steps
+    per_op = {}
+    for name, flops, a, b in events:
+        x = per_op.setdefault(name, [0, 0.0, 0.0])
+        x[0] += 1
+        x[1] += a.elapsed_time(b)
+        x[2] += flops
+    return ms, per_op
+
+
+def run_prefill_e2e(model, ids_host, steps, warmup):
+    """Public API (`model(input_ids).logits`) with host buffers: each step
+    copies the ids up from pinned memory and reads the last-position logits
+    (the next-token distribution of every row) back into pinned memory."""
+    ids_pin = ids_host.pin_memory()
+    out_pin = torch.empty(ids_host.shape[0], model.config.vocab_size, dtype=torch.bfloat16).pin_memory()
+    for _ in range(warmup):
+        lg = model(ids_pin.to("cuda", non_blocking=True)).logits
+        out_pin.copy_(lg[:, -1])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        lg = model(ids_pin.to("cuda", non_blocking=True)).logits
+        out_pin.copy_(lg[:, -1])
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t0) / steps
+    return ids_host.numel() / dt, ids_pin.numel() * 8, out_pin.numel() * 2
+
+
+def run_decode(model, cfg, batch, ctx, steps, warmup, seed, world):
+    """Device-timed lockstep greedy decode steps after a `ctx`-token prefill;
+    with N > 1 the sampled tokens of every rank are all-gathered each step."""
+    from dispatcher_b200 import FusedGraphedHybridDecoder
+    ids = prompt_ids(1, ctx, seed, cfg.vocab_size, cfg.eot_token).expand(batch, ctx).contiguous().cuda()
+    dec = FusedGraphedHybridDecoder(model)
+    nxt = dec.prefill(ids)[:, -1].argmax(-1)
+    steps = max(1, min(steps, cfg.max_len - ctx - warmup))
+    gathered = [torch.empty_like(nxt) for _ in range(world)] if world > 1 else None
+
+    def one(tok):
+        out = dec.step(tok).argmax(-1)
+        if gathered is not None:
+            torch.distributed.all_gather(gathered, out)
+        return out
+    for _ in range(warmup):
+        nxt = one(nxt)
     torch.cuda.synchronize()
     barrier(world)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(steps):
-        nxt = dec.step(nxt).argmax(-1)
+        nxt = one(nxt)
     e.record()
     torch.cuda.synchronize()
     barrier(world)
-    ms = max_over_ranks(s.elapsed_time(e), world)
-    return ms / steps, steps, dec
+    ms = max_over_ranks(s.elapsed_time(e), world) / steps
+    if int(dec.status.item()) != 0:
+        raise RuntimeError(f"decode kernel reported status {int(dec.status.item())}")
+    return ms, steps, dec.persistent
 
 
-def run_decode_e2e(model, cfg, batch, ctx, steps, seed):
-    """Public-API decode with host buffers: per step the host token ids go up
-    from pinned memory and the chosen tokens come back."""
-    from dispatcher_b200 import FusedGraphedHybridDecoder
-    ids = prompt_ids(batch, ctx, seed, cfg.vocab_size, cfg.eot_token, share=True)
-    dec = FusedGraphedHybridDecoder(model)
-    logits = dec.prefill(ids.cuda())[:, -1]
-    host_tok = logits.argmax(-1).cpu().pin_memory()
-    steps = min(steps, cfg.max_len - ctx)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        dev_tok = host_tok.to("cuda", non_blocking=True)
-        nxt = dec.step(dev_tok).argmax(-1)
-        host_tok.copy_(nxt, non_blocking=False)
-    torch.cuda.synchronize()
-    dt = time.perf_counter() - t0
-    return batch * steps / dt, host_tok.numel() * 8, host_tok.numel() * 8
-
-
-def cpu_decode_baseline(cfg, ctx=3900, steps=3):
-    """Reference algorithm (oracle restatement of IncrementalDecoder) on the
-    host cores, fp32, batch 1: prefill `ctx` tokens untimed, time `steps`."""
+# ----------------------------------------------------------------- CPU legs
+def cpu_prefill_sample(cfg, T=1024, steps=1):
+    """The reference algorithm (oracle restatement of the reference's eager
+    parallel forward), fp32 on the host cores: one sequence of T tokens."""
     import oracle
     from dispatcher_b200 import make_state_dict
     torch.set_num_threads(os.cpu_count() or 1)
     sd = make_state_dict(cfg, seed=0)
-    dec = oracle.OracleDecoder(sd, cfg)
-    ids = prompt_ids(1, ctx, 1, cfg.vocab_size, cfg.eot_token)
-    dec.prefill(ids)
-    tok = torch.tensor([11])
-    dec.step(tok)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        dec.step(tok)
-    dt = time.perf_counter() - t0
-    return {"value": steps / dt, "unit": "tok/s", "cores": torch.get_num_threads(),
-            "kind": "port",
-            "sample": f"oracle IncrementalDecoder restatement, fp32, batch 1, ctx {ctx}, "
-                      f"{steps} steps after 1 warm step"}
+    ids = prompt_ids(1, T, 0, cfg.vocab_size, cfg.eot_token, keep_eot=True)
+    with torch.no_grad():
+        oracle.forward(sd, cfg, ids[:, :64])
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            oracle.forward(sd, cfg, ids)
+        dt = (time.perf_counter() - t0) / steps
+    return {"value": T / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"oracle (eager restatement of the reference forward), fp32, 1 x {T} tokens "
+                      f"of the same synthetic distribution, {steps} timed pass(es)"}
+
+
+def reference_arm(args, world, rank, cfg):
+    """The reference's own algorithm on the host cores (the oracle restates the
+    reference's eager PyTorch forward op for op): each step is a bounded
+    sample (one 1024-token sequence) of the prefill workload."""
+    if rank == 0:
+        steps = max(1, min(args.steps, 10))
+        import oracle
+        from dispatcher_b200 import make_state_dict
+        torch.set_num_threads(os.cpu_count() or 1)
+        sd = make_state_dict(cfg, seed=0)
+        ids = prompt_ids(1, 1024, 0, cfg.vocab_size, cfg.eot_token, keep_eot=True)
+        with torch.no_grad():
+            for _ in range(max(1, min(args.warmup, 2))):
+                oracle.forward(sd, cfg, ids[:, :256])
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                oracle.forward(sd, cfg, ids)
+            dt = (time.perf_counter() - t0) / steps
+        v = 1024 / dt
+        sample = (f"oracle eager restatement of the reference forward, fp32, 1 x 1024 tokens per "
+                  f"step, {steps} steps")
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "prefill sample on host CPU",
+                                            "model": "dispatcher-hybrid-292m random init"},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode"])
+    ap.add_argument("--decode-steps", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
     world, rank, local = dist_setup()
     from dispatcher_b200 import DispatcherConfig, DispatcherHybridForCausalLM
+    from dispatcher_b200.engine import PrefillEngine
     cfg = DispatcherConfig()
-
     if args.impl == "reference":
-        if rank == 0:
-            base = cpu_decode_baseline(cfg, steps=max(2, min(args.steps, 5)))
-            print(json.dumps({
-                "impl": "reference", "metric": "decode tok/s (batch 16 lockstep, ctx 3900)",
-                "value": base["value"], "unit": "tok/s", "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                "scaling": "weak", "dtype": "f32", "data": "synthetic",
-                "config": {"workload": "decode, batch 1 sample of the 16-row lockstep config"},
-                "cpu_baseline": base,
-                "e2e": {"value": base["value"], "unit": "tok/s",
-                        "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return
+        return reference_arm(args, world, rank, cfg)
 
     pk, pk_kind = peaks()
     model = DispatcherHybridForCausalLM(cfg, seed=0).to("cuda", torch.bfloat16).eval()
+    model.enable_fused_gates()
+    ids_host = prompt_ids(PREFILL_B, PREFILL_T, 1000 * rank, cfg.vocab_size, cfg.eot_token,
+                          keep_eot=True)
+    ids = ids_host.cuda()
+    engine = PrefillEngine(model)
+    logits_buf = torch.empty(PREFILL_B * PREFILL_T, (cfg.vocab_size + 7) // 8 * 8, device="cuda",
+                             dtype=torch.bfloat16)
+    engine.calls = 0
+    engine.forward(ids, logits_out=logits_buf)
+    launches_per_step = engine.calls
+
     clocks = ClockSampler(local)
-    B, ctx = 16, 3900
     clocks.start()
-    ms16, k16, _ = run_decode(model, cfg, B, ctx, args.steps, args.warmup, seed=2, world=world)
-    ms1, k1, _ = run_decode(model, cfg, 1, ctx, args.steps, args.warmup, seed=1, world=world)
+    ms, per_op = run_prefill(engine, ids, args.steps, args.warmup, world, logits_buf)
     clk = clocks.stop()
-    e2e_v, hb, db = run_decode_e2e(model, cfg, B, ctx, min(args.steps, 50), seed=2)
-    e2e_v = max_over_ranks(-e2e_v, world) * -1.0  # slowest rank
-    tot16, _, _ = decode_bytes_per_step(cfg, B, ctx)
-    tot1, _, _ = decode_bytes_per_step(cfg, 1, ctx)
-    hbm = pk["hbm_gbs"]
+    tokens = PREFILL_B * PREFILL_T
+    flop_tok = prefill_flops_per_token(cfg)
+    g_n = sum(v[0] for k, v in per_op.items() if k in ("proj3", "qkv", "out", "gate_up", "down", "lm_head"))
+    g_ms = sum(v[1] for k, v in per_op.items() if k in ("proj3", "qkv", "out", "gate_up", "down", "lm_head"))
+    g_fl = sum(v[2] for k, v in per_op.items() if k in ("proj3", "qkv", "out", "gate_up", "down", "lm_head"))
+    peak_t = pk["bf16_tflops_sustained"]
+    gemm_tf = g_fl / (g_ms * 1e-3) / 1e12
+    e2e_v, h2d, d2h = run_prefill_e2e(model, ids_host, max(2, min(args.steps, 5)), 2)
+    e2e_v = -max_over_ranks(-e2e_v, world) * world
+
+    dec_lines = {}
+    for name, batch, seed in (("b16", 16, 2), ("b1", 1, 1)):
+        dms, dsteps, persistent = run_decode(model, cfg, batch, DECODE_CTX, args.decode_steps,
+                                             args.warmup, seed, world)
+        nbytes = decode_bytes_per_step(cfg, batch, DECODE_CTX)
+        dec_lines[name] = {
+            "value": world * batch * 1000.0 / dms, "unit": "tok/s", "ms_per_step": dms,
+            "steps": dsteps, "batch_per_gpu": batch, "ctx": DECODE_CTX,
+            "kernel": "persistent step kernel" if persistent else "per-op kernels in a CUDA graph",
+            "roofline": {"bound": "hbm", "achieved": nbytes / (dms * 1e-3) / 1e9,
+                         "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": nbytes / (dms * 1e-3) / 1e9 / pk["hbm_gbs"],
+                         "bytes_per_step": nbytes}}
+    dec_lines["b1"]["vs_reference_a6000_fused_525"] = dec_lines["b1"]["value"] / world / 525.1
+
     line = {
-        "metric": "decode tok/s (batch 16 lockstep, ctx 3900)",
-        "value": world * B * 1000.0 / ms16, "unit": "tok/s", "n_gpus": world,
-        "steps": k16, "warmup": args.warmup, "ms_per_step": ms16, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "decode: 16 lockstep rows/GPU, shared 3900-token prompt "
-                               "(seed 2), greedy", "model": "dispatcher-hybrid-292m random init",
-                   "global_batch": B * world, "seq_len": ctx, "parallelism": f"dp{world}",
-                   "l2": "no flush: weights (584 MB) exceed L2 (126 MB)"},
-        "roofline": {"bound": "hbm", "kernel": "whole decode step (CUDA graph)",
-                     "achieved": tot16 / (ms16 * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
-                     "frac": tot16 / (ms16 * 1e-3) / 1e9 / hbm, "traffic": None,
-                     "peak_kind": pk_kind},
-        "decode_b1": {"value": world * 1000.0 / ms1, "unit": "tok/s", "ms_per_step": ms1,
-                      "steps": k1, "roofline_frac": tot1 / (ms1 * 1e-3) / 1e9 / hbm,
-                      "vs_a6000_fused_525": world * 1000.0 / ms1 / 525.1},
+        "metric": METRIC, "value": world * tokens * 1000.0 / ms, "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "configs[1]: parallel-forward prefill, 8 x 4096 tokens per GPU, "
+                               "uniform ids (EOT kept, doc-reset mask live)",
+                   "model": "dispatcher-hybrid-292m random init (seed 0)",
+                   "global_batch": PREFILL_B * world, "seq_len": PREFILL_T,
+                   "parallelism": f"dp{world} (batch rows sharded)",
+                   "l2": "no flush: weights (584 MB) and per-step activations exceed L2 (126 MB)"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05, all prefill projections)",
+                     "achieved": gemm_tf, "peak": peak_t, "unit": "TFLOP/s",
+                     "frac": gemm_tf / peak_t, "traffic": None, "peak_kind": f"{pk_kind} sustained",
+                     "launches_timed": g_n,
+                     "whole_step_tflops": flop_tok * tokens / (ms * 1e-3) / 1e12,
+                     "whole_step_frac": flop_tok * tokens / (ms * 1e-3) / 1e12 / peak_t,
+                     "algorithmic_flops_per_token": flop_tok},
+        "per_op_ms_per_step": {k: round(v[1] / args.steps, 3) for k, v in per_op.items()},
+        "decode": dec_lines,
         "clocks": clk,
-        "e2e": {"value": e2e_v * world, "unit": "tok/s", "h2d_bytes_per_step": hb,
-                "d2h_bytes_per_step": db},
-        "gpu_launches": None,
+        "e2e": {"value": e2e_v, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
     }
-    n_kernels = 1 + 5 * cfg.num_layers + 2
-    line["gpu_launches"] = n_kernels * k16
-    if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_decode_baseline(cfg)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_prefill_sample(cfg)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -79,14 +79,14 @@ __global__ void __launch_bounds__(1024) tree_mask_kernel(const int64_t* ids, int
 }
 
 // ------------------------------------------------------------------ gates
-constexpr int kStagesBW = 4;
+constexpr int kStagesBW = 6;
 constexpr int kTileT = 128;
 constexpr int kSlice = 64;  // gate-hidden columns per step (128 B of bf16)
 constexpr int kSBytes = kTileT * kSlice * 2;  // 16 KB operand tile
 constexpr int kWBytes = 8192;                 // W slot (NP <= 64 rows of 128 B)
 constexpr int kBuilderWarps = 8;              // 2 threads per tile row
 constexpr int kGateThreads = 64 + kBuilderWarps * 32;
-constexpr int kHBufs = 4;                     // hidden tiles in flight (MMA latency)
+constexpr int kHBufs = 2;                     // hidden tiles in flight
 constexpr int kBiasMax = 16 * 64;             // L * NP floats
 
 struct GateArgs {
@@ -244,43 +244,47 @@ __global__ void __launch_bounds__(kGateThreads, 1)
     }
     int as = 0, s = 0, hs = 0;
     uint32_t aph = 0, ph = 0, hph = 0, dph = 0;
+    // A failed (bounded) wait clears `ok`; the thread then skips every
+    // further wait but still walks the same loops, so each named barrier
+    // below is reached by all builder threads and nothing can hang.
     bool ok = true;
     const int coff = half * 4;  // first of this thread's four 16-byte chunks
-    for (int grp = 0; grp < ngroups && ok; ++grp) {
+    for (int grp = 0; grp < ngroups; ++grp) {
       const int l0 = grp * g.group;
       const int l1 = min(l0 + g.group, g.n_calc);
-      for (int kc = 0; kc < nk && ok; ++kc) {
-        if (!mbar_wait(&a_full[as], aph, g.err)) { ok = false; break; }
+      for (int kc = 0; kc < nk; ++kc) {
+        ok = ok && mbar_wait(&a_full[as], aph, g.err);
         const uint8_t* arow = sA + as * kSBytes + r * 128;
-        float fa[4][8];
+        uint4 av[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          unpack8(*reinterpret_cast<const uint4*>(arow + (((coff + j) ^ (r & 7)) << 4)), fa[j]);
+          av[j] = *reinterpret_cast<const uint4*>(arow + (((coff + j) ^ (r & 7)) << 4));
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_empty[as]);
         if (++as == 2) { as = 0; aph ^= 1; }
         for (int l = l0; l < l1; ++l) {
-          if (!mbar_wait(&bw_full[s], ph, g.err) || !mbar_wait(&h_empty[hs], hph ^ 1, g.err)) {
-            ok = false;
-            break;
-          }
+          ok = ok && mbar_wait(&bw_full[s], ph, g.err);
+          ok = ok && mbar_wait(&h_empty[hs], hph ^ 1, g.err);
           // masked rows drop the shifted source (rows with t < 2^l arrive as TMA zeros)
-          const float m = g.mask ? (float)((mbits >> l) & 1u) : 1.f;
+          const float mf = g.mask ? (float)((mbits >> l) & 1u) : 1.f;
+          const __nv_bfloat162 m2 = __floats2bfloat162_rn(mf, mf);
+          const __nv_bfloat162 z2 = __floats2bfloat162_rn(0.f, 0.f);
           const uint8_t* brow = sBW + s * (kSBytes + kWBytes) + r * 128;
           uint8_t* hrow = sH + hs * kSBytes + r * 128;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int off = ((coff + j) ^ (r & 7)) << 4;
-            float fb[8], fh[8];
-            unpack8(*reinterpret_cast<const uint4*>(brow + off), fb);
+            uint4 bv = *reinterpret_cast<const uint4*>(brow + off);
+            const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&av[j]);
+            __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&bv);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              // reference rounding: A + B in the model dtype, then relu^2 in bf16
-              float x = bf2f(f2bf(fa[j][e] + m * fb[e]));
-              x = fmaxf(x, 0.f);
-              fh[e] = x * x;
+            for (int e = 0; e < 4; ++e) {
+              // bf16 arithmetic as in the reference: (A + m*B) rounded once, relu, squared
+              __nv_bfloat162 x = __hfma2(m2, b2[e], a2[e]);
+              x = __hmax2(x, z2);
+              b2[e] = __hmul2(x, x);
             }
-            *reinterpret_cast<uint4*>(hrow + off) = pack8(fh);
+            *reinterpret_cast<uint4*>(hrow + off) = bv;
           }
           fence_proxy_async();
           __syncwarp();
@@ -289,14 +293,18 @@ __global__ void __launch_bounds__(kGateThreads, 1)
           if (++hs == kHBufs) { hs = 0; hph ^= 1; }
         }
       }
-      if (!ok) break;
-      // ---- epilogue of this level group: the two warp halves split the levels
-      if (!mbar_wait(d_full, dph, g.err)) break;
+      // ---- epilogue of this level group: the two warp halves split the levels.
+      // All MMAs of the group are complete, so the hidden buffers are idle:
+      // half k stages each level's (3H x 128) gate tile in hidden buffer k,
+      // column-major, and the half then writes it as 16-byte runs along T.
+      ok = ok && mbar_wait(d_full, dph, g.err);
       dph ^= 1;
       tc_fence_after();
       const int H = g.H;
       const int nl = l1 - l0, mid = (nl + 1) / 2;
       const int la = half ? l0 + mid : l0, lb = half ? l1 : l0 + mid;
+      __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(sH + half * kSBytes);
+      const bool vec_out = (g.T % 8) == 0;
       for (int l = la; l < lb; ++l) {
         const uint32_t base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((l - l0) * g.NP);
         const float* bias = sBias + l * g.NP;
@@ -305,28 +313,58 @@ __global__ void __launch_bounds__(kGateThreads, 1)
           uint32_t v[16];
           tmem_ld16(base + c, v);
           tmem_ld_wait();
-          if (!row_ok) continue;
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const int col = c + e;
             if (col >= 3 * H) break;
-            const int gi = col / H, h = col - gi * H;
+            const int gi = col / H;
             const float pre = __uint_as_float(v[e]) + bias[col];
-            if (l < g.n_lv) {
-              if (g.mode == 0) {
-                const float sg = sigmoidf_(pre);
-                const float val = gi == 0 ? sg * m : (gi == 1 ? sg * m + (1.f - m) : sg);
-                g.gates[((((size_t)b * H + h) * g.L + l) * 3 + gi) * g.T + t] = f2bf(val);
-              } else {
-                __nv_bfloat16* dst = gi == 0 ? g.pre_i : (gi == 1 ? g.pre_f : g.pre_r);
-                dst[(((size_t)b * g.T + t) * g.n_lv + l) * H + h] = f2bf(pre);
-              }
+            float val;
+            if (g.mode == 0) {
+              const float sg = sigmoidf_(pre);
+              val = gi == 0 ? sg * m : (gi == 1 ? sg * m + (1.f - m) : sg);
+            } else {
+              val = pre;
             }
-            if (g.rg_hist && gi == 2)
-              g.rg_hist[(((size_t)b * g.rg_T + t) * g.L + l) * H + h] = f2bf(sigmoidf_(pre));
+            stg[col * kTileT + r] = f2bf(val);
+            if (g.rg_hist && gi == 2 && row_ok)
+              g.rg_hist[(((size_t)b * g.rg_T + t) * g.L + l) * H + (col - 2 * H)] =
+                  f2bf(g.mode == 0 ? val : sigmoidf_(pre));
           }
         }
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
+        if (l < g.n_lv) {
+          const int tid_h = q * 32 + lane;  // 0..127 within this half
+          if (g.mode == 0) {
+            // gates (B, H, L, 3, T): tile column col = gi*H + h -> row ((b*H+h)*L+l)*3+gi
+            const int chunks = 3 * H * (kTileT / 8);
+            for (int ck = tid_h; ck < chunks; ck += 128) {
+              const int col = ck / (kTileT / 8), part = ck % (kTileT / 8);
+              const int gi = col / H, h = col - gi * H;
+              const int tt = t0 + part * 8;
+              if (tt >= g.T) continue;
+              __nv_bfloat16* dst = g.gates + ((((size_t)b * H + h) * g.L + l) * 3 + gi) * g.T + tt;
+              const __nv_bfloat16* srcp = stg + col * kTileT + part * 8;
+              if (vec_out && tt + 8 <= g.T) {
+                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(srcp);
+              } else {
+                for (int e = 0; e < 8 && tt + e < g.T; ++e) dst[e] = srcp[e];
+              }
+            }
+          } else if (row_ok) {
+            const size_t o = (((size_t)b * g.T + t) * g.n_lv + l) * H;
+            for (int h = 0; h < H; ++h) {
+              g.pre_i[o + h] = stg[h * kTileT + r];
+              g.pre_f[o + h] = stg[(H + h) * kTileT + r];
+              g.pre_r[o + h] = stg[(2 * H + h) * kTileT + r];
+            }
+          }
+        }
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
       }
+      // both halves must be done with their staging buffers (the hidden
+      // buffers) before either starts building the next group into them
+      asm volatile("bar.sync 3, %0;" ::"n"(kBuilderWarps * 32) : "memory");
       tc_fence_before();
     }
   }
@@ -340,10 +378,13 @@ __global__ void __launch_bounds__(kGateThreads, 1)
 
 // ------------------------------------------------------------------ scan
 // One CTA per (sequence, head, 8-channel slice).  Thread j owns positions
-// j, j+512, j+1024, ... of the slice in fp32 registers; bf16 copies are
-// exchanged through shared memory once per level (consecutive threads touch
-// consecutive 16-byte rows: no bank conflicts).  The gates of level l+1 are
-// already in flight while level l is computed.
+// j, j+512, j+1024, ... of the slice.  V is kept as bf16 in registers and
+// rounded once per level (the reference's bf16 path rounds V after every
+// level, modeling_dispatcher.py:119-120); the update itself is fp32.  The
+// registers are mirrored to shared memory once per level so that every
+// thread can read V(t - 2^l) (consecutive threads touch consecutive 16-byte
+// rows: no bank conflicts).  Gates are double-buffered in registers: level
+// l+1's loads are in flight while level l is computed.
 constexpr int kScanThreads = 512;
 constexpr int kScanPer = 8;  // positions per thread (T <= 4096)
 
@@ -374,74 +415,92 @@ __device__ __forceinline__ void load_level(const __nv_bfloat16* __restrict__ ga,
   }
 }
 
+struct ScanState {
+  uint4 V[kScanPer];
+};
+
+__device__ __forceinline__ void write_ring(const ScanArgs& a, const ScanState& st, int b, int col,
+                                           int tid, int j) {
+  const int T = a.T, d = a.H * a.hd;
+  const int lo = T - (2 << j);
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int t = tid + i * kScanThreads;
+    if (t < T && t >= lo) {
+      const int slot = ((2 << j) - 2) + (t & ((2 << j) - 1));
+      *reinterpret_cast<uint4*>(a.ring + ((size_t)b * a.S + slot) * d + col) = st.V[i];
+    }
+  }
+}
+
+// one level of the sweep; loads the next level's gates into `nxt` first
+__device__ __forceinline__ void scan_level(const ScanArgs& a, ScanState& st, uint4* sx,
+                                           const __nv_bfloat16* gbase, int b, int col, int tid,
+                                           int l, int nl, const LevelGates& cur,
+                                           LevelGates& nxt) {
+  const int T = a.T, s = 1 << l;
+  if (l + 1 < nl) load_level(gbase + (size_t)(l + 1) * 3 * T, T, tid, 2 * s, nxt);
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int t = tid + i * kScanThreads;
+    if (t < T) sx[t] = st.V[i];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int t = tid + i * kScanThreads;
+    if (t >= T) continue;
+    const float f = bf2f(cur.f[i]);
+    float v[8];
+    unpack8(st.V[i], v);
+    if (t >= s) {
+      const float coef = bf2f(cur.a[i]) * bf2f(cur.r[i]);
+      float vs[8];
+      unpack8(sx[t - s], vs);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = f * v[e] + coef * vs[e];
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = f * v[e];
+    }
+    st.V[i] = pack8(v);
+  }
+  if (a.ring && l + 1 < a.L) write_ring(a, st, b, col, tid, l + 1);
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
   extern __shared__ uint4 sx[];  // [T] x 8 bf16
   const int slices = a.hd / 8;
   const int cc = blockIdx.x % slices;
   const int h = (blockIdx.x / slices) % a.H;
   const int b = blockIdx.x / (slices * a.H);
-  const int d = a.H * a.hd;
   const int col = h * a.hd + cc * 8;
   const int tid = threadIdx.x;
   const int T = a.T;
-  float V[kScanPer][8];
+  ScanState st;
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
     const int t = tid + i * kScanThreads;
-    if (t < T) unpack8(*reinterpret_cast<const uint4*>(a.v0 + ((size_t)b * T + t) * a.ld_v0 + col), V[i]);
+    st.V[i] = t < T ? *reinterpret_cast<const uint4*>(a.v0 + ((size_t)b * T + t) * a.ld_v0 + col)
+                    : make_uint4(0, 0, 0, 0);
   }
-  auto write_ring = [&](int j) {
-    const int lo = T - (2 << j);
-#pragma unroll
-    for (int i = 0; i < kScanPer; ++i) {
-      const int t = tid + i * kScanThreads;
-      if (t < T && t >= lo) {
-        const int slot = ((2 << j) - 2) + (t & ((2 << j) - 1));
-        *reinterpret_cast<uint4*>(a.ring + ((size_t)b * a.S + slot) * d + col) = pack8(V[i]);
-      }
-    }
-  };
-  if (a.ring) write_ring(0);
+  if (a.ring) write_ring(a, st, b, col, tid, 0);
   const __nv_bfloat16* gbase = a.gates + (((size_t)b * a.H + h) * a.L) * 3 * (size_t)T;
   int nl = a.n_lv;
   while (nl > 0 && (1 << (nl - 1)) > T) --nl;   // the reference stops at shift > T
-  LevelGates cur, nxt;
-  if (nl > 0) load_level(gbase, T, tid, 1, cur);
-  for (int l = 0; l < nl; ++l) {
-    const int s = 1 << l;
-    if (l + 1 < nl) load_level(gbase + (size_t)(l + 1) * 3 * T, T, tid, 2 * s, nxt);
-#pragma unroll
-    for (int i = 0; i < kScanPer; ++i) {
-      const int t = tid + i * kScanThreads;
-      if (t < T) sx[t] = pack8(V[i]);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < kScanPer; ++i) {
-      const int t = tid + i * kScanThreads;
-      if (t >= T) continue;
-      const float f = bf2f(cur.f[i]);
-      if (t >= s) {
-        const float coef = bf2f(cur.a[i]) * bf2f(cur.r[i]);
-        float vs[8];
-        unpack8(sx[t - s], vs);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) V[i][e] = f * V[i][e] + coef * vs[e];
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) V[i][e] = f * V[i][e];
-      }
-    }
-    if (a.ring && l + 1 < a.L) write_ring(l + 1);
-    __syncthreads();
-    cur = nxt;
+  LevelGates g0, g1;
+  if (nl > 0) load_level(gbase, T, tid, 1, g0);
+  for (int l = 0; l < nl; l += 2) {
+    scan_level(a, st, sx, gbase, b, col, tid, l, nl, g0, g1);
+    if (l + 1 < nl) scan_level(a, st, sx, gbase, b, col, tid, l + 1, nl, g1, g0);
   }
   if (a.ring)
-    for (int j = a.n_lv + 1; j < a.L; ++j) write_ring(j);
+    for (int j = a.n_lv + 1; j < a.L; ++j) write_ring(a, st, b, col, tid, j);
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
     const int t = tid + i * kScanThreads;
-    if (t < T) *reinterpret_cast<uint4*>(a.out + ((size_t)b * T + t) * a.ld_out + col) = pack8(V[i]);
+    if (t < T) *reinterpret_cast<uint4*>(a.out + ((size_t)b * T + t) * a.ld_out + col) = st.V[i];
   }
 }
 

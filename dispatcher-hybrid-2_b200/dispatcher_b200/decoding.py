@@ -71,6 +71,16 @@ def check_single_document(cfg, ids):
             f"single document. Remove the separator, or use model.generate().")
 
 
+class _DirectStep:
+    """Stand-in for a captured graph: re-issues the (single-launch) step."""
+
+    def __init__(self, dec):
+        self.dec = dec
+
+    def replay(self):
+        self.dec._record_step(torch.cuda.current_stream().cuda_stream)
+
+
 class FusedGraphedHybridDecoder:
     """Exact per-token decoder on B200 kernels, one CUDA-graph replay per token."""
 
@@ -133,11 +143,24 @@ class FusedGraphedHybridDecoder:
         self.part = torch.zeros(batch, H, self.nsplit, hd + 2, device=dev, dtype=f32)
         self.counters = torch.zeros(H + batch * H, device=dev, dtype=torch.int32)
         self.status = torch.zeros(1, device=dev, dtype=torch.int32)
+        self.barrier = torch.zeros(2, device=dev, dtype=torch.int64)
         self.graph = None
+        # one persistent kernel per step for lockstep batches of up to 16 rows
+        # (dh_decode_step); larger batches run the per-op kernels in 16-row chunks
+        self.persistent = (batch <= 16 and batch * d <= 16384 and d % 8 == 0 and hd == 64
+                           and cfg.levels <= 16)
+        self._step_params = None
+        if self.persistent:
+            from .step_params import build_step_params
+            self._step_params = build_step_params(self)
 
     # ------------------------------------------------------------ one step
     def _record_step(self, stream):
         """Issue every kernel of one decode step on `stream` (captured once)."""
+        if self.persistent:
+            import ctypes
+            _lib.call("dh_decode_step", ctypes.byref(self._step_params), ctypes_void(stream))
+            return
         cfg, W, B = self.cfg, self.w, self.batch
         d, H, L, ff = cfg.d_model, cfg.num_heads, cfg.levels, cfg.dim_feedforward
         hd = d // H
@@ -181,8 +204,16 @@ class FusedGraphedHybridDecoder:
         with torch.cuda.stream(side):
             self._record_step(side.cuda_stream)   # warm-up: binds lazy attributes
         torch.cuda.current_stream().wait_stream(side)
-        with torch.cuda.graph(g):
-            self._record_step(torch.cuda.current_stream().cuda_stream)
+        try:
+            with torch.cuda.graph(g):
+                self._record_step(torch.cuda.current_stream().cuda_stream)
+        except Exception:
+            if not self.persistent:
+                raise
+            # a single cooperative launch per step: replay it directly when the
+            # driver refuses to capture it
+            torch.cuda.synchronize()
+            g = _DirectStep(self)
         self.t_buf.fill_(saved_t)
         self.graph = g
 

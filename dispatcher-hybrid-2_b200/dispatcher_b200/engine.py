@@ -65,6 +65,7 @@ class PrefillEngine:
         self._bufs = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.record_events = None   # optional list collecting (name, start, end) events
+        self.calls = 0              # C-ABI launches issued (each starts one kernel)
 
     def stale(self):
         return self.w.stale()
@@ -90,6 +91,7 @@ class PrefillEngine:
         """Run one C-ABI call; with `record_events` set (a list), bracket it
         with CUDA events on the current stream for per-op timing."""
         ev = self.record_events
+        self.calls += 1
         if ev is None:
             return _lib.call(fn, *args)
         e0 = torch.cuda.Event(enable_timing=True)
@@ -123,7 +125,9 @@ class PrefillEngine:
         buf = self._buffers(B, T)
         x, h, P, Vb, U, gates, mask = (buf[k] for k in ("x", "h", "P", "V", "U", "gates", "mask"))
         s = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
-        call = _lib.call
+        def call(*a):
+            self.calls += 1
+            return _lib.call(*a)
         n_lv = n_levels(L, T)
         call("dh_embed_bf16", _p(ids), _p(W.emb), _p(x), M, d, Vv, _p(self.status), s)
         use_mask = bool(cfg.doc_reset)
@@ -163,7 +167,16 @@ class PrefillEngine:
             self._gemm("gate_up", h, lay["w_gu"], U, epi=2, s=s)
             self._gemm("down", U, lay["w_down"], x, epi=1, residual=x, s=s)
         call("dh_rmsnorm_bf16", _p(x), d, _p(W.norm_out), _p(h), d, M, d, s)
+        # logits rows are padded to a multiple of 8 columns so every row starts
+        # 16-byte aligned (full-width vector stores); the result is a view
+        vp = ((Vv + 7) // 8) * 8
         if logits_out is None:
-            logits_out = torch.empty(M, Vv, device=self.device, dtype=torch.bfloat16)
-        self._gemm("lm_head", h, W.lm_head, logits_out.view(M, Vv), s=s)
-        return logits_out.view(B, T, Vv)
+            logits_out = torch.empty(M, vp, device=self.device, dtype=torch.bfloat16)
+        lo = logits_out.view(M, -1)
+        if lo.shape[1] < Vv:
+            raise ValueError(f"logits_out has {lo.shape[1]} columns, need {Vv}")
+        M_, N_, K_ = M, Vv, h.shape[1]
+        self._timed("lm_head", 2.0 * M_ * N_ * K_, "dh_gemm_bf16", _p(h), h.stride(0),
+                    _p(W.lm_head), W.lm_head.stride(0), _p(lo), lo.stride(0), None, 0, M_, N_,
+                    K_, 0, _p(self.status), s)
+        return lo.view(B, T, lo.shape[1])[..., :Vv]

@@ -196,6 +196,69 @@ DH_API int dh_copy_rows(const void* src, int ld_src, void* dst, int ld_dst,
 DH_API int dh_window_attn_prefill(const void* qkv, int ld, void* out, int ldo, int batch, int T,
                                   int H, int hd, int window, void* stream);
 
+/* ------------------------------------------------- persistent decode step */
+
+/* Per-layer weights and caches of the whole-step decode kernel.  Weights
+ * are bf16 row-major; packed forms (built once by the host):
+ *   w_in3   tree: [W_in; W1x; W1s] (3d x d); attention: [Wq; Wk; Wv]
+ *   w_gates tree: (L*H, 3, gh): rows admit/forget/transmit of (level, head)
+ *   b_gates tree: (L*H, 3) fp32
+ *   w_gu    (ff, 2, d): gate row j followed by up row j
+ *   w_down  (d, ff) */
+typedef struct {
+  int kind; /* 0 tree block, 1 attention block */
+  const void* norm1;
+  const void* norm2;
+  const void* w_in3;
+  const void* w_gates;
+  const float* b_gates;
+  const void* w_out;
+  const void* w_gu;
+  const void* w_down;
+  void* b_hist;  /* tree caches (decoding.py:50-66 layouts) */
+  void* rg_hist;
+  void* v_ring;
+  void* k_cache; /* attention caches (decoding.py:79-86) */
+  void* v_cache;
+} dh_layer_params;
+
+typedef struct {
+  int n_layers, batch, d, H, hd, L, ff, vocab, max_len, window, nsplit;
+  const int64_t* tokens;  /* (batch) next tokens */
+  int64_t* t_buf;         /* position, advanced by the kernel */
+  const void* emb;        /* (vocab, d), also the tied lm_head */
+  const void* norm_out;
+  const float* rope_cos;  /* (max_len, hd/2) fp32 */
+  const float* rope_sin;
+  const dh_layer_params* layers; /* device array of n_layers */
+  void* logits;           /* bf16 (batch, vocab) */
+  /* caller-provided scratch (device memory, zero before first use):
+   * x fp32 (batch, d); a, v0, y, q bf16 (batch, d); u bf16 (batch, ff);
+   * ig, fg fp32 (batch, L, H); part fp32 (batch, H, nsplit, hd + 2);
+   * counters int (H + batch*H); barrier uint64 [2]; status int [1] */
+  float* x;
+  void* a;
+  void* v0;
+  void* y;
+  void* q;
+  void* u;
+  float* ig;
+  float* fg;
+  float* part;
+  int* counters;
+  unsigned long long* barrier;
+  int* status;
+} dh_step_params;
+
+/* One whole lockstep decode step (embedding, every block, logits, t += 1)
+ * as ONE persistent cooperative kernel: one CTA per SM, phases separated by
+ * a bounded grid barrier (a timeout sets *status = DH_ERR_TIMEOUT and the
+ * kernel still runs to completion).  Replaces the captured per-token graph
+ * of decoding.py:437-443 with the fused tree step of decoding.py:468-488.
+ * batch <= 16, hd == 64.  `params` is a host pointer; its `layers` array
+ * must already be in device memory. */
+DH_API int dh_decode_step(const dh_step_params* params, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

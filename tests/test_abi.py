@@ -60,3 +60,21 @@ def test_ring_layout_constants():
     for j in range(L):
         slots = {oracle.ring_slot(j, t) for t in range(5000, 5000 + 2 ** (j + 1))}
         assert slots == set(range(offs[j], offs[j] + 2 ** (j + 1)))
+
+
+def test_step_params_layout_matches_header(tmp_path):
+    """ctypes mirrors of dh_layer_params / dh_step_params have the C layout."""
+    import subprocess
+    from dispatcher_b200.step_params import LayerParams, StepParams
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "dispatcher_b200.h"\n'
+        'int main(void){printf("%zu %zu %zu %zu %zu\\n", sizeof(dh_layer_params), '
+        'sizeof(dh_step_params), offsetof(dh_step_params, tokens), '
+        'offsetof(dh_step_params, layers), offsetof(dh_step_params, status));return 0;}\n')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", build.INCLUDE, str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    want = [ctypes.sizeof(LayerParams), ctypes.sizeof(StepParams), StepParams.tokens.offset,
+            StepParams.layers.offset, StepParams.status.offset]
+    assert got == want

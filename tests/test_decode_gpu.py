@@ -214,8 +214,30 @@ def test_engine_prefill_caches_match_stepwise(small_nd):
             names = ("B_hist", "rg_hist", "V_ring") if hasattr(ca, "V_ring") else ("k", "v")
             for n in names:
                 xa, xb = getattr(ca, n).float(), getattr(cb, n).float()
-                assert torch.equal(xa != 0, xb != 0), f"T={T} {n}: written-slot pattern differs"
+                # written slots / positions: any nonzero channel (a single bf16
+                # channel can legitimately round to 0.0 in one of the two routes)
+                wa, wb = xa.abs().flatten(2).sum(-1) != 0, xb.abs().flatten(2).sum(-1) != 0
+                if not torch.equal(wa, wb):
+                    bad = (wa != wb).nonzero()[:6].tolist()
+                    raise AssertionError(f"T={T} {n}: written slots differ at (row, slot) {bad}")
                 scale = xb.abs().max().item() + 1e-6
                 assert max_err(xa, xb) < 0.03 * scale + 1e-3, f"T={T} {n}"
         nxt = torch.randint(0, cfg.vocab_size - 1, (2,), generator=g).cuda()
         assert max_err(a.step(nxt).float(), b.step(nxt).float()) < 0.05
+
+
+def test_batch_above_16_uses_chunked_kernels(small_nd):
+    """Lockstep batches above 16 rows run the per-op kernels in 16-row chunks."""
+    cfg, model, sd32 = small_nd
+    g = torch.Generator().manual_seed(8)
+    ids = torch.randint(0, cfg.vocab_size - 1, (18, 30), generator=g)
+    dec = FusedGraphedHybridDecoder(model)
+    out = dec.prefill(ids.cuda())
+    assert not dec.persistent
+    nxt = torch.randint(0, cfg.vocab_size - 1, (18,), generator=g)
+    got = dec.step(nxt.cuda()).float().cpu()
+    ref = oracle.forward(sd32, cfg, torch.cat([ids, nxt[:, None]], 1))[:, -1]
+    ref16 = oracle.forward(cast_sd(sd32, torch.bfloat16), cfg,
+                           torch.cat([ids, nxt[:, None]], 1))[:, -1].float()
+    assert max_err(got, ref) < bf16_bound(ref, ref16)
+    assert out.shape == (18, 30, cfg.vocab_size)
