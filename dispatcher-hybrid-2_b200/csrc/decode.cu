@@ -176,53 +176,140 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvIn in, Epi ep
   const int u_begin = blockIdx.x * upc;
   const int u_end = min(nunits, u_begin + upc);
 
-  // weights do not depend on the previous kernel: pull this warp's rows
-  // into L2 while the producer of x is still running
-  if (lane == 0) {
-    for (int u = u_begin + warp; u < u_end; u += kGemvWarps) {
-      const __nv_bfloat16 *r0, *r1;
-      const bool has1 = epi.rows(u, r0, r1);
-      prefetch_l2(r0, (uint32_t)K * 2);
-      if (has1) prefetch_l2(r1, (uint32_t)K * 2);
+  // weights do not depend on the previous kernel: pull this warp's first row
+  // pair into registers (and the rest of its rows into L2) while the producer
+  // of x is still running
+  // (only for one or two lockstep rows: from 4 rows on the registers cost
+  // more occupancy than the head start gains)
+  constexpr int kPre = MAXB <= 2 ? 4 : 0;  // 256-column iterations held in registers
+  uint4 wpre[kPre > 0 ? 2 * kPre : 1];
+  if (u_begin + warp < u_end) {
+    const __nv_bfloat16 *r0, *r1;
+    epi.rows(u_begin + warp, r0, r1);
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+      const int k = lane * 8 + i * 256;
+      if (k < K) {
+        wpre[2 * i] = ld_stream16(r0 + k);
+        wpre[2 * i + 1] = ld_stream16(r1 + k);
+      }
+    }
+    if (lane == 0) {
+      for (int u = u_begin + warp + (kPre > 0 ? kGemvWarps : 0); u < u_end; u += kGemvWarps) {
+        epi.rows(u, r0, r1);
+        prefetch_l2(r0, (uint32_t)K * 2);
+        prefetch_l2(r1, (uint32_t)K * 2);
+      }
     }
   }
   pdl_wait();
 
-  if (in.x_f32) {
-    const float* x = static_cast<const float*>(in.x);
-    if (in.norm_w) {
-      for (int b = warp; b < batch; b += kGemvWarps) {
-        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)b * K);
-        float ss = 0.f;
-        for (int i = lane; i < K / 4; i += 32) {
-          const float4 v = xr[i];
-          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  // one or two rows: the whole staging is one round trip per thread;
+  // more rows: fewer registers keep two CTAs per SM
+  if constexpr (MAXB <= 2) {
+    if (in.x_f32) {
+      // normalised input: every thread takes float4s of the rows (one L2 round
+      // trip), squares are reduced per row in shared memory
+      const float* x = static_cast<const float*>(in.x);
+      const int k4 = K / 4, n4 = batch * k4;
+      if (threadIdx.x < MAXB) s_rstd[threadIdx.x] = 0.f;
+      __syncthreads();
+      constexpr int NV = (MAXB * 1024) / (kGemvWarps * 32 * 4) > 0 ? (MAXB * 1024) / (kGemvWarps * 32 * 4) : 1;
+      static_assert(NV <= 16, "row staging held in registers");
+      float4 v[NV];
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int i = threadIdx.x + j * kGemvWarps * 32;
+        float sq = 0.f;
+        if (i < n4) {
+          v[j] = reinterpret_cast<const float4*>(x)[i];
+          sq = v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
         }
-        ss = warp_sum(ss);
-        if (lane == 0) s_rstd[b] = rsqrtf(ss / (float)K + kNormEps);
+        if (in.norm_w) {
+          if ((k4 & 31) == 0) {
+            sq = warp_sum(sq);
+            if (lane == 0 && i < n4) atomicAdd(&s_rstd[i / k4], sq);
+          } else if (i < n4) {
+            atomicAdd(&s_rstd[i / k4], sq);
+          }
+        }
       }
       __syncthreads();
-    }
-    const int k4 = K / 4;
-    for (int i = threadIdx.x; i < batch * k4; i += blockDim.x) {
-      const int b = i / k4, k = (i - b * k4) * 4;
-      float4 v = reinterpret_cast<const float4*>(x + (size_t)b * K)[k / 4];
-      if (in.norm_w) {
-        const float r = s_rstd[b];
-        v.x = v.x * r * bf2f(in.norm_w[k]);
-        v.y = v.y * r * bf2f(in.norm_w[k + 1]);
-        v.z = v.z * r * bf2f(in.norm_w[k + 2]);
-        v.w = v.w * r * bf2f(in.norm_w[k + 3]);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int i = threadIdx.x + j * kGemvWarps * 32;
+        if (i < n4) {
+          const int b = i / k4, k = (i - b * k4) * 4;
+          float4 q = v[j];
+          if (in.norm_w) {
+            const float r = rsqrtf(s_rstd[b] / (float)K + kNormEps);
+            q.x = q.x * r * bf2f(in.norm_w[k]);
+            q.y = q.y * r * bf2f(in.norm_w[k + 1]);
+            q.z = q.z * r * bf2f(in.norm_w[k + 2]);
+            q.w = q.w * r * bf2f(in.norm_w[k + 3]);
+          }
+          uint2 pk;
+          pk.x = pack2(q.x, q.y);
+          pk.y = pack2(q.z, q.w);
+          *reinterpret_cast<uint2*>(xs + (size_t)b * K + k) = pk;
+        }
       }
-      uint2 pk;
-      pk.x = pack2(v.x, v.y);
-      pk.y = pack2(v.z, v.w);
-      *reinterpret_cast<uint2*>(xs + (size_t)b * K + k) = pk;
+    } else {
+      const uint4* x = static_cast<const uint4*>(in.x);
+      const int n = batch * K / 8;
+      for (int i0 = threadIdx.x; i0 < n; i0 += 8 * kGemvWarps * 32) {
+        uint4 t8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = i0 + j * kGemvWarps * 32;
+          if (i < n) t8[j] = x[i];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = i0 + j * kGemvWarps * 32;
+          if (i < n) reinterpret_cast<uint4*>(xs)[i] = t8[j];
+        }
+      }
     }
   } else {
-    const uint4* x = static_cast<const uint4*>(in.x);
-    for (int i = threadIdx.x; i < batch * K / 8; i += blockDim.x)
-      reinterpret_cast<uint4*>(xs)[i] = x[i];
+    if (in.x_f32) {
+      // normalised input, row by row: one warp per row sums the squares, then
+      // all threads scale and convert
+      const float* x = static_cast<const float*>(in.x);
+      if (in.norm_w) {
+        for (int b = warp; b < batch; b += kGemvWarps) {
+          const float4* xr = reinterpret_cast<const float4*>(x + (size_t)b * K);
+          float ss = 0.f;
+          for (int i = lane; i < K / 4; i += 32) {
+            const float4 v = xr[i];
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+          }
+          ss = warp_sum(ss);
+          if (lane == 0) s_rstd[b] = rsqrtf(ss / (float)K + kNormEps);
+        }
+        __syncthreads();
+      }
+      const int k4 = K / 4;
+      for (int i = threadIdx.x; i < batch * k4; i += blockDim.x) {
+        const int b = i / k4, k = (i - b * k4) * 4;
+        float4 v = reinterpret_cast<const float4*>(x + (size_t)b * K)[k / 4];
+        if (in.norm_w) {
+          const float r = s_rstd[b];
+          v.x = v.x * r * bf2f(in.norm_w[k]);
+          v.y = v.y * r * bf2f(in.norm_w[k + 1]);
+          v.z = v.z * r * bf2f(in.norm_w[k + 2]);
+          v.w = v.w * r * bf2f(in.norm_w[k + 3]);
+        }
+        uint2 pk;
+        pk.x = pack2(v.x, v.y);
+        pk.y = pack2(v.z, v.w);
+        *reinterpret_cast<uint2*>(xs + (size_t)b * K + k) = pk;
+      }
+    } else {
+      const uint4* x = static_cast<const uint4*>(in.x);
+      for (int i = threadIdx.x; i < batch * K / 8; i += blockDim.x)
+        reinterpret_cast<uint4*>(xs)[i] = x[i];
+    }
   }
   __syncthreads();
 
@@ -232,11 +319,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvIn in, Epi ep
     float acc[2 * MAXB];
 #pragma unroll
     for (int i = 0; i < 2 * MAXB; ++i) acc[i] = 0.f;
-#pragma unroll 2
-    for (int k = lane * 8; k < K; k += 256) {
+    auto fma_chunk = [&](const uint4& wa, const uint4& wb, int k) {
       float fa[8], fb[8];
-      unpack8(ld_stream16(r0 + k), fa);
-      unpack8(ld_stream16(r1 + k), fb);
+      unpack8(wa, fa);
+      unpack8(wb, fb);
 #pragma unroll
       for (int b = 0; b < MAXB; ++b) {
         if (b < batch) {
@@ -249,7 +335,19 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvIn in, Epi ep
           }
         }
       }
+    };
+    const bool first = u == u_begin + warp;
+#pragma unroll
+    for (int i = 0; i < kPre; ++i) {
+      const int k = lane * 8 + i * 256;
+      if (k < K) {
+        if (first) fma_chunk(wpre[2 * i], wpre[2 * i + 1], k);
+        else fma_chunk(ld_stream16(r0 + k), ld_stream16(r1 + k), k);
+      }
     }
+#pragma unroll(MAXB <= 2 ? 4 : 2)
+    for (int k = lane * 8 + kPre * 256; k < K; k += 256)
+      fma_chunk(ld_stream16(r0 + k), ld_stream16(r1 + k), k);
     const float r = transpose_reduce<2 * MAXB>(acc);
     const float other = __shfl_xor_sync(0xffffffffu, r, MAXB);
     const int b = lane % MAXB, row = (lane / MAXB) & 1;
@@ -280,6 +378,8 @@ template <class Epi>
 int launch_gemv(GemvIn in, const Epi& epi, int nunits, cudaStream_t st) {
   if (in.K % 8 != 0 || in.K > 2816 * 2)
     return set_error(DH_ERR_SHAPE, "gemv: K=%d must be a multiple of 8 and <= 5632", in.K);
+  if (in.x_f32 && in.K > 1024)
+    return set_error(DH_ERR_SHAPE, "gemv: normalised input width %d exceeds 1024", in.K);
   if (in.batch <= 0 || in.batch > kMaxRows)
     return set_error(DH_ERR_SHAPE, "gemv: batch chunk %d outside [1, 16]", in.batch);
   if ((size_t)in.batch * in.K * 2 > (size_t)kMaxRows * 2816 * 2 + 8192)

@@ -84,7 +84,12 @@ class _DirectStep:
 class FusedGraphedHybridDecoder:
     """Exact per-token decoder on B200 kernels, one CUDA-graph replay per token."""
 
-    def __init__(self, model, max_len=None, dtype=None):
+    def __init__(self, model, max_len=None, dtype=None, step_kernel="graph"):
+        """step_kernel: "graph" (per-op kernels captured in one CUDA graph) or
+        "persistent" (one cooperative kernel per step, batch <= 16)."""
+        if step_kernel not in ("graph", "persistent"):
+            raise ValueError(f"step_kernel must be 'graph' or 'persistent', got {step_kernel!r}")
+        self.step_kernel = step_kernel
         if not torch.cuda.is_available():
             raise RuntimeError("FusedGraphedHybridDecoder requires CUDA")
         param_dtype = next(model.parameters()).dtype
@@ -147,8 +152,8 @@ class FusedGraphedHybridDecoder:
         self.graph = None
         # one persistent kernel per step for lockstep batches of up to 16 rows
         # (dh_decode_step); larger batches run the per-op kernels in 16-row chunks
-        self.persistent = (batch <= 16 and batch * d <= 16384 and d % 8 == 0 and hd == 64
-                           and cfg.levels <= 16)
+        self.persistent = (self.step_kernel == "persistent" and batch <= 16 and d <= 1024
+                           and d % 8 == 0 and hd == 64 and cfg.levels <= 16)
         self._step_params = None
         if self.persistent:
             from .step_params import build_step_params

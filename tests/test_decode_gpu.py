@@ -226,6 +226,23 @@ def test_engine_prefill_caches_match_stepwise(small_nd):
         assert max_err(a.step(nxt).float(), b.step(nxt).float()) < 0.05
 
 
+@pytest.mark.parametrize("kernel", ["graph", "persistent"])
+def test_step_kernels_match_oracle(small_nd, kernel):
+    """Both step implementations against the fp32 oracle (prompt 40 + 8 steps)."""
+    cfg, model, sd32 = small_nd
+    g = torch.Generator().manual_seed(17)
+    ids = torch.randint(0, cfg.vocab_size - 1, (2, 48), generator=g)
+    ref32 = oracle.forward(sd32, cfg, ids)[:, 39:47]
+    ref16 = oracle.forward(cast_sd(sd32, torch.bfloat16), cfg, ids)[:, 39:47].float()
+    dec = FusedGraphedHybridDecoder(model, step_kernel=kernel)
+    got = [dec.prefill(ids[:, :40].cuda())[:, -1].float()]
+    got += [dec.step(ids[:, t].cuda()).float() for t in range(40, 47)]
+    got = torch.stack(got, 1).cpu()
+    assert dec.persistent == (kernel == "persistent")
+    assert max_err(got, ref32) < bf16_bound(ref32, ref16)
+    assert int(dec.status.item()) == 0
+
+
 def test_batch_above_16_uses_chunked_kernels(small_nd):
     """Lockstep batches above 16 rows run the per-op kernels in 16-row chunks."""
     cfg, model, sd32 = small_nd
