@@ -7,6 +7,8 @@
 // transpose-reduction so that lane l ends up owning (row, batch) = (l / B, l % B).
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace dh {
@@ -862,5 +864,124 @@ extern "C" int dh_decode_advance(int64_t* t_buf, void* stream) {
   DH_REQUIRE(t_buf, DH_ERR_ARG, "dh_decode_advance: null pointer");
   if (launch_pdl(advance_kernel, dim3(1), dim3(1), 0, STREAM(stream), t_buf))
     return check_launch("advance_kernel");
+  return DH_OK;
+}
+
+// ------------------------------------------- split-window attention, no allocation
+// dh_decode_attn_noalloc runs the same split-window kernel as dh_decode_attn,
+// but its two scratch buffers live in this file's own device storage instead
+// of memory the caller passes in.  It exists for callers that cannot allocate
+// device memory: a host that binds the C ABI from another language runtime
+// and owns no CUDA allocator, or a serving loop that must not call cudaMalloc
+// between steps (it can synchronise the whole device, and it can fail when
+// the pool is nearly full, in the middle of a decode step).
+//
+// Limits: batch * H * nsplit * (hd + 2) <= kNoAllocPartFloats (131072 floats,
+// 512 KiB) and batch * H <= kNoAllocCounters (1024).  Larger requests are
+// rejected with DH_ERR_SHAPE before anything is launched.
+//
+// What must start at zero: the counters.  They are zeroed once, when a device
+// is set up, and every call leaves them zero again (the last CTA of each
+// (row, head) resets its own counter).  The partial results need no initial
+// value: each split writes its slot before the combining CTA reads it.
+//
+// The first call on each device does the setup (symbol lookup, kernel
+// attribute, zeroing of the counters, all on that device while it is
+// current); make that first call before any stream capture.  There is one
+// scratch area per device: calls whose executions overlap in time on the same
+// device (two streams, two host threads) race on it and must be serialised by
+// the caller.
+namespace dh {
+
+constexpr int kNoAllocPartFloats = 131072;
+constexpr int kNoAllocCounters = 1024;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) float g_noalloc_part[kNoAllocPartFloats];
+static __device__ __align__(256) int g_noalloc_counters[kNoAllocCounters];
+
+struct NoAllocScratch {
+  float* part;
+  int* counters;
+};
+
+static NoAllocScratch g_noalloc_dev[kNoAllocMaxDevices];  // zero until set up
+static std::mutex g_noalloc_mu;
+
+static int noalloc_scratch(cudaStream_t st, NoAllocScratch* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(DH_ERR_CUDA, "dh_decode_attn_noalloc: cudaGetDevice: %s",
+                                         cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(DH_ERR_DEVICE, "dh_decode_attn_noalloc: device %d beyond %d", dev,
+                     kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocScratch& s = g_noalloc_dev[dev];
+  if (!s.part) {
+    void* part = nullptr;
+    void* counters = nullptr;
+    e = cudaGetSymbolAddress(&part, g_noalloc_part);
+    if (e != cudaSuccess)
+      return set_error(DH_ERR_CUDA, "dh_decode_attn_noalloc: scratch symbol lookup: %s",
+                       cudaGetErrorString(e));
+    e = cudaGetSymbolAddress(&counters, g_noalloc_counters);
+    if (e != cudaSuccess)
+      return set_error(DH_ERR_CUDA, "dh_decode_attn_noalloc: counter symbol lookup: %s",
+                       cudaGetErrorString(e));
+    e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             12288 * 4);
+    if (e != cudaSuccess)
+      return set_error(DH_ERR_CUDA, "dh_decode_attn_noalloc: kernel attribute: %s",
+                       cudaGetErrorString(e));
+    e = cudaMemsetAsync(counters, 0, sizeof(int) * kNoAllocCounters, st);
+    if (e != cudaSuccess)
+      return set_error(DH_ERR_CUDA, "dh_decode_attn_noalloc: zeroing counters: %s",
+                       cudaGetErrorString(e));
+    s.part = static_cast<float*>(part);
+    s.counters = static_cast<int*>(counters);
+  }
+  *out = s;
+  return DH_OK;
+}
+
+}  // namespace dh
+
+extern "C" int dh_decode_attn_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                      void* y, const int64_t* t_buf, int nsplit, int batch,
+                                      int max_len, int H, int hd, int window, void* stream) {
+  DH_REQUIRE(q && k_cache && v_cache && y && t_buf, DH_ERR_ARG,
+             "dh_decode_attn_noalloc: null pointer");
+  DH_REQUIRE(hd == 64, DH_ERR_SHAPE, "dh_decode_attn_noalloc: head_dim %d unsupported (64 only)",
+             hd);
+  DH_REQUIRE(nsplit >= 1 && nsplit <= 64, DH_ERR_SHAPE, "dh_decode_attn_noalloc: nsplit %d",
+             nsplit);
+  DH_REQUIRE(batch >= 1 && H >= 1 && max_len >= 1, DH_ERR_SHAPE,
+             "dh_decode_attn_noalloc: batch %d, H %d, max_len %d", batch, H, max_len);
+  const long long part_floats = (long long)batch * H * nsplit * (hd + 2);
+  DH_REQUIRE(part_floats <= kNoAllocPartFloats, DH_ERR_SHAPE,
+             "dh_decode_attn_noalloc: batch*H*nsplit*(hd+2) = %lld floats of partial results "
+             "exceeds the built-in scratch of %d floats",
+             part_floats, kNoAllocPartFloats);
+  DH_REQUIRE((long long)batch * H <= kNoAllocCounters, DH_ERR_SHAPE,
+             "dh_decode_attn_noalloc: batch*H = %lld exceeds the built-in %d counters",
+             (long long)batch * H, kNoAllocCounters);
+  const int span = (window > 0 && window < max_len) ? window : max_len;
+  const int cap = (span + nsplit - 1) / nsplit;
+  DH_REQUIRE(cap <= 12288, DH_ERR_SHAPE, "dh_decode_attn_noalloc: window chunk %d too large", cap);
+  NoAllocScratch s;
+  const int rc = noalloc_scratch(STREAM(stream), &s);
+  if (rc) return rc;
+  const size_t smem = (size_t)cap * sizeof(float);
+  const int d = H * hd;
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    AttnParams p{BF(q) + (size_t)b0 * d, BF(k_cache) + (size_t)b0 * max_len * d,
+                 BF(v_cache) + (size_t)b0 * max_len * d, BFM(y) + (size_t)b0 * d, t_buf,
+                 s.part + (size_t)b0 * H * nsplit * (hd + 2), s.counters + (size_t)b0 * H,
+                 max_len, H, window, cap};
+    if (launch_pdl(attn_decode_kernel, dim3(H, nb, nsplit), dim3(128), smem, STREAM(stream), p))
+      return check_launch("attn_decode_kernel");
+  }
   return DH_OK;
 }

@@ -101,6 +101,18 @@ DH_API int dh_decode_attn(const void* q, const void* k_cache, const void* v_cach
                    const int64_t* t_buf, float* part, int* counters, int nsplit, int batch,
                    int max_len, int H, int hd, int window, void* stream);
 
+/* dh_decode_attn without caller scratch.  No counterpart in the reference
+ * (its decoder allocates torch tensors for everything); added for callers that
+ * cannot allocate device memory.  Same arguments and result as dh_decode_attn
+ * minus part/counters, which live in the library's own static device storage:
+ * batch*H*nsplit*(hd+2) <= 131072 floats and batch*H <= 1024, else DH_ERR_SHAPE.
+ * The first call on a device sets that device's scratch up (make it before any
+ * stream capture).  One scratch area per device: calls that overlap in time on
+ * the same device race and must be serialised by the caller. */
+DH_API int dh_decode_attn_noalloc(const void* q, const void* k_cache, const void* v_cache, void* y,
+                           const int64_t* t_buf, int nsplit, int batch, int max_len, int H,
+                           int hd, int window, void* stream);
+
 /* logits = RMSNorm(x; norm_w) . E^T, bf16 (batch, vocab) (decoding.py:442). */
 DH_API int dh_decode_logits(const float* x, const void* norm_w, const void* emb, void* logits,
                      int batch, int d, int vocab, void* stream);
