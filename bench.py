@@ -135,27 +135,24 @@ def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
     if world > 1:
         import datetime
         torch.distributed.init_process_group(
             "nccl" if torch.cuda.is_available() else "gloo",
             timeout=datetime.timedelta(seconds=300))
-    if torch.cuda.is_available():
-        torch.cuda.set_device(local)
     return world, rank, local
 
 
 def barrier(world):
-    if world > 1:
-        torch.distributed.barrier()
+    from dispatcher_b200 import sharding
+    sharding.barrier(torch.cuda.current_device() if torch.cuda.is_available() else None)
 
 
 def max_over_ranks(v, world):
-    if world == 1:
-        return v
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item())
+    from dispatcher_b200 import sharding
+    return sharding.max_over_ranks(v, "cuda" if torch.cuda.is_available() else None)
 
 
 def prompt_ids(n_rows, T, seed, vocab=50257, eot=50256, keep_eot=False):
@@ -173,13 +170,14 @@ def prompt_ids(n_rows, T, seed, vocab=50257, eot=50256, keep_eot=False):
 
 # ----------------------------------------------------------------- b200 arm
 def run_prefill(engine, ids, steps, warmup, world, logits_buf):
-    """Device-timed prefill steps; every GEMM launch inside the timed region
-    is also bracketed with CUDA events for the roofline of the dominant kernel."""
+    """Device-timed prefill steps (no instrumentation inside the timed
+    region), then the same number of steps again with every launch bracketed
+    by CUDA events on the engine's stream, for the per-op split and the
+    roofline of the dominant kernel."""
     for _ in range(warmup):
         engine.forward(ids, logits_out=logits_buf)
     torch.cuda.synchronize()
     barrier(world)
-    engine.record_events = []
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(steps):
@@ -187,8 +185,12 @@ def run_prefill(engine, ids, steps, warmup, world, logits_buf):
     e.record()
     torch.cuda.synchronize()
     barrier(world)
-    events, engine.record_events = engine.record_events, None
     ms = max_over_ranks(s.elapsed_time(e), world) / steps
+    engine.record_events = []
+    for _ in range(steps):
+        engine.forward(ids, logits_out=logits_buf)
+    torch.cuda.synchronize()
+    events, engine.record_events = engine.record_events, None
     per_op = {}
     for name, flops, a, b in events:
         x = per_op.setdefault(name, [0, 0.0, 0.0])
@@ -220,17 +222,15 @@ def run_prefill_e2e(model, ids_host, steps, warmup):
 def run_decode(model, cfg, batch, ctx, steps, warmup, seed, world):
     """Device-timed lockstep greedy decode steps after a `ctx`-token prefill;
     with N > 1 the sampled tokens of every rank are all-gathered each step."""
-    from dispatcher_b200 import FusedGraphedHybridDecoder
+    from dispatcher_b200 import FusedGraphedHybridDecoder, sharding
     ids = prompt_ids(1, ctx, seed, cfg.vocab_size, cfg.eot_token).expand(batch, ctx).contiguous().cuda()
     dec = FusedGraphedHybridDecoder(model)
     nxt = dec.prefill(ids)[:, -1].argmax(-1)
     steps = max(1, min(steps, cfg.max_len - ctx - warmup))
-    gathered = [torch.empty_like(nxt) for _ in range(world)] if world > 1 else None
-
     def one(tok):
         out = dec.step(tok).argmax(-1)
-        if gathered is not None:
-            torch.distributed.all_gather(gathered, out)
+        if world > 1:
+            sharding.gather_rows(out, batch * world)   # every rank sees every row's token
         return out
     for _ in range(warmup):
         nxt = one(nxt)
@@ -247,6 +247,15 @@ def run_decode(model, cfg, batch, ctx, steps, warmup, seed, world):
     if int(dec.status.item()) != 0:
         raise RuntimeError(f"decode kernel reported status {int(dec.status.item())}")
     return ms, steps, dec.persistent
+
+
+def prefill_config(world):
+    return {"workload": "configs[1]: parallel-forward prefill, 8 x 4096 tokens per GPU, "
+                        "uniform ids (EOT kept, doc-reset mask live)",
+            "model": "dispatcher-hybrid-292m random init (seed 0)",
+            "global_batch": PREFILL_B * world, "seq_len": PREFILL_T,
+            "parallelism": f"dp{world} (batch rows sharded)",
+            "l2": "no flush: weights (584 MB) and per-step activations exceed L2 (126 MB)"}
 
 
 # ----------------------------------------------------------------- CPU legs
@@ -294,8 +303,7 @@ def reference_arm(args, world, rank, cfg):
             "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s",
             "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": "prefill sample on host CPU",
-                                            "model": "dispatcher-hybrid-292m random init"},
+            "data": "synthetic", "config": prefill_config(world),
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": torch.get_num_threads(),
                              "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -363,18 +371,20 @@ def main():
                          "frac": nbytes / (dms * 1e-3) / 1e9 / pk["hbm_gbs"],
                          "bytes_per_step": nbytes}}
     dec_lines["b1"]["vs_reference_a6000_fused_525"] = dec_lines["b1"]["value"] / world / 525.1
+    # batch-1 decode cost across context lengths (flatness)
+    flat = {}
+    for ctx in (256, 1024, 2048):
+        fms, _, _ = run_decode(model, cfg, 1, ctx, 32, args.warmup, 1, world)
+        flat[str(ctx)] = round(fms, 4)
+    flat[str(DECODE_CTX)] = round(dec_lines["b1"]["ms_per_step"], 4)
+    dec_lines["b1_ms_per_step_by_ctx"] = flat
 
     line = {
         "metric": METRIC, "value": world * tokens * 1000.0 / ms, "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": "configs[1]: parallel-forward prefill, 8 x 4096 tokens per GPU, "
-                               "uniform ids (EOT kept, doc-reset mask live)",
-                   "model": "dispatcher-hybrid-292m random init (seed 0)",
-                   "global_batch": PREFILL_B * world, "seq_len": PREFILL_T,
-                   "parallelism": f"dp{world} (batch rows sharded)",
-                   "l2": "no flush: weights (584 MB) and per-step activations exceed L2 (126 MB)"},
+        "config": prefill_config(world),
         "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05, all prefill projections)",
                      "achieved": gemm_tf, "peak": peak_t, "unit": "TFLOP/s",
                      "frac": gemm_tf / peak_t, "traffic": None, "peak_kind": f"{pk_kind} sustained",

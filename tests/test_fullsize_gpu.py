@@ -1,0 +1,85 @@
+"""Size-independent properties at the default 292M config and full context
+(max_len 4096), where the fp32 oracle would take minutes per case:
+causality (exact), decoder == parallel forward (the reference's bf16 rule,
+tests/test_decoding.py:61-86), batched == solo rows
+(tests/test_decoding.py:134-153), and the context limit."""
+
+import pytest
+import torch
+
+from dispatcher_b200 import DispatcherConfig, DispatcherHybridForCausalLM, FusedGraphedHybridDecoder
+from tests.helpers import decisive_argmax_ok
+
+pytestmark = pytest.mark.gpu
+
+BF16_ABS = 1.0   # the reference's bf16 decoder-vs-forward bound (tests/test_decoding.py:177-178)
+
+
+@pytest.fixture(scope="module")
+def model():
+    cfg = DispatcherConfig()
+    m = DispatcherHybridForCausalLM(cfg, seed=1, nondegenerate=True).to("cuda", torch.bfloat16)
+    return m.eval()
+
+
+def _ids(rows, T, seed, vocab=50256):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, vocab, (rows, T), generator=g)
+
+
+def test_causality_exact_at_4096(model):
+    ids = _ids(1, 4096, 11)
+    a = model(ids.cuda()).logits[:, :3000].clone()
+    ids2 = ids.clone()
+    ids2[:, 3000:] = _ids(1, 1096, 12)
+    b = model(ids2.cuda()).logits[:, :3000]
+    assert torch.equal(a, b)
+
+
+def test_decoder_matches_forward_at_3900(model):
+    prompt, steps = 3900, 8
+    ids = _ids(2, prompt + steps, 13).cuda()
+    want = model(ids).logits[:, prompt - 1:prompt - 1 + steps].float()
+    dec = FusedGraphedHybridDecoder(model)
+    got = [dec.prefill(ids[:, :prompt])[:, -1].float()]
+    for i in range(steps - 1):
+        got.append(dec.step(ids[:, prompt + i]).float())
+    got = torch.stack(got, dim=1)
+    assert int(dec.status.item()) == 0
+    err = (got - want).abs().max().item()
+    assert err < BF16_ABS, err
+    ok, agree = decisive_argmax_ok(got.cpu(), want.cpu(), err)
+    assert ok, agree
+
+
+def test_sixteen_lockstep_rows_equal_solo(model):
+    prompt, steps = 1000, 6
+    ids = _ids(16, prompt + steps, 14).cuda()
+    dec = FusedGraphedHybridDecoder(model)
+    batched = [dec.prefill(ids[:, :prompt])[:, -1].float()]
+    for i in range(steps - 1):
+        batched.append(dec.step(ids[:, prompt + i]).float())
+    batched = torch.stack(batched, dim=1)
+    for row in (0, 9, 15):
+        solo_dec = FusedGraphedHybridDecoder(model)
+        solo = [solo_dec.prefill(ids[row:row + 1, :prompt])[:, -1].float()]
+        for i in range(steps - 1):
+            solo.append(solo_dec.step(ids[row:row + 1, prompt + i]).float())
+        solo = torch.stack(solo, dim=1)
+        err = (solo - batched[row:row + 1]).abs().max().item()
+        # the GEMV reduction tree depends on the batch width, so fp32 sums
+        # (and a few bf16 roundings) may differ; argmax must not
+        assert err < 0.1, (row, err)
+        assert torch.equal(solo.argmax(-1), batched[row:row + 1].argmax(-1)), row
+        del solo_dec
+
+
+def test_context_limit_at_max_len(model):
+    dec = FusedGraphedHybridDecoder(model)
+    ids = _ids(1, 4090, 15).cuda()
+    tok = dec.prefill(ids)[:, -1].argmax(-1)
+    while dec.t < dec.max_len:
+        tok = dec.step(tok).argmax(-1)
+    assert dec.t == 4096 and int(dec.status.item()) == 0
+    with pytest.raises(ValueError):
+        dec.step(tok)
