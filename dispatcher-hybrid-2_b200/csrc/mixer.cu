@@ -309,27 +309,32 @@ __global__ void __launch_bounds__(kGateThreads, 1)
         const uint32_t base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((l - l0) * g.NP);
         const float* bias = sBias + l * g.NP;
         const float m = (float)((mbits >> l) & 1u);
-        for (int c = 0; c < 3 * H; c += 16) {
+        const int H3 = 3 * H;
+        const bool mode0 = g.mode == 0;
+        for (int c = 0; c < H3; c += 16) {
           uint32_t v[16];
           tmem_ld16(base + c, v);
           tmem_ld_wait();
+          // 16 independent columns with no early exit and no division, so the
+          // exp / reciprocal chains of the columns overlap.  Columns past 3H
+          // are the zero padding up to NP (bias 0): computed, never stored.
+          float val[16], sg[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const int col = c + e;
-            if (col >= 3 * H) break;
-            const int gi = col / H;
             const float pre = __uint_as_float(v[e]) + bias[col];
-            float val;
-            if (g.mode == 0) {
-              const float sg = sigmoidf_(pre);
-              val = gi == 0 ? sg * m : (gi == 1 ? sg * m + (1.f - m) : sg);
-            } else {
-              val = pre;
-            }
-            stg[col * kTileT + r] = f2bf(val);
-            if (g.rg_hist && gi == 2 && row_ok)
-              g.rg_hist[(((size_t)b * g.rg_T + t) * g.L + l) * H + (col - 2 * H)] =
-                  f2bf(g.mode == 0 ? val : sigmoidf_(pre));
+            sg[e] = sigmoidf_(pre);
+            const float gated = col < H ? sg[e] * m : (col < 2 * H ? fmaf(sg[e], m, 1.f - m) : sg[e]);
+            val[e] = mode0 ? gated : pre;
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (c + e < H3) stg[(c + e) * kTileT + r] = f2bf(val[e]);
+          if (g.rg_hist && row_ok) {  // transmit gates (columns 2H..3H-1) into the decoder cache
+            __nv_bfloat16* rg = g.rg_hist + (((size_t)b * g.rg_T + t) * g.L + l) * H;
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (c + e >= 2 * H && c + e < H3) rg[c + e - 2 * H] = f2bf(sg[e]);
           }
         }
         asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
@@ -337,10 +342,12 @@ __global__ void __launch_bounds__(kGateThreads, 1)
           const int tid_h = q * 32 + lane;  // 0..127 within this half
           if (g.mode == 0) {
             // gates (B, H, L, 3, T): tile column col = gi*H + h -> row ((b*H+h)*L+l)*3+gi
-            const int chunks = 3 * H * (kTileT / 8);
+            static_assert(kTileT / 8 == 16, "16 chunks of 8 positions per tile column");
+            const int chunks = 3 * H * 16;
+#pragma unroll 2
             for (int ck = tid_h; ck < chunks; ck += 128) {
-              const int col = ck / (kTileT / 8), part = ck % (kTileT / 8);
-              const int gi = col / H, h = col - gi * H;
+              const int col = ck >> 4, part = ck & 15;
+              const int gi = (col >= H) + (col >= 2 * H), h = col - gi * H;
               const int tt = t0 + part * 8;
               if (tt >= g.T) continue;
               __nv_bfloat16* dst = g.gates + ((((size_t)b * H + h) * g.L + l) * 3 + gi) * g.T + tt;
