@@ -79,19 +79,38 @@ __global__ void __launch_bounds__(1024) tree_mask_kernel(const int64_t* ids, int
 }
 
 // ------------------------------------------------------------------ gates
-constexpr int kStagesBW = 6;
+// One CTA per 128 positions of one sequence.  For every 64-column slice of the
+// gate-hidden width the CTA builds relu^2(A + m*B[t - 2^l]) for each level
+// straight into tensor memory and contracts it with W_l on the tensor cores
+// (A operand from TMEM, W from shared memory; accumulators in TMEM, one
+// NP-column block per level).  TMEM holds the accumulators of one group of
+// levels in columns [0, 384) and four hidden tiles in [384, 512).  Levels are
+// processed in groups that fit:
+//   group 0, levels 0..min(8, 384/NP)-1 (shift <= 128): one 256-row B window
+//            [t0-128, t0+128) loaded together with the A tile serves them all;
+//   later groups: B tiles of 128 rows, two levels per stage.
+// W is loaded four levels (4*NP rows) per copy.  Fewer, larger copies keep
+// the TMA queue short: each copy costs the pipeline a roughly fixed amount of
+// time whatever its size.
 constexpr int kTileT = 128;
-constexpr int kSlice = 64;  // gate-hidden columns per step (128 B of bf16)
+constexpr int kSlice = 64;                    // gate-hidden columns per step (128 B of bf16)
 constexpr int kSBytes = kTileT * kSlice * 2;  // 16 KB operand tile
-constexpr int kWBytes = 8192;                 // W slot (NP <= 64 rows of 128 B)
+constexpr int kWinLevels = 8;                 // levels served by the B window (2^l <= kTileT)
+constexpr int kABStages = 2;                  // A + B-region stages
+constexpr int kABBytes = 3 * kSBytes;         // A tile + 32 KB B region (window or two tiles)
+constexpr int kWLevels = 4;                   // levels of W per copy
 constexpr int kBuilderWarps = 8;              // 2 threads per tile row
 constexpr int kGateThreads = 64 + kBuilderWarps * 32;
-constexpr int kHBufs = 2;                     // hidden tiles in flight
+constexpr int kHBufs = 4;                     // hidden tiles in flight (TMEM)
+constexpr int kHCols = kSlice / 2;            // TMEM columns of one hidden tile (2 bf16 each)
+constexpr int kHCol0 = 512 - kHBufs * kHCols; // first hidden-tile column
 constexpr int kBiasMax = 16 * 64;             // L * NP floats
+constexpr int kMaxWStages = 3;
 
 struct GateArgs {
   int B, T, H, L, NP, gh;
-  int n_lv, n_calc, group;
+  int n_lv, n_calc;
+  int nws;            // W stages (3 when NP <= 48, else 2)
   const float* bias;  // (L, NP)
   const uint8_t* mask;
   int mask_L;
@@ -103,25 +122,56 @@ struct GateArgs {
   int* err;
 };
 
-constexpr int kGateSmem =
-    1024 + 2 * kSBytes + kStagesBW * (kSBytes + kWBytes) + kHBufs * kSBytes + kBiasMax * 4 + 256;
+__host__ __device__ constexpr int gate_wbytes(int NP) { return kWLevels * NP * 128; }
+__host__ __device__ constexpr int gate_smem(int NP, int nws) {
+  return 1024 + kABStages * kABBytes + nws * gate_wbytes(NP) + 2 * kSBytes + kBiasMax * 4 + 256;
+}
+
+// level groups: group 0 = the window levels, then groups of `cap` levels,
+// cap = accumulator blocks that fit in front of the hidden tiles
+__device__ __forceinline__ int gate_cap(int NP) { return kHCol0 / NP; }
+__device__ __forceinline__ int gate_g0(int NP) { return min(gate_cap(NP), kWinLevels); }
+__device__ __forceinline__ int gate_ngroups(int n_calc, int NP) {
+  const int g0 = gate_g0(NP), cap = gate_cap(NP);
+  return n_calc <= g0 ? 1 : 1 + (n_calc - g0 + cap - 1) / cap;
+}
+__device__ __forceinline__ void gate_group(int grp, int n_calc, int NP, int& l0, int& l1) {
+  const int g0 = gate_g0(NP), cap = gate_cap(NP);
+  l0 = grp == 0 ? 0 : g0 + (grp - 1) * cap;
+  l1 = min(grp == 0 ? g0 : l0 + cap, n_calc);
+}
+// AB stages of a group for one slice, and the levels each one serves
+__device__ __forceinline__ int gate_nab(int grp, int l0, int l1) {
+  return grp == 0 ? 1 : (l1 - l0 + 1) / 2;
+}
+__device__ __forceinline__ void gate_ab_levels(int grp, int i, int l0, int l1, int& a0, int& a1) {
+  if (grp == 0) {
+    a0 = l0;
+    a1 = l1;
+  } else {
+    a0 = l0 + 2 * i;
+    a1 = min(a0 + 2, l1);
+  }
+}
 
 __global__ void __launch_bounds__(kGateThreads, 1)
     gate_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmW, GateArgs g) {
+                const __grid_constant__ CUtensorMap tmBw, const __grid_constant__ CUtensorMap tmW,
+                GateArgs g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* sA = smem;                                   // 2 x 16 KB
-  uint8_t* sBW = sA + 2 * kSBytes;                      // stages x (16 KB B + 8 KB W)
-  uint8_t* sH = sBW + kStagesBW * (kSBytes + kWBytes);  // kHBufs x 16 KB
-  float* sBias = reinterpret_cast<float*>(sH + kHBufs * kSBytes);
+  const int wbytes = gate_wbytes(g.NP);
+  uint8_t* sAB = smem;                                  // kABStages x (A 16 KB + B 32 KB)
+  uint8_t* sW = sAB + kABStages * kABBytes;             // nws x (4 * NP rows of 128 B)
+  uint8_t* sStg = sW + g.nws * wbytes;                  // 2 x 16 KB epilogue staging
+  float* sBias = reinterpret_cast<float*>(sStg + 2 * kSBytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sBias + kBiasMax);
-  uint64_t* a_full = bars;
-  uint64_t* a_empty = bars + 2;
-  uint64_t* bw_full = bars + 4;
-  uint64_t* bw_empty = bw_full + kStagesBW;
-  uint64_t* h_full = bw_empty + kStagesBW;
+  uint64_t* ab_full = bars;
+  uint64_t* ab_empty = ab_full + kABStages;
+  uint64_t* w_full = ab_empty + kABStages;
+  uint64_t* w_empty = w_full + kMaxWStages;
+  uint64_t* h_full = w_empty + kMaxWStages;
   uint64_t* h_empty = h_full + kHBufs;
   uint64_t* d_full = h_empty + kHBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_full + 1);
@@ -129,20 +179,20 @@ __global__ void __launch_bounds__(kGateThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kTileT, b = blockIdx.y;
   const int nk = g.gh / kSlice;
-  const int ngroups = (g.n_calc + g.group - 1) / g.group;
+  const int ngroups = gate_ngroups(g.n_calc, g.NP);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&a_full[i], 1);
-      mbar_init(&a_empty[i], kBuilderWarps);
+    for (int i = 0; i < kABStages; ++i) {
+      mbar_init(&ab_full[i], 1);
+      mbar_init(&ab_empty[i], kBuilderWarps);
+    }
+    for (int i = 0; i < g.nws; ++i) {
+      mbar_init(&w_full[i], 1);
+      mbar_init(&w_empty[i], 1);
     }
     for (int i = 0; i < kHBufs; ++i) {
       mbar_init(&h_full[i], kBuilderWarps);
       mbar_init(&h_empty[i], 1);
-    }
-    for (int s = 0; s < kStagesBW; ++s) {
-      mbar_init(&bw_full[s], 1);
-      mbar_init(&bw_empty[s], 1);
     }
     mbar_init(d_full, 1);
     fence_barrier_init();
@@ -154,6 +204,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmBw);
     prefetch_tmap(&tmW);
   }
   for (int i = threadIdx.x; i < g.L * g.NP; i += blockDim.x) sBias[i] = g.bias[i];
@@ -164,66 +215,82 @@ __global__ void __launch_bounds__(kGateThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {  // ---------------- TMA producer
-      int as = 0, s = 0;
-      uint32_t aph = 0, ph = 0;
-      long fills_a = 0, fills_bw = 0;
+      int abs_ = 0, ws = 0;
+      uint32_t abph = 0, wph = 0;
+      long fills_ab = 0, fills_w = 0;
       bool ok = true;
       for (int grp = 0; grp < ngroups && ok; ++grp) {
-        const int l0 = grp * g.group;
-        const int l1 = min(l0 + g.group, g.n_calc);
+        int l0, l1;
+        gate_group(grp, g.n_calc, g.NP, l0, l1);
+        const int nab = gate_nab(grp, l0, l1);
         for (int kc = 0; kc < nk && ok; ++kc) {
-          if (!mbar_wait(&a_empty[as], aph ^ 1, g.err)) { ok = false; break; }
-          mbar_arrive_expect_tx(&a_full[as], kSBytes);
-          tma_load_3d(&tmA, &a_full[as], sA + as * kSBytes, kc * kSlice, t0, b);
-          ++fills_a;
-          if (++as == 2) { as = 0; aph ^= 1; }
-          for (int l = l0; l < l1; ++l) {
-            if (!mbar_wait(&bw_empty[s], ph ^ 1, g.err)) { ok = false; break; }
-            uint8_t* slot = sBW + s * (kSBytes + kWBytes);
-            mbar_arrive_expect_tx(&bw_full[s], kSBytes + g.NP * 128);
-            tma_load_3d(&tmB, &bw_full[s], slot, kc * kSlice, t0 - (1 << l), b);
-            tma_load_2d(&tmW, &bw_full[s], slot + kSBytes, kc * kSlice, l * g.NP);
-            ++fills_bw;
-            if (++s == kStagesBW) { s = 0; ph ^= 1; }
+          const int x = kc * kSlice;
+          // W of the group's levels, kWLevels levels per copy
+          for (int c0 = l0; c0 < l1 && ok; c0 += kWLevels) {
+            if (!mbar_wait(&w_empty[ws], wph ^ 1, g.err)) { ok = false; break; }
+            mbar_arrive_expect_tx(&w_full[ws], (uint32_t)wbytes);
+            tma_load_2d(&tmW, &w_full[ws], sW + ws * wbytes, x, c0 * g.NP);
+            ++fills_w;
+            if (++ws == g.nws) { ws = 0; wph ^= 1; }
+          }
+          // A tile + the B rows of the stage's levels
+          for (int i = 0; i < nab && ok; ++i) {
+            if (!mbar_wait(&ab_empty[abs_], abph ^ 1, g.err)) { ok = false; break; }
+            uint8_t* st = sAB + abs_ * kABBytes;
+            int a0, a1;
+            gate_ab_levels(grp, i, l0, l1, a0, a1);
+            const uint32_t bytes = grp == 0 ? 3u * kSBytes : (uint32_t)(1 + a1 - a0) * kSBytes;
+            mbar_arrive_expect_tx(&ab_full[abs_], bytes);
+            tma_load_3d(&tmA, &ab_full[abs_], st, x, t0, b);
+            if (grp == 0) {
+              // window rows [t0 - 128, t0 + 128); rows before 0 arrive as zeros
+              tma_load_3d(&tmBw, &ab_full[abs_], st + kSBytes, x, t0 - kTileT, b);
+            } else {
+              for (int l = a0; l < a1; ++l)
+                tma_load_3d(&tmB, &ab_full[abs_], st + (1 + l - a0) * kSBytes, x, t0 - (1 << l), b);
+            }
+            ++fills_ab;
+            if (++abs_ == kABStages) { abs_ = 0; abph ^= 1; }
           }
         }
       }
-      for (int i = 0; i < 2; ++i) {
-        const long n = fills_a / 2 + (i < fills_a % 2 ? 1 : 0);
-        if (n > 0) mbar_wait(&a_full[i], (uint32_t)((n - 1) & 1), nullptr, 1u << 20);
+      // drain: no copy may still be writing shared memory when the CTA exits
+      for (int i = 0; i < kABStages; ++i) {
+        const long n = fills_ab / kABStages + (i < fills_ab % kABStages ? 1 : 0);
+        if (n > 0) mbar_wait(&ab_full[i], (uint32_t)((n - 1) & 1), nullptr, 1u << 20);
       }
-      for (int i = 0; i < kStagesBW; ++i) {
-        const long n = fills_bw / kStagesBW + (i < fills_bw % kStagesBW ? 1 : 0);
-        if (n > 0) mbar_wait(&bw_full[i], (uint32_t)((n - 1) & 1), nullptr, 1u << 20);
+      for (int i = 0; i < g.nws; ++i) {
+        const long n = fills_w / g.nws + (i < fills_w % g.nws ? 1 : 0);
+        if (n > 0) mbar_wait(&w_full[i], (uint32_t)((n - 1) & 1), nullptr, 1u << 20);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
       const uint32_t idesc = idesc_bf16(kTileT, g.NP);
-      int s = 0, hs = 0;
-      uint32_t ph = 0, hph = 0;
+      int ws = 0, hs = 0;
+      uint32_t wph = 0, hph = 0;
       bool ok = true;
       for (int grp = 0; grp < ngroups && ok; ++grp) {
-        const int l0 = grp * g.group;
-        const int l1 = min(l0 + g.group, g.n_calc);
+        int l0, l1;
+        gate_group(grp, g.n_calc, g.NP, l0, l1);
         for (int kc = 0; kc < nk && ok; ++kc) {
           for (int l = l0; l < l1; ++l) {
-            if (!mbar_wait(&bw_full[s], ph, g.err) || !mbar_wait(&h_full[hs], hph, g.err)) {
-              ok = false;
-              break;
-            }
+            const int c0 = l0 + ((l - l0) / kWLevels) * kWLevels;
+            if (l == c0 && !mbar_wait(&w_full[ws], wph, g.err)) { ok = false; break; }
+            if (!mbar_wait(&h_full[hs], hph, g.err)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t hA = smem_u32(sH + hs * kSBytes);
-            const uint32_t wB = smem_u32(sBW + s * (kSBytes + kWBytes) + kSBytes);
+            const uint32_t hA = tmem_base + (uint32_t)(kHCol0 + hs * kHCols);
+            const uint32_t wB = smem_u32(sW + ws * wbytes + (l - c0) * g.NP * 128);
             const uint32_t d = tmem_base + (uint32_t)((l - l0) * g.NP);
 #pragma unroll
-            for (int k = 0; k < kSlice / 16; ++k)
-              umma_bf16(d, sw128_desc(hA + k * 32), sw128_desc(wB + k * 32), idesc,
-                        (kc | k) != 0);
-            umma_commit(&bw_empty[s]);
+            for (int k = 0; k < kSlice / 16; ++k)  // 16 bf16 of K = 8 TMEM columns
+              umma_bf16_ts(d, hA + k * 8, sw128_desc(wB + k * 32), idesc, (kc | k) != 0);
             umma_commit(&h_empty[hs]);
-            if (++s == kStagesBW) { s = 0; ph ^= 1; }
             if (++hs == kHBufs) { hs = 0; hph ^= 1; }
+            if (l + 1 == l1 || l + 1 == c0 + kWLevels) {  // last level of this W copy
+              umma_commit(&w_empty[ws]);
+              if (++ws == g.nws) { ws = 0; wph ^= 1; }
+            }
           }
         }
         if (ok) umma_commit(d_full);
@@ -242,68 +309,82 @@ __global__ void __launch_bounds__(kGateThreads, 1)
       if (g.mask) m = row_ok && g.mask[((size_t)b * g.T + t) * g.mask_L + l] != 0;
       mbits |= (m ? 1u : 0u) << l;
     }
-    int as = 0, s = 0, hs = 0;
-    uint32_t aph = 0, ph = 0, hph = 0, dph = 0;
+    int abs_ = 0, hs = 0;
+    uint32_t abph = 0, hph = 0, dph = 0;
     // A failed (bounded) wait clears `ok`; the thread then skips every
     // further wait but still walks the same loops, so each named barrier
     // below is reached by all builder threads and nothing can hang.
     bool ok = true;
     const int coff = half * 4;  // first of this thread's four 16-byte chunks
     for (int grp = 0; grp < ngroups; ++grp) {
-      const int l0 = grp * g.group;
-      const int l1 = min(l0 + g.group, g.n_calc);
+      int l0, l1;
+      gate_group(grp, g.n_calc, g.NP, l0, l1);
+      const int nab = gate_nab(grp, l0, l1);
       for (int kc = 0; kc < nk; ++kc) {
-        ok = ok && mbar_wait(&a_full[as], aph, g.err);
-        const uint8_t* arow = sA + as * kSBytes + r * 128;
-        uint4 av[4];
+        for (int i = 0; i < nab; ++i) {
+          ok = ok && mbar_wait(&ab_full[abs_], abph, g.err);
+          const uint8_t* st = sAB + abs_ * kABBytes;
+          uint4 av[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          av[j] = *reinterpret_cast<const uint4*>(arow + (((coff + j) ^ (r & 7)) << 4));
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_empty[as]);
-        if (++as == 2) { as = 0; aph ^= 1; }
-        for (int l = l0; l < l1; ++l) {
-          ok = ok && mbar_wait(&bw_full[s], ph, g.err);
-          ok = ok && mbar_wait(&h_empty[hs], hph ^ 1, g.err);
-          // masked rows drop the shifted source (rows with t < 2^l arrive as TMA zeros)
-          const float mf = g.mask ? (float)((mbits >> l) & 1u) : 1.f;
-          const __nv_bfloat162 m2 = __floats2bfloat162_rn(mf, mf);
-          const __nv_bfloat162 z2 = __floats2bfloat162_rn(0.f, 0.f);
-          const uint8_t* brow = sBW + s * (kSBytes + kWBytes) + r * 128;
-          uint8_t* hrow = sH + hs * kSBytes + r * 128;
+          for (int j = 0; j < 4; ++j)
+            av[j] = *reinterpret_cast<const uint4*>(st + r * 128 + (((coff + j) ^ (r & 7)) << 4));
+          int a0, a1;
+          gate_ab_levels(grp, i, l0, l1, a0, a1);
+          for (int l = a0; l < a1; ++l) {
+            ok = ok && mbar_wait(&h_empty[hs], hph ^ 1, g.err);
+            tc_fence_after();
+            // source row t - 2^l: row r + 128 - 2^l of the window (group 0) or
+            // row r of the level's own tile (group 1); rows before position 0
+            // arrive as TMA zeros, which is the wrap mask
+            const int bi = grp == 0 ? r + kTileT - (1 << l) : r;
+            const uint8_t* brow =
+                st + (grp == 0 ? kSBytes : (1 + l - a0) * kSBytes) + bi * 128;
+            // masked rows drop the shifted source
+            const float mf = g.mask ? (float)((mbits >> l) & 1u) : 1.f;
+            const __nv_bfloat162 m2 = __floats2bfloat162_rn(mf, mf);
+            const __nv_bfloat162 z2 = __floats2bfloat162_rn(0.f, 0.f);
+            uint32_t hv[16];  // this thread's 32 hidden values, two per TMEM column
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int off = ((coff + j) ^ (r & 7)) << 4;
-            uint4 bv = *reinterpret_cast<const uint4*>(brow + off);
-            const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&av[j]);
-            __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&bv);
+            for (int j = 0; j < 4; ++j) {
+              uint4 bv = *reinterpret_cast<const uint4*>(brow + (((coff + j) ^ (bi & 7)) << 4));
+              const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&av[j]);
+              __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&bv);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              // bf16 arithmetic as in the reference: (A + m*B) rounded once, relu, squared
-              __nv_bfloat162 x = __hfma2(m2, b2[e], a2[e]);
-              x = __hmax2(x, z2);
-              b2[e] = __hmul2(x, x);
+              for (int e = 0; e < 4; ++e) {
+                // bf16 arithmetic as in the reference: (A + m*B) rounded once, relu, squared
+                __nv_bfloat162 x = __hfma2(m2, b2[e], a2[e]);
+                x = __hmax2(x, z2);
+                b2[e] = __hmul2(x, x);
+              }
+              hv[4 * j] = bv.x;
+              hv[4 * j + 1] = bv.y;
+              hv[4 * j + 2] = bv.z;
+              hv[4 * j + 3] = bv.w;
             }
-            *reinterpret_cast<uint4*>(hrow + off) = bv;
+            tmem_st16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(kHCol0 + hs * kHCols + half * 16),
+                      hv);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&h_full[hs]);
+            if (++hs == kHBufs) { hs = 0; hph ^= 1; }
           }
-          fence_proxy_async();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&h_full[hs]);
-          if (++s == kStagesBW) { s = 0; ph ^= 1; }
-          if (++hs == kHBufs) { hs = 0; hph ^= 1; }
+          if (lane == 0) mbar_arrive(&ab_empty[abs_]);
+          if (++abs_ == kABStages) { abs_ = 0; abph ^= 1; }
         }
       }
       // ---- epilogue of this level group: the two warp halves split the levels.
-      // All MMAs of the group are complete, so the hidden buffers are idle:
-      // half k stages each level's (3H x 128) gate tile in hidden buffer k,
-      // column-major, and the half then writes it as 16-byte runs along T.
+      // All MMAs of the group are complete: half k stages each level's
+      // (3H x 128) gate tile in staging buffer k, column-major, and the half
+      // then writes it as 16-byte runs along T.
       ok = ok && mbar_wait(d_full, dph, g.err);
       dph ^= 1;
       tc_fence_after();
       const int H = g.H;
       const int nl = l1 - l0, mid = (nl + 1) / 2;
       const int la = half ? l0 + mid : l0, lb = half ? l1 : l0 + mid;
-      __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(sH + half * kSBytes);
+      __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(sStg + half * kSBytes);
       const bool vec_out = (g.T % 8) == 0;
       for (int l = la; l < lb; ++l) {
         const uint32_t base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((l - l0) * g.NP);
@@ -369,8 +450,8 @@ __global__ void __launch_bounds__(kGateThreads, 1)
         }
         asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
       }
-      // both halves must be done with their staging buffers (the hidden
-      // buffers) before either starts building the next group into them
+      // both halves must be done reading this group's accumulators before
+      // either builds hidden tiles that start the next group's MMAs
       asm volatile("bar.sync 3, %0;" ::"n"(kBuilderWarps * 32) : "memory");
       tc_fence_before();
     }
@@ -542,35 +623,35 @@ static int launch_gates(const void* a, int lda, const void* bsrc, int ldb, const
              DH_ERR_SHAPE,
              "mixer gates: level counts n_lv=%d n_calc=%d L=%d", g.n_lv, g.n_calc, g.L);
   DH_REQUIRE(lda % 8 == 0 && ldb % 8 == 0, DH_ERR_SHAPE, "mixer gates: row strides must be multiples of 8");
-  g.group = 512 / g.NP;
-  if (g.group > g.n_calc) g.group = g.n_calc;
-  {  // balance the groups
-    const int ng = (g.n_calc + g.group - 1) / g.group;
-    g.group = (g.n_calc + ng - 1) / ng;
-  }
-  CUtensorMap ta, tb, tw;
+  g.nws = g.NP <= 48 ? 3 : 2;
+  const int smem = gate_smem(g.NP, g.nws);
+  CUtensorMap ta, tb, tbw, tw;
   const uint64_t da[3] = {(uint64_t)g.gh, (uint64_t)g.T, (uint64_t)g.B};
   const uint64_t sa[2] = {(uint64_t)lda * 2, (uint64_t)lda * 2 * g.T};
   const uint64_t sb[2] = {(uint64_t)ldb * 2, (uint64_t)ldb * 2 * g.T};
   const uint32_t box3[3] = {kSlice, kTileT, 1};
+  const uint32_t boxw3[3] = {kSlice, 2 * kTileT, 1};
   int rc = make_tmap_bf16(&ta, a, 3, da, sa, box3, true);
   if (rc) return rc;
   rc = make_tmap_bf16(&tb, bsrc, 3, da, sb, box3, true);
   if (rc) return rc;
+  rc = make_tmap_bf16(&tbw, bsrc, 3, da, sb, boxw3, true);
+  if (rc) return rc;
   const uint64_t dw[2] = {(uint64_t)g.gh, (uint64_t)g.L * g.NP};
   const uint64_t sw[1] = {(uint64_t)g.gh * 2};
-  const uint32_t bw[2] = {kSlice, (uint32_t)g.NP};
+  const uint32_t bw[2] = {kSlice, (uint32_t)(kWLevels * g.NP)};
   rc = make_tmap_bf16(&tw, wg, 2, dw, sw, bw, true);
   if (rc) return rc;
   static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_dev != dev) {
-    cudaFuncSetAttribute(gate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGateSmem);
+    cudaFuncSetAttribute(gate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         gate_smem(64, 2) > gate_smem(48, 3) ? gate_smem(64, 2) : gate_smem(48, 3));
     configured_dev = dev;
   }
   dim3 grid((g.T + kTileT - 1) / kTileT, g.B);
-  gate_kernel<<<grid, kGateThreads, kGateSmem, st>>>(ta, tb, tw, g);
+  gate_kernel<<<grid, kGateThreads, smem, st>>>(ta, tb, tbw, tw, g);
   return check_launch("gate_kernel");
 }
 
