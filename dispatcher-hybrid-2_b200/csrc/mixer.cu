@@ -385,7 +385,6 @@ __global__ void __launch_bounds__(kGateThreads, 1)
       const int nl = l1 - l0, mid = (nl + 1) / 2;
       const int la = half ? l0 + mid : l0, lb = half ? l1 : l0 + mid;
       __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(sStg + half * kSBytes);
-      const bool vec_out = (g.T % 8) == 0;
       for (int l = la; l < lb; ++l) {
         const uint32_t base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((l - l0) * g.NP);
         const float* bias = sBias + l * g.NP;
@@ -422,21 +421,34 @@ __global__ void __launch_bounds__(kGateThreads, 1)
         if (l < g.n_lv) {
           const int tid_h = q * 32 + lane;  // 0..127 within this half
           if (g.mode == 0) {
-            // gates (B, H, L, 3, T): tile column col = gi*H + h -> row ((b*H+h)*L+l)*3+gi
-            static_assert(kTileT / 8 == 16, "16 chunks of 8 positions per tile column");
-            const int chunks = 3 * H * 16;
+            // gates (B, H, L, T, 4): (admit, forget, transmit, 0) per position,
+            // two positions per store; tile column col = gi*H + h
+            static_assert(kTileT / 2 == 64, "64 position pairs per tile");
+            const int chunks = H * (kTileT / 2);
 #pragma unroll 2
             for (int ck = tid_h; ck < chunks; ck += 128) {
-              const int col = ck >> 4, part = ck & 15;
-              const int gi = (col >= H) + (col >= 2 * H), h = col - gi * H;
-              const int tt = t0 + part * 8;
+              const int h = ck >> 6, p = (ck & 63) * 2;
+              const int tt = t0 + p;
               if (tt >= g.T) continue;
-              __nv_bfloat16* dst = g.gates + ((((size_t)b * H + h) * g.L + l) * 3 + gi) * g.T + tt;
-              const __nv_bfloat16* srcp = stg + col * kTileT + part * 8;
-              if (vec_out && tt + 8 <= g.T) {
-                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(srcp);
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const uint32_t ga = __bfloat16_as_ushort(stg[h * kTileT + p + e]);
+                const uint32_t gf = __bfloat16_as_ushort(stg[(H + h) * kTileT + p + e]);
+                const uint32_t gr = __bfloat16_as_ushort(stg[(2 * H + h) * kTileT + p + e]);
+                w[2 * e] = ga | (gf << 16);
+                w[2 * e + 1] = gr;
+              }
+              // 8 bytes per position: a pair is 16-byte aligned only when its
+              // first position index (over the whole buffer) is even, which
+              // fails for odd T on every other (head, level) row
+              const size_t e0 = (((size_t)b * H + h) * g.L + l) * (size_t)g.T + tt;
+              __nv_bfloat16* dst = g.gates + e0 * 4;
+              if (tt + 1 < g.T && (e0 & 1) == 0) {
+                *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
               } else {
-                for (int e = 0; e < 8 && tt + e < g.T; ++e) dst[e] = srcp[e];
+                *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+                if (tt + 1 < g.T) *reinterpret_cast<uint2*>(dst + 4) = make_uint2(w[2], w[3]);
               }
             }
           } else if (row_ok) {
@@ -466,20 +478,22 @@ __global__ void __launch_bounds__(kGateThreads, 1)
 
 // ------------------------------------------------------------------ scan
 // One CTA per (sequence, head, 8-channel slice).  Thread j owns positions
-// j, j+512, j+1024, ... of the slice.  V is kept as bf16 in registers and
-// rounded once per level (the reference's bf16 path rounds V after every
-// level, modeling_dispatcher.py:119-120); the update itself is fp32.  The
-// registers are mirrored to shared memory once per level so that every
-// thread can read V(t - 2^l) (consecutive threads touch consecutive 16-byte
-// rows: no bank conflicts).  Gates are double-buffered in registers: level
-// l+1's loads are in flight while level l is computed.
-constexpr int kScanThreads = 512;
-constexpr int kScanPer = 8;  // positions per thread (T <= 4096)
+// j, j+1024, j+2048, j+3072 of the slice.  Per level l (shift s = 2^l), in the
+// reference's order and rounding (modeling_dispatcher.py:116-120, bf16):
+//   msg(t) = r(t) * V(t)                      published to shared memory
+//   V(t)   = f(t) * V(t) + a(t) * msg(t - s)
+// in bf16x2 arithmetic, one rounding per product and per sum.  Each thread
+// needs only the gates of its own positions: one 8-byte load (admit, forget,
+// transmit, 0) per position.  Consecutive threads touch consecutive 16-byte
+// rows of the message buffer (no bank conflicts).  The next level's gates
+// are loaded while the current level is computed.
+constexpr int kScanThreads = 1024;  // 32 warps hide the per-level barrier latency
+constexpr int kScanPer = 4;        // positions per thread (T <= 4096)
 
 struct ScanArgs {
   const __nv_bfloat16* v0;
   int ld_v0;
-  const __nv_bfloat16* gates;  // (B, H, L, 3, T)
+  const __nv_bfloat16* gates;  // (B, H, L, T, 4)
   __nv_bfloat16* out;
   int ld_out;
   int B, T, H, hd, L, n_lv;
@@ -488,18 +502,18 @@ struct ScanArgs {
 };
 
 struct LevelGates {
-  __nv_bfloat16 a[kScanPer], f[kScanPer], r[kScanPer];  // r at the source position t - 2^l
+  uint2 g[kScanPer];  // (admit | forget << 16, transmit) of each owned position
 };
 
-__device__ __forceinline__ void load_level(const __nv_bfloat16* __restrict__ ga, int T, int tid,
-                                           int s, LevelGates& G) {
+__device__ __forceinline__ void load_level(const __nv_bfloat16* __restrict__ gl, int T, int tid,
+                                           LevelGates& G) {
+  // Unconditional loads (positions past the end read the last one and are
+  // never used): a select on the loaded value would make the thread wait for
+  // the loads here instead of where the next level consumes them.
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
-    const int t = tid + i * kScanThreads;
-    const bool in = t < T, src = in && t >= s;
-    G.a[i] = in ? ga[t] : __float2bfloat16_rn(0.f);
-    G.f[i] = in ? ga[T + t] : __float2bfloat16_rn(1.f);
-    G.r[i] = src ? ga[2 * (size_t)T + t - s] : __float2bfloat16_rn(0.f);
+    const int t = min(tid + i * kScanThreads, T - 1);
+    G.g[i] = __ldg(reinterpret_cast<const uint2*>(gl) + t);
   }
 }
 
@@ -521,37 +535,51 @@ __device__ __forceinline__ void write_ring(const ScanArgs& a, const ScanState& s
   }
 }
 
+// broadcast the low / high bf16 of a 32-bit word to both halves
+__device__ __forceinline__ __nv_bfloat162 bcast_lo(uint32_t w) {
+  const uint32_t x = __byte_perm(w, w, 0x1010);
+  return *reinterpret_cast<const __nv_bfloat162*>(&x);
+}
+__device__ __forceinline__ __nv_bfloat162 bcast_hi(uint32_t w) {
+  const uint32_t x = __byte_perm(w, w, 0x3232);
+  return *reinterpret_cast<const __nv_bfloat162*>(&x);
+}
+
 // one level of the sweep; loads the next level's gates into `nxt` first
 __device__ __forceinline__ void scan_level(const ScanArgs& a, ScanState& st, uint4* sx,
                                            const __nv_bfloat16* gbase, int b, int col, int tid,
                                            int l, int nl, const LevelGates& cur,
                                            LevelGates& nxt) {
   const int T = a.T, s = 1 << l;
-  if (l + 1 < nl) load_level(gbase + (size_t)(l + 1) * 3 * T, T, tid, 2 * s, nxt);
+  if (l + 1 < nl) load_level(gbase + (size_t)(l + 1) * 4 * T, T, tid, nxt);
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
     const int t = tid + i * kScanThreads;
-    if (t < T) sx[t] = st.V[i];
+    if (t < T) {
+      const __nv_bfloat162 r2 = bcast_lo(cur.g[i].y);
+      uint4 m = st.V[i];
+      __nv_bfloat162* mv = reinterpret_cast<__nv_bfloat162*>(&m);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mv[e] = __hmul2(r2, mv[e]);  // msg = r * V
+      sx[t] = m;
+    }
   }
   __syncthreads();
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
     const int t = tid + i * kScanThreads;
     if (t >= T) continue;
-    const float f = bf2f(cur.f[i]);
-    float v[8];
-    unpack8(st.V[i], v);
+    const __nv_bfloat162 a2 = bcast_lo(cur.g[i].x), f2 = bcast_hi(cur.g[i].x);
+    __nv_bfloat162* v = reinterpret_cast<__nv_bfloat162*>(&st.V[i]);
     if (t >= s) {
-      const float coef = bf2f(cur.a[i]) * bf2f(cur.r[i]);
-      float vs[8];
-      unpack8(sx[t - s], vs);
+      uint4 m = sx[t - s];
+      const __nv_bfloat162* mv = reinterpret_cast<const __nv_bfloat162*>(&m);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = f * v[e] + coef * vs[e];
+      for (int e = 0; e < 4; ++e) v[e] = __hadd2(__hmul2(f2, v[e]), __hmul2(a2, mv[e]));
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = f * v[e];
+      for (int e = 0; e < 4; ++e) v[e] = __hmul2(f2, v[e]);
     }
-    st.V[i] = pack8(v);
   }
   if (a.ring && l + 1 < a.L) write_ring(a, st, b, col, tid, l + 1);
   __syncthreads();
@@ -574,11 +602,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
                     : make_uint4(0, 0, 0, 0);
   }
   if (a.ring) write_ring(a, st, b, col, tid, 0);
-  const __nv_bfloat16* gbase = a.gates + (((size_t)b * a.H + h) * a.L) * 3 * (size_t)T;
+  const __nv_bfloat16* gbase = a.gates + (((size_t)b * a.H + h) * a.L) * 4 * (size_t)T;
   int nl = a.n_lv;
   while (nl > 0 && (1 << (nl - 1)) > T) --nl;   // the reference stops at shift > T
   LevelGates g0, g1;
-  if (nl > 0) load_level(gbase, T, tid, 1, g0);
+  if (nl > 0) load_level(gbase, T, tid, g0);
   for (int l = 0; l < nl; l += 2) {
     scan_level(a, st, sx, gbase, b, col, tid, l, nl, g0, g1);
     if (l + 1 < nl) scan_level(a, st, sx, gbase, b, col, tid, l + 1, nl, g1, g0);

@@ -83,7 +83,7 @@ class PrefillEngine:
                 P=torch.empty(M, 3 * d, device=dev, dtype=bf),
                 V=torch.empty(M, d, device=dev, dtype=bf),
                 U=torch.empty(M, ff, device=dev, dtype=bf),
-                gates=torch.empty(B, H, L, 3, T, device=dev, dtype=bf),
+                gates=torch.empty(B, H, L, T, 4, device=dev, dtype=bf),
                 mask=torch.empty(B, T, L, device=dev, dtype=torch.uint8))
         return self._bufs[key]
 

@@ -94,12 +94,13 @@ def pack_gate_weights(wi, wf, wr, bi, bf, br):
 
 
 def mixer_gates(a, b, wg, bias, NP, H, L, n_lv, batch, mask=None, rg_hist=None, status=None):
-    """Sigmoid gates (batch, H, L, 3, T) bf16 from A, B rows (batch*T, gh)."""
+    """Sigmoid gates (batch, H, L, T, 4) bf16 from A, B rows (batch*T, gh):
+    (admit, forget, transmit, 0) per position, the level sweep's input."""
     _check(a, "a")
     _check(b, "b")
     M, gh = a.shape
     T = M // batch
-    gates = torch.empty(batch, H, L, 3, T, device=a.device, dtype=torch.bfloat16)
+    gates = torch.empty(batch, H, L, T, 4, device=a.device, dtype=torch.bfloat16)
     _lib.call("dh_mixer_gates", _p(a), a.stride(0), _p(b), b.stride(0), _p(wg), _p(bias),
               _p(mask), batch, T, H, L, NP, gh, n_lv, _p(gates), _p(rg_hist),
               rg_hist.shape[1] if rg_hist is not None else 0, _p(status), _stream())

@@ -152,7 +152,8 @@ DH_API int dh_tree_mask(const int64_t* ids, int batch, int T, int L, int64_t eot
  * transmit) of head h, rows 3H..NP-1 zero (NP % 16 == 0, NP <= 64).
  * bias fp32 (L, NP) in the same order.  mask: uint8 (batch, T, L) from
  * dh_tree_mask, or NULL for the wrap mask alone.  Levels 0..n_lv-1 go to
- * gates bf16 (batch, H, L, 3, T): admit*m, forget*m + 1-m, transmit.  When
+ * gates bf16 (batch, H, L, T, 4): per position (admit*m, forget*m + 1-m,
+ * transmit, 0), the layout dh_level_scan reads.  When
  * rg_hist is not NULL the transmit gates of all L levels are also written
  * to rg_hist bf16 (batch, rg_T, L, H) (decoder cache, decoding.py:164-174). */
 DH_API int dh_mixer_gates(const void* a, int lda, const void* bsrc, int ldb, const void* wg,
@@ -170,7 +171,8 @@ DH_API int dh_gate_preacts_fwd(const void* a, int lda, const void* bsrc, int ldb
                                void* pre_f, void* pre_r, int* status, void* stream);
 
 /* Dyadic level sweep (modeling_dispatcher.py:116-120): for l < n_lv,
- * V(t) <- f_l(t) V(t) + a_l(t) r_l(t-2^l) V(t-2^l).  v0 bf16 (batch*T, hd*H)
+ * V(t) <- f_l(t) V(t) + a_l(t) msg(t-2^l), msg = r_l V, in bf16 with the
+ * reference's rounding points.  v0 bf16 (batch*T, hd*H)
  * with row stride ld_v0 (heads are contiguous 64-channel groups, the
  * reference's transpose at :70-71); gates from dh_mixer_gates; out bf16
  * with row stride ld_out.  ring (nullable): decoder V_ring (batch, 2^(L+1)-2,

@@ -67,10 +67,11 @@ def test_gates_and_scan_small(T, eot):
     ref = oracle.mixer_internals(sd, p, cfg.num_heads, cfg.levels, x, mask)
     gates, V, n_lv = _gpu_internals(sd, p, cfg, x, mask, B, T)
     H = cfg.num_heads
-    g = gates.float().cpu()[:, :, :n_lv]                        # (B, H, n_lv, 3, T)
+    g = gates.float().cpu()[:, :, :n_lv]                        # (B, H, n_lv, T, 4)
     for gi, name in enumerate(("admit", "forget", "transmit")):
         want = ref[name].view(B, H, T, n_lv).permute(0, 1, 3, 2)
-        assert max_err(g[:, :, :, gi], want) < 2e-2, name
+        assert max_err(g[..., gi], want) < 2e-2, name
+    assert torch.equal(g[..., 3], torch.zeros_like(g[..., 3]))
     ref16 = oracle.mixer_internals(cast_sd(sd, torch.bfloat16), p, H, cfg.levels,
                                    x.bfloat16(), mask.bfloat16())["V"].float()
     bound = 2 * max_err(ref16, ref["V"]) + 2e-2
