@@ -7,6 +7,7 @@
 // transpose-reduction so that lane l ends up owning (row, batch) = (l / B, l % B).
 #include <math.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -87,10 +88,11 @@ struct EpiMixerIn {  // W3 = [W_in; W1x; W1s], adjacent row pairs
   }
 };
 
-struct EpiResidual {  // x[b, n] += v
+struct EpiResidual {  // x[b, n] += v (and x_copy[b, n] = the new x when x_copy is set)
   const __nv_bfloat16* w;
   int N, K;
   float* x;
+  float* x_copy;
   __device__ int units() const { return N / 2; }
   __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
     r0 = w + (size_t)(2 * u) * K;
@@ -98,7 +100,10 @@ struct EpiResidual {  // x[b, n] += v
     return true;
   }
   __device__ void store(int u, int b, int row, float v, float, bool) const {
-    x[(size_t)b * N + 2 * u + row] += v;
+    const size_t i = (size_t)b * N + 2 * u + row;
+    const float nx = x[i] + v;
+    x[i] = nx;
+    if (x_copy) x_copy[i] = nx;
   }
 };
 
@@ -410,6 +415,8 @@ struct TreeStepParams {
 // grid (L, H): block (level l, head h) forms the three gate readouts of head h
 // at level l for every row, then the last of the L blocks of head h to finish
 // runs the level recurrence of head h (no block ever waits on another).
+constexpr int kTreeGroups = 8;  // 8-channel groups per head (hd <= 64)
+
 template <int MAXB>
 __global__ void __launch_bounds__(128) tree_step_kernel(TreeStepParams p) {
   constexpr int LMAX = 16;
@@ -501,46 +508,48 @@ __global__ void __launch_bounds__(128) tree_step_kernel(TreeStepParams p) {
   __threadfence();
 
   // level recurrence for head h (fused_step.py:62-88 semantics, fp32 state).
-  // Every level's inputs are read before the serial chain: the ring slots
-  // read (positions t - 2^l) never coincide with the slots written (t).
+  // First every level's inputs are fetched in parallel (one round trip: the
+  // ring slots read, positions t - 2^l, never coincide with the slots
+  // written, position t), then a short serial chain runs from shared memory.
+  __shared__ float s_f[MAXB][LMAX], s_c[MAXB][LMAX];
+  __shared__ uint4 s_v[MAXB][LMAX][kTreeGroups];
   const int groups = p.hd / 8;
-  for (int idx = tid; idx < p.batch * groups; idx += blockDim.x) {
-    const int b = idx / groups;
-    const int c0 = h * p.hd + (idx - b * groups) * 8;
-    __nv_bfloat16* ringb = p.ring + (size_t)b * p.S * d;
-    uint4 vsrc[LMAX];
-    float coef[LMAX], fgv[LMAX];
-#pragma unroll
-    for (int lv = 0; lv < LMAX; ++lv) {
-      if (lv < L) {
-        const long long s = t - (1ll << lv);
-        fgv[lv] = __ldcg(p.fg + ((size_t)b * L + lv) * H + h);
-        coef[lv] = 0.f;
-        vsrc[lv] = make_uint4(0, 0, 0, 0);
-        if (s >= 0) {
-          const float igv = __ldcg(p.ig + ((size_t)b * L + lv) * H + h);
-          const float rgv = bf2f(p.rg[(((size_t)b * p.max_len + s) * L + lv) * H + h]);
-          coef[lv] = igv * rgv;
-          const long long slot = ((2ll << lv) - 2) + (s & ((2ll << lv) - 1));
-          vsrc[lv] = *reinterpret_cast<const uint4*>(ringb + (size_t)slot * d + c0);
-        }
-      }
+  for (int item = tid; item < p.batch * L * groups; item += blockDim.x) {
+    const int b = item / (L * groups), rem = item - b * (L * groups);
+    const int lv = rem / groups, g = rem - lv * groups;
+    const long long s = t - (1ll << lv);
+    uint4 vs = make_uint4(0, 0, 0, 0);
+    if (s >= 0) {
+      const long long slot = ((2ll << lv) - 2) + (s & ((2ll << lv) - 1));
+      vs = *reinterpret_cast<const uint4*>(p.ring + ((size_t)b * p.S + slot) * d + h * p.hd +
+                                           g * 8);
     }
+    s_v[b][lv][g] = vs;
+    if (g == 0) {
+      s_f[b][lv] = __ldcg(p.fg + ((size_t)b * L + lv) * H + h);
+      s_c[b][lv] = s >= 0 ? __ldcg(p.ig + ((size_t)b * L + lv) * H + h) *
+                                bf2f(p.rg[(((size_t)b * p.max_len + s) * L + lv) * H + h])
+                          : 0.f;
+    }
+  }
+  __syncthreads();
+  for (int idx = tid; idx < p.batch * groups; idx += blockDim.x) {
+    const int b = idx / groups, g = idx - b * groups;
+    const int c0 = h * p.hd + g * 8;
+    __nv_bfloat16* ringb = p.ring + (size_t)b * p.S * d;
     float V[8];
     const uint4 v0 = *reinterpret_cast<const uint4*>(p.v0 + (size_t)b * d + c0);
     unpack8(v0, V);
     *reinterpret_cast<uint4*>(ringb + (size_t)(t & 1) * d + c0) = v0;  // ring 0 at t
+    for (int lv = 0; lv < L; ++lv) {
+      float vs[8];
+      unpack8(s_v[b][lv][g], vs);
+      const float f = s_f[b][lv], c = s_c[b][lv];
 #pragma unroll
-    for (int lv = 0; lv < LMAX; ++lv) {
-      if (lv < L) {
-        float vs[8];
-        unpack8(vsrc[lv], vs);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) V[j] = fgv[lv] * V[j] + coef[lv] * vs[j];
-        if (lv + 1 < L) {
-          const long long slot = ((2ll << (lv + 1)) - 2) + (t & ((2ll << (lv + 1)) - 1));
-          *reinterpret_cast<uint4*>(ringb + (size_t)slot * d + c0) = pack8(V);
-        }
+      for (int j = 0; j < 8; ++j) V[j] = f * V[j] + c * vs[j];
+      if (lv + 1 < L) {
+        const long long slot = ((2ll << (lv + 1)) - 2) + (t & ((2ll << (lv + 1)) - 1));
+        *reinterpret_cast<uint4*>(ringb + (size_t)slot * d + c0) = pack8(V);
       }
     }
     *reinterpret_cast<uint4*>(p.y + (size_t)b * d + c0) = pack8(V);
@@ -673,6 +682,209 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
   if (tid == 0) p.counters[b * H + h] = 0;
 }
 
+// ---------------------------------------------------------------- fused FFN
+// h = RMSNorm(x_in); u = silu(h . Wg^T) * (h . Wu^T) (bf16); x += u . Wd^T.
+// One launch instead of two: CTA c owns a contiguous run of u elements,
+// forms them as the SwiGLU GEMV does (warp per unit, transpose-reduction over
+// the lockstep rows), keeps them in shared memory and adds their share of the
+// down projection, rows of Wd^T (ff x d, contiguous per u element), into the
+// fp32 residual x with vector atomics.  x_in is a copy of x written by the
+// preceding residual kernel, so no block reads x while others add into it.
+struct FfnParams {
+  const float* x_in;
+  const __nv_bfloat16* norm_w;
+  const __nv_bfloat16 *wg, *wu, *wdT;
+  float* x;
+  int d, ff, batch, upc;  // upc: u elements per CTA
+};
+
+constexpr int kFfnMaxUpc = 32;
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+constexpr int kFfnWarps = 16;
+constexpr int kFfnMaxK = 2048;  // d supported by the fully unrolled row loop
+
+template <int MAXB>
+__global__ void __launch_bounds__(kFfnWarps * 32) ffn_kernel(FfnParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [batch][d]
+  __shared__ float s_rstd[MAXB];
+  __shared__ float us[MAXB][kFfnMaxUpc];
+  pdl_trigger();
+  const int d = p.d, batch = p.batch;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int u0 = blockIdx.x * p.upc;
+  const int u1 = min(p.ff, u0 + p.upc);
+  // weights do not depend on the previous kernel: warm them into L2
+  for (int u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
+    prefetch_l2(p.wg + (size_t)u * d, (uint32_t)d * 2);
+    prefetch_l2(p.wu + (size_t)u * d, (uint32_t)d * 2);
+    prefetch_l2(p.wdT + (size_t)u * d, (uint32_t)d * 2);
+  }
+  pdl_wait();
+
+  // normalised input rows in shared memory (bf16).  Up to 4 rows: one pass,
+  // every thread keeps its float4s of the rows in registers and the squares
+  // are reduced per row in shared memory; more rows: a warp per row sums,
+  // then all threads scale.
+  if constexpr (MAXB <= 4) {
+    const int k4 = d / 4, n4 = batch * k4;
+    if (threadIdx.x < MAXB) s_rstd[threadIdx.x] = 0.f;  // sums accumulate below
+    __syncthreads();
+    constexpr int NV = (MAXB * kFfnMaxK / 4 + kFfnWarps * 32 - 1) / (kFfnWarps * 32);
+    float4 v[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = threadIdx.x + j * kFfnWarps * 32;
+      float sq = 0.f;
+      if (i < n4) {
+        v[j] = reinterpret_cast<const float4*>(p.x_in)[i];
+        sq = v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+      }
+      if ((k4 & 31) == 0) {  // a warp's 32 float4s lie in one row: reduce first
+        sq = warp_sum(sq);
+        if (lane == 0 && i < n4) atomicAdd(&s_rstd[i / k4], sq);
+      } else if (i < n4) {
+        atomicAdd(&s_rstd[i / k4], sq);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = threadIdx.x + j * kFfnWarps * 32;
+      if (i < n4) {
+        const int b = i / k4, k = (i - b * k4) * 4;
+        const float r = rsqrtf(s_rstd[b] / (float)d + kNormEps);
+        uint2 pk;
+        pk.x = pack2(v[j].x * r * bf2f(p.norm_w[k]), v[j].y * r * bf2f(p.norm_w[k + 1]));
+        pk.y = pack2(v[j].z * r * bf2f(p.norm_w[k + 2]), v[j].w * r * bf2f(p.norm_w[k + 3]));
+        *reinterpret_cast<uint2*>(xs + (size_t)b * d + k) = pk;
+      }
+    }
+  } else {
+    for (int b = warp; b < batch; b += kFfnWarps) {
+      const float4* xr = reinterpret_cast<const float4*>(p.x_in + (size_t)b * d);
+      float ss = 0.f;
+      for (int i = lane; i < d / 4; i += 32) {
+        const float4 v = xr[i];
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) s_rstd[b] = rsqrtf(ss / (float)d + kNormEps);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < batch * d / 4; i += blockDim.x) {
+      const int b = i / (d / 4), k = (i - b * (d / 4)) * 4;
+      const float4 v = reinterpret_cast<const float4*>(p.x_in + (size_t)b * d)[k / 4];
+      const float r = s_rstd[b];
+      uint2 pk;
+      pk.x = pack2(v.x * r * bf2f(p.norm_w[k]), v.y * r * bf2f(p.norm_w[k + 1]));
+      pk.y = pack2(v.z * r * bf2f(p.norm_w[k + 2]), v.w * r * bf2f(p.norm_w[k + 3]));
+      *reinterpret_cast<uint2*>(xs + (size_t)b * d + k) = pk;
+    }
+  }
+  __syncthreads();
+
+  // u elements of this CTA: warp per element, gate and up rows together; the
+  // whole row pair is requested at once (one round trip per element)
+  for (int u = u0 + warp; u < u1; u += kFfnWarps) {
+    const __nv_bfloat16* r0 = p.wg + (size_t)u * d;
+    const __nv_bfloat16* r1 = p.wu + (size_t)u * d;
+    float acc[2 * MAXB];
+#pragma unroll
+    for (int i = 0; i < 2 * MAXB; ++i) acc[i] = 0.f;
+    auto fma_chunk = [&](const uint4& ua, const uint4& ub, int k) {
+      float fa[8], fb[8];
+      unpack8(ua, fa);
+      unpack8(ub, fb);
+#pragma unroll
+      for (int b = 0; b < MAXB; ++b) {
+        if (b < batch) {
+          float fx[8];
+          unpack8(*reinterpret_cast<const uint4*>(xs + (size_t)b * d + k), fx);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            acc[b] = fmaf(fa[j], fx[j], acc[b]);
+            acc[MAXB + b] = fmaf(fb[j], fx[j], acc[MAXB + b]);
+          }
+        }
+      }
+    };
+    if constexpr (MAXB <= 4) {
+      // the whole row pair requested at once: one round trip per element
+      constexpr int KI = kFfnMaxK / 256;
+      uint4 wa[KI], wb[KI];
+#pragma unroll
+      for (int i = 0; i < KI; ++i) {
+        const int k = lane * 8 + i * 256;
+        if (k < d) {
+          wa[i] = ld_stream16(r0 + k);
+          wb[i] = ld_stream16(r1 + k);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < KI; ++i) {
+        const int k = lane * 8 + i * 256;
+        if (k < d) fma_chunk(wa[i], wb[i], k);
+      }
+    } else {
+#pragma unroll 2
+      for (int k = lane * 8; k < d; k += 256) fma_chunk(ld_stream16(r0 + k), ld_stream16(r1 + k), k);
+    }
+    const float rr = transpose_reduce<2 * MAXB>(acc);
+    const float other = __shfl_xor_sync(0xffffffffu, rr, MAXB);
+    const int b = lane % MAXB, row = (lane / MAXB) & 1;
+    if (lane < 2 * MAXB && row == 0 && b < batch) {
+      const float g = rr, up = other;
+      us[b][u - u0] = bf2f(f2bf(g / (1.0f + expf(-g)) * up));  // u in bf16, as the reference
+    }
+  }
+  __syncthreads();
+
+  // this CTA's share of the down projection: x[b, o] += sum_j Wd^T[u0 + j, o] * u[b, j]
+  const int nu = u1 - u0;
+  for (int o = threadIdx.x * 4; o < d; o += blockDim.x * 4) {
+    float acc[MAXB][4];
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.f;
+    auto fma_row = [&](const uint2& w2, int j) {
+      const float2 wa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w2.x));
+      const float2 wb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w2.y));
+#pragma unroll
+      for (int b = 0; b < MAXB; ++b) {
+        if (b < batch) {
+          const float uv = us[b][j];
+          acc[b][0] = fmaf(wa.x, uv, acc[b][0]);
+          acc[b][1] = fmaf(wa.y, uv, acc[b][1]);
+          acc[b][2] = fmaf(wb.x, uv, acc[b][2]);
+          acc[b][3] = fmaf(wb.y, uv, acc[b][3]);
+        }
+      }
+    };
+    if constexpr (MAXB <= 4) {  // every row requested at once
+      uint2 w[kFfnMaxUpc];
+#pragma unroll
+      for (int j = 0; j < kFfnMaxUpc; ++j)
+        if (j < nu) w[j] = __ldg(reinterpret_cast<const uint2*>(p.wdT + (size_t)(u0 + j) * d + o));
+#pragma unroll
+      for (int j = 0; j < kFfnMaxUpc; ++j)
+        if (j < nu) fma_row(w[j], j);
+    } else {
+#pragma unroll 4
+      for (int j = 0; j < nu; ++j)
+        fma_row(__ldg(reinterpret_cast<const uint2*>(p.wdT + (size_t)(u0 + j) * d + o)), j);
+    }
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b)
+      if (b < batch) red_add_v4(p.x + (size_t)b * d + o, acc[b][0], acc[b][1], acc[b][2], acc[b][3]);
+  }
+}
+
 // ---------------------------------------------------------------- small ones
 __global__ void embed_kernel(const int64_t* tokens, const __nv_bfloat16* emb, float* x, int d,
                              int vocab, int* status) {
@@ -744,7 +956,8 @@ extern "C" int dh_decode_tree_step(const void* a_in, const void* b_hist, const v
   DH_REQUIRE(a_in && b_hist && wi && wf && wr && bi && bf && br && t_buf && ig && fg && rg_hist &&
                  v0 && v_ring && y && counters,
              DH_ERR_ARG, "dh_decode_tree_step: null pointer");
-  DH_REQUIRE(L >= 1 && L <= 16 && H >= 1 && hd % 8 == 0 && gh % 8 == 0 && batch > 0,
+  DH_REQUIRE(L >= 1 && L <= 16 && H >= 1 && hd % 8 == 0 && hd <= 8 * kTreeGroups &&
+                 gh % 8 == 0 && batch > 0,
              DH_ERR_SHAPE, "dh_decode_tree_step: bad sizes (L=%d H=%d hd=%d gh=%d)", L, H, hd, gh);
   const int d = H * hd, S = (1 << (L + 1)) - 2;
   for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
@@ -767,16 +980,59 @@ extern "C" int dh_decode_tree_step(const void* a_in, const void* b_hist, const v
   return DH_OK;
 }
 
-extern "C" int dh_decode_linear_residual(const void* y, const void* w, float* x, int batch, int k,
-                                         int d_out, void* stream) {
+extern "C" int dh_decode_linear_residual(const void* y, const void* w, float* x, float* x_copy,
+                                         int batch, int k, int d_out, void* stream) {
   DH_REQUIRE(y && w && x, DH_ERR_ARG, "dh_decode_linear_residual: null pointer");
   DH_REQUIRE(d_out % 2 == 0, DH_ERR_SHAPE, "dh_decode_linear_residual: odd output width");
   for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
     const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
     GemvIn in{BF(y) + (size_t)b0 * k, 0, nullptr, k, nb};
-    EpiResidual e{BF(w), d_out, k, x + (size_t)b0 * d_out};
+    EpiResidual e{BF(w), d_out, k, x + (size_t)b0 * d_out,
+                  x_copy ? x_copy + (size_t)b0 * d_out : nullptr};
     int rc = launch_gemv(in, e, d_out / 2, STREAM(stream));
     if (rc) return rc;
+  }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_ffn(const float* x_in, const void* norm_w, const void* w_gate,
+                             const void* w_up, const void* w_down_t, float* x, int batch, int d,
+                             int ff, void* stream) {
+  DH_REQUIRE(x_in && norm_w && w_gate && w_up && w_down_t && x, DH_ERR_ARG,
+             "dh_decode_ffn: null pointer");
+  DH_REQUIRE(d % 8 == 0 && d <= 2048 && ff >= 1 && batch >= 1, DH_ERR_SHAPE,
+             "dh_decode_ffn: unsupported sizes d=%d ff=%d", d, ff);
+  DH_REQUIRE(aligned16(x_in) && aligned16(x) && aligned16(w_gate) && aligned16(w_up) &&
+                 aligned16(w_down_t),
+             DH_ERR_ARG, "dh_decode_ffn: pointers must be 16-byte aligned");
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaFuncSetAttribute(ffn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2048 * 2);
+    cudaFuncSetAttribute(ffn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * 2048 * 2);
+    cudaFuncSetAttribute(ffn_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         16 * 2048 * 2);
+    configured_dev = dev;
+  }
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    const int maxb = nb == 1 ? 1 : (nb <= 4 ? 4 : 16);
+    // one wave of CTAs at small batches; more u elements per CTA (fewer
+    // atomic row updates) at large batches
+    const int upc = maxb >= 16 ? kFfnMaxUpc
+                               : std::min(kFfnMaxUpc, std::max(8, (ff + sm_count() - 1) / sm_count()));
+    FfnParams prm{x_in + (size_t)b0 * d, BF(norm_w), BF(w_gate), BF(w_up), BF(w_down_t),
+                  x + (size_t)b0 * d, d, ff, nb, upc};
+    const dim3 grid((ff + upc - 1) / upc);
+    const size_t smem = (size_t)maxb * d * 2;
+    const int bad = maxb == 1 ? launch_pdl(ffn_kernel<1>, grid, dim3(kFfnWarps * 32), smem,
+                                           STREAM(stream), prm)
+                    : maxb == 4 ? launch_pdl(ffn_kernel<4>, grid, dim3(kFfnWarps * 32), smem,
+                                             STREAM(stream), prm)
+                                : launch_pdl(ffn_kernel<16>, grid, dim3(kFfnWarps * 32), smem,
+                                             STREAM(stream), prm);
+    if (bad) return check_launch("ffn_kernel");
   }
   return DH_OK;
 }

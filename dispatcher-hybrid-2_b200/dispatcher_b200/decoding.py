@@ -136,6 +136,7 @@ class FusedGraphedHybridDecoder:
         self.t_buf = torch.zeros(1, dtype=torch.long, device=dev)
         self.logits_out = torch.zeros(batch, cfg.vocab_size, device=dev, dtype=bf)
         self.x = torch.zeros(batch, d, device=dev, dtype=f32)
+        self.x_copy = torch.zeros(batch, d, device=dev, dtype=f32)   # input of the fused FFN
         self.v0 = torch.zeros(batch, d, device=dev, dtype=bf)
         self.a = torch.zeros(batch, d, device=dev, dtype=bf)
         self.y = torch.zeros(batch, d, device=dev, dtype=bf)
@@ -154,6 +155,11 @@ class FusedGraphedHybridDecoder:
         # (dh_decode_step); larger batches run the per-op kernels in 16-row chunks
         self.persistent = (self.step_kernel == "persistent" and batch <= 16 and d <= 1024
                            and d % 8 == 0 and hd == 64 and cfg.levels <= 16)
+        if not self.persistent:
+            # the fused FFN reads the down projection by rows of its transpose
+            for lay in self.w.layers:
+                if "w_downT" not in lay:
+                    lay["w_downT"] = lay["w_down"].t().contiguous()
         self._step_params = None
         if self.persistent:
             from .step_params import build_step_params
@@ -192,10 +198,12 @@ class FusedGraphedHybridDecoder:
                 call("dh_decode_attn", P(self.q), P(cache.k), P(cache.v), P(self.y),
                      P(self.t_buf), P(self.part), P(attn_ctr), self.nsplit, B, self.max_len,
                      H, hd, cfg.attn_window, s)
-            call("dh_decode_linear_residual", P(self.y), P(lay["w_out"]), P(self.x), B, d, d, s)
-            call("dh_decode_ffn_in", P(self.x), P(lay["norm2"]), P(lay["w_gate"]),
-                 P(lay["w_up"]), P(self.u), B, d, ff, s)
-            call("dh_decode_linear_residual", P(self.u), P(lay["w_down"]), P(self.x), B, ff, d, s)
+            # output projection + residual (also leaves a copy of x for the FFN),
+            # then the whole FFN with its residual in one launch
+            call("dh_decode_linear_residual", P(self.y), P(lay["w_out"]), P(self.x),
+                 P(self.x_copy), B, d, d, s)
+            call("dh_decode_ffn", P(self.x_copy), P(lay["norm2"]), P(lay["w_gate"]),
+                 P(lay["w_up"]), P(lay["w_downT"]), P(self.x), B, d, ff, s)
         call("dh_decode_logits", P(self.x), P(W.norm_out), P(W.lm_head), P(self.logits_out),
              B, d, V, s)
         call("dh_decode_advance", P(self.t_buf), s)

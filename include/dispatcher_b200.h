@@ -74,9 +74,19 @@ DH_API int dh_decode_tree_step(const void* a_in, const void* b_hist, const void*
                         int max_len, int L, int H, int hd, int gh, void* stream);
 
 /* x += y . W^T (W: d_out x k, bf16; y bf16 (batch, k)): linear_out and
- * linear_down with the residual add (decoding.py:487-488, 434-435). */
-DH_API int dh_decode_linear_residual(const void* y, const void* w, float* x, int batch, int k,
-                              int d_out, void* stream);
+ * linear_down with the residual add (decoding.py:487-488, 434-435).  x_copy
+ * (nullable) receives a copy of the updated x (the input of dh_decode_ffn). */
+DH_API int dh_decode_linear_residual(const void* y, const void* w, float* x, float* x_copy,
+                              int batch, int k, int d_out, void* stream);
+
+/* Whole SwiGLU feed-forward with the residual add, one launch
+ * (modeling_dispatcher.py:196-197, decoding.py:434-435, 488):
+ * x += silu(RMSNorm(x_in) . Wg^T) * (RMSNorm(x_in) . Wu^T) . Wd^T, u rounded
+ * to bf16.  x_in: fp32 (batch, d), a copy of x (from dh_decode_linear_residual);
+ * w_down_t: Wd transposed, bf16 (ff, d); x fp32 (batch, d) receives the down
+ * projection through atomic adds (summation order not fixed).  d <= 2048. */
+DH_API int dh_decode_ffn(const float* x_in, const void* norm_w, const void* w_gate, const void* w_up,
+                  const void* w_down_t, float* x, int batch, int d, int ff, void* stream);
 
 /* FFN input side: h = RMSNorm(x; norm_w); u = silu(h . Wg^T) * (h . Wu^T),
  * bf16 (batch, ff) (modeling_dispatcher.py:196-197). */

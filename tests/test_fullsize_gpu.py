@@ -67,10 +67,13 @@ def test_sixteen_lockstep_rows_equal_solo(model):
             solo.append(solo_dec.step(ids[row:row + 1, prompt + i]).float())
         solo = torch.stack(solo, dim=1)
         err = (solo - batched[row:row + 1]).abs().max().item()
-        # the GEMV reduction tree depends on the batch width, so fp32 sums
-        # (and a few bf16 roundings) may differ; argmax must not
+        # the GEMV reduction tree depends on the batch width and residual
+        # adds may be accumulated in any order, so fp32 sums (and a few bf16
+        # roundings) may differ; decisive argmaxes must not (the reference's
+        # bf16 rule, tests/test_decoding.py:61-86)
         assert err < 0.1, (row, err)
-        assert torch.equal(solo.argmax(-1), batched[row:row + 1].argmax(-1)), row
+        ok, agree = decisive_argmax_ok(solo.cpu(), batched[row:row + 1].cpu(), err)
+        assert ok, (row, agree)
         del solo_dec
 
 
