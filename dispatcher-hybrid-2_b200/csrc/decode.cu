@@ -514,6 +514,7 @@ __global__ void __launch_bounds__(128) tree_step_kernel(TreeStepParams p) {
   __shared__ float s_f[MAXB][LMAX], s_c[MAXB][LMAX];
   __shared__ uint4 s_v[MAXB][LMAX][kTreeGroups];
   const int groups = p.hd / 8;
+#pragma unroll 4
   for (int item = tid; item < p.batch * L * groups; item += blockDim.x) {
     const int b = item / (L * groups), rem = item - b * (L * groups);
     const int lv = rem / groups, g = rem - lv * groups;
