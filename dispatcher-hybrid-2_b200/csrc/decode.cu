@@ -409,6 +409,7 @@ struct TreeStepParams {
   __nv_bfloat16* ring;
   __nv_bfloat16* y;
   int* counters;
+  const int* doc;  // nullable: document id per (row, position), (batch, max_len)
   int batch, max_len, L, H, hd, gh, S;
 };
 
@@ -444,6 +445,17 @@ __global__ void __launch_bounds__(128) tree_step_kernel(TreeStepParams p) {
   }
   pdl_wait();
 
+  // per-row level mask: the source position exists and, with document
+  // tracking, lies in the same document (the parallel forward's doc-reset
+  // mask, modeling_dispatcher.py:311-323)
+  __shared__ bool s_ok[MAXB];
+  if (tid < MAXB) {
+    bool okb = ok && tid < p.batch;
+    if (okb && p.doc)
+      okb = p.doc[(size_t)tid * p.max_len + srcc] == p.doc[(size_t)tid * p.max_len + t];
+    s_ok[tid] = okb;
+  }
+  __syncthreads();
   float acc[MAXB][3];
 #pragma unroll
   for (int b = 0; b < MAXB; ++b) acc[b][0] = acc[b][1] = acc[b][2] = 0.f;
@@ -457,7 +469,7 @@ __global__ void __launch_bounds__(128) tree_step_kernel(TreeStepParams p) {
       if (b < p.batch) {
         float fa[8], fs[8];
         unpack8(*reinterpret_cast<const uint4*>(p.a + (size_t)b * gh + k), fa);
-        if (ok) {
+        if (s_ok[b]) {
           unpack8(*reinterpret_cast<const uint4*>(p.bh + ((size_t)b * p.max_len + srcc) * gh + k),
                   fs);
         } else {
@@ -491,7 +503,7 @@ __global__ void __launch_bounds__(128) tree_step_kernel(TreeStepParams p) {
 #pragma unroll
     for (int g = 0; g < 3; ++g) pre[g] = red[0][b * 3 + g] + red[1][b * 3 + g] + red[2][b * 3 + g] + red[3][b * 3 + g];
     const int lh = l * H + h;
-    const float okf = ok ? 1.f : 0.f;
+    const float okf = s_ok[b] ? 1.f : 0.f;
     const float ig = sigmoidf_(pre[0] + p.bi[lh]) * okf;
     const float fg = sigmoidf_(pre[1] + p.bf[lh]) * okf + (1.f - okf);
     const float rg = sigmoidf_(pre[2] + p.br[lh]);
@@ -906,6 +918,22 @@ __global__ void embed_kernel(const int64_t* tokens, const __nv_bfloat16* emb, fl
   }
 }
 
+// document id of the position being decoded: the previous position's id,
+// plus one if the previous token was the separator (exclusive cumulative
+// count of separators, the forward's doc_id)
+__global__ void doc_step_kernel(const int64_t* tokens, const int64_t* t_buf, int* doc,
+                                int64_t* last_tok, int64_t eot, int max_len, int batch) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  const long long t = *t_buf;
+  if (t < 0 || t >= max_len) return;
+  const int id = t > 0 ? doc[(size_t)b * max_len + t - 1] + (last_tok[b] == eot ? 1 : 0) : 0;
+  doc[(size_t)b * max_len + t] = id;
+  last_tok[b] = tokens[b];
+}
+
 __global__ void advance_kernel(int64_t* t) {
   pdl_trigger();
   pdl_wait();
@@ -952,8 +980,9 @@ extern "C" int dh_decode_tree_step(const void* a_in, const void* b_hist, const v
                                    const void* wf, const void* wr, const float* bi,
                                    const float* bf, const float* br, const int64_t* t_buf,
                                    float* ig, float* fg, void* rg_hist, const void* v0,
-                                   void* v_ring, void* y, int* counters, int batch, int max_len,
-                                   int L, int H, int hd, int gh, void* stream) {
+                                   void* v_ring, void* y, int* counters, const int* doc_hist,
+                                   int batch, int max_len, int L, int H, int hd, int gh,
+                                   void* stream) {
   DH_REQUIRE(a_in && b_hist && wi && wf && wr && bi && bf && br && t_buf && ig && fg && rg_hist &&
                  v0 && v_ring && y && counters,
              DH_ERR_ARG, "dh_decode_tree_step: null pointer");
@@ -971,7 +1000,8 @@ extern "C" int dh_decode_tree_step(const void* a_in, const void* b_hist, const v
                      BF(v0) + (size_t)b0 * d,
                      BFM(v_ring) + (size_t)b0 * S * d,
                      BFM(y) + (size_t)b0 * d,
-                     counters, nb, max_len, L, H, hd, gh, S};
+                     counters, doc_hist ? doc_hist + (size_t)b0 * max_len : nullptr,
+                     nb, max_len, L, H, hd, gh, S};
     dim3 grid(L, H);
     const int bad = nb == 1   ? launch_pdl(tree_step_kernel<1>, grid, dim3(128), 0, STREAM(stream), p)
                     : nb <= 4 ? launch_pdl(tree_step_kernel<4>, grid, dim3(128), 0, STREAM(stream), p)
@@ -1114,6 +1144,18 @@ extern "C" int dh_decode_logits(const float* x, const void* norm_w, const void* 
     int rc = launch_gemv(in, e, (vocab + 1) / 2, STREAM(stream));
     if (rc) return rc;
   }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_doc_step(const int64_t* tokens, const int64_t* t_buf, int* doc_hist,
+                                  int64_t* last_tok, int64_t eot, int batch, int max_len,
+                                  void* stream) {
+  DH_REQUIRE(tokens && t_buf && doc_hist && last_tok, DH_ERR_ARG,
+             "dh_decode_doc_step: null pointer");
+  DH_REQUIRE(batch >= 1 && max_len >= 1, DH_ERR_SHAPE, "dh_decode_doc_step: bad sizes");
+  if (launch_pdl(doc_step_kernel, dim3((batch + 127) / 128), dim3(128), 0, STREAM(stream), tokens,
+                 t_buf, doc_hist, last_tok, eot, max_len, batch))
+    return check_launch("doc_step_kernel");
   return DH_OK;
 }
 

@@ -84,12 +84,22 @@ class _DirectStep:
 class FusedGraphedHybridDecoder:
     """Exact per-token decoder on B200 kernels, one CUDA-graph replay per token."""
 
-    def __init__(self, model, max_len=None, dtype=None, step_kernel="graph"):
+    def __init__(self, model, max_len=None, dtype=None, step_kernel="graph",
+                 multi_document=False):
         """step_kernel: "graph" (per-op kernels captured in one CUDA graph) or
-        "persistent" (one cooperative kernel per step, batch <= 16)."""
+        "persistent" (one cooperative kernel per step, batch <= 16).
+
+        multi_document: accept prompts (and generated tokens) that contain the
+        document separator of a doc_reset model.  The decoder then keeps each
+        row's document id per position and masks every tree level across a
+        separator, as the parallel forward does; by default it refuses such
+        prompts like the reference's decoders (decoding.py:89-98)."""
         if step_kernel not in ("graph", "persistent"):
             raise ValueError(f"step_kernel must be 'graph' or 'persistent', got {step_kernel!r}")
+        if multi_document and step_kernel != "graph":
+            raise ValueError("multi_document decoding runs on step_kernel='graph'")
         self.step_kernel = step_kernel
+        self.multi_document = bool(multi_document)
         if not torch.cuda.is_available():
             raise RuntimeError("FusedGraphedHybridDecoder requires CUDA")
         param_dtype = next(model.parameters()).dtype
@@ -133,6 +143,11 @@ class FusedGraphedHybridDecoder:
         f32, bf = torch.float32, torch.bfloat16
         ff = cfg.dim_feedforward
         self.token_buf = torch.zeros(batch, dtype=torch.long, device=dev)
+        # document ids per (row, position) and each row's last token, used
+        # only when the decoder tracks documents
+        self.doc_hist = (torch.zeros(batch, self.max_len, dtype=torch.int32, device=dev)
+                         if self.multi_document else None)
+        self.last_tok = torch.zeros(batch, dtype=torch.long, device=dev)
         self.t_buf = torch.zeros(1, dtype=torch.long, device=dev)
         self.logits_out = torch.zeros(batch, cfg.vocab_size, device=dev, dtype=bf)
         self.x = torch.zeros(batch, d, device=dev, dtype=f32)
@@ -179,6 +194,9 @@ class FusedGraphedHybridDecoder:
         s = ctypes_void(stream)
         P = _ptr
         call = _lib.call
+        if self.doc_hist is not None:
+            call("dh_decode_doc_step", P(self.token_buf), P(self.t_buf), P(self.doc_hist),
+                 P(self.last_tok), cfg.eot_token, B, self.max_len, s)
         call("dh_decode_embed", P(self.token_buf), P(W.emb), P(self.x), B, d, V,
              P(self.status), s)
         tree_ctr = self.counters[:H]
@@ -190,7 +208,8 @@ class FusedGraphedHybridDecoder:
                 call("dh_decode_tree_step", P(self.a), P(cache.B_hist), P(lay["wi"]),
                      P(lay["wf"]), P(lay["wr"]), P(lay["bi"]), P(lay["bf"]), P(lay["br"]),
                      P(self.t_buf), P(self.ig), P(self.fg), P(cache.rg_hist), P(self.v0),
-                     P(cache.V_ring), P(self.y), P(tree_ctr), B, self.max_len, L, H, hd, d, s)
+                     P(cache.V_ring), P(self.y), P(tree_ctr), P(self.doc_hist), B,
+                     self.max_len, L, H, hd, d, s)
             else:
                 call("dh_decode_attn_in", P(self.x), P(lay["norm1"]), P(lay["wqkv"]),
                      P(cache.rope_cos), P(cache.rope_sin), P(self.q), P(cache.k), P(cache.v),
@@ -234,7 +253,8 @@ class FusedGraphedHybridDecoder:
     def _prepare_prompt(self, idx):
         self._squeeze = idx.dim() == 1
         ids = idx.view(1, -1) if self._squeeze else idx
-        check_single_document(self.cfg, ids)
+        if not self.multi_document:
+            check_single_document(self.cfg, ids)
         T = ids.shape[1]
         if T > self.max_len:
             raise ValueError(f"prompt of {T} exceeds max_len {self.max_len}")
@@ -263,6 +283,12 @@ class FusedGraphedHybridDecoder:
             from .engine import PrefillEngine
             self._engine = PrefillEngine(self.m, packed=self.w)
         out = self._engine.forward(ids, caches=self.caches)
+        if self.doc_hist is not None:
+            # exclusive count of separators before each position (the
+            # forward's doc_id); later positions come from the step kernels
+            sep = (ids == self.cfg.eot_token).to(torch.int32)
+            self.doc_hist[:, :T] = torch.cumsum(sep, 1, dtype=torch.int32) - sep
+            self.last_tok.copy_(ids[:, T - 1])
         self.t = T
         self.t_buf.fill_(T)
         return out[0] if self._squeeze else out

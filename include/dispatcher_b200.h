@@ -66,12 +66,17 @@ DH_API int dh_decode_mixer_in(const float* x, const void* norm_w, const void* w3
  * decoding.py:477-486).  Gate weights Wi/Wf/Wr bf16 (L, H, gh), biases fp32
  * (L, H).  ig/fg: fp32 scratch (batch, L, H); counters: int scratch (H),
  * zero before the first call and left zero after each call.  Writes
- * rg_hist[:, t], ring slots of every level at t, and y (batch, d) bf16. */
+ * rg_hist[:, t], ring slots of every level at t, and y (batch, d) bf16.
+ * doc_hist (nullable): int (batch, max_len) document id per position; level l
+ * is then also masked where doc(t - 2^l) != doc(t), the parallel forward's
+ * doc-reset mask (modeling_dispatcher.py:311-323), so prompts may hold
+ * several documents (the reference decoder refuses them, decoding.py:89-98). */
 DH_API int dh_decode_tree_step(const void* a_in, const void* b_hist, const void* wi, const void* wf,
                         const void* wr, const float* bi, const float* bf, const float* br,
                         const int64_t* t_buf, float* ig, float* fg, void* rg_hist,
-                        const void* v0, void* v_ring, void* y, int* counters, int batch,
-                        int max_len, int L, int H, int hd, int gh, void* stream);
+                        const void* v0, void* v_ring, void* y, int* counters,
+                        const int* doc_hist, int batch, int max_len, int L, int H, int hd, int gh,
+                        void* stream);
 
 /* x += y . W^T (W: d_out x k, bf16; y bf16 (batch, k)): linear_out and
  * linear_down with the residual add (decoding.py:487-488, 434-435).  x_copy
@@ -126,6 +131,13 @@ DH_API int dh_decode_attn_noalloc(const void* q, const void* k_cache, const void
 /* logits = RMSNorm(x; norm_w) . E^T, bf16 (batch, vocab) (decoding.py:442). */
 DH_API int dh_decode_logits(const float* x, const void* norm_w, const void* emb, void* logits,
                      int batch, int d, int vocab, void* stream);
+
+/* Document tracking for multi-document decoding (no counterpart in the
+ * reference decoder, which refuses separators in the prompt): doc_hist[b, t]
+ * = doc_hist[b, t-1] + (last_tok[b] == eot) (0 at t = 0), then last_tok[b] =
+ * tokens[b]; t read from t_buf.  Launch before the step's tree layers. */
+DH_API int dh_decode_doc_step(const int64_t* tokens, const int64_t* t_buf, int* doc_hist,
+                       int64_t* last_tok, int64_t eot, int batch, int max_len, void* stream);
 
 /* t_buf[0] += 1 (decoding.py:443). */
 DH_API int dh_decode_advance(int64_t* t_buf, void* stream);
