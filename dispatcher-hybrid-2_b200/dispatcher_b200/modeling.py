@@ -99,6 +99,32 @@ class DispatcherHybridForCausalLM(nn.Module):
         self._engine = None
         self.load_state_dict(make_state_dict(config, seed, nondegenerate), strict=True)
 
+    # ------------------------------------------------------------ loading
+    @classmethod
+    def from_pretrained(cls, path, dtype=None, device=None):
+        """A released model directory: config.json + model.safetensors (or
+        sharded / pytorch_model.bin), the layout the reference's
+        save_pretrained and scripts/convert_checkpoint.py write."""
+        from .checkpoint import load_pretrained
+        cfg, sd = load_pretrained(path)
+        return cls._with_weights(cfg, sd, dtype, device)
+
+    @classmethod
+    def from_research_checkpoint(cls, path, dtype=None, device=None):
+        """A research training checkpoint, remapped as the reference's converter
+        does (scripts/convert_checkpoint.py:25-57)."""
+        from .checkpoint import load_research_checkpoint
+        cfg, sd = load_research_checkpoint(path)
+        return cls._with_weights(cfg, sd, dtype, device)
+
+    @classmethod
+    def _with_weights(cls, cfg, sd, dtype, device):
+        from .checkpoint import check_keys
+        model = check_keys(cls(cfg), sd)
+        if dtype is not None or device is not None:
+            model = model.to(device=device, dtype=dtype)
+        return model.eval()
+
     # ------------------------------------------------------------ reference API
     def enable_fused_gates(self, enabled=True):
         """modeling_dispatcher.py:365-377.  The B200 engine is the only compute
