@@ -160,8 +160,8 @@ class PrefillEngine:
                     mlen = cache.k.shape[1]
                     call("dh_copy_rows", _p(P[:, d:2 * d]), 3 * d, _p(cache.k), d, mlen * d, B, T, d, s)
                     call("dh_copy_rows", _p(P[:, 2 * d:]), 3 * d, _p(cache.v), d, mlen * d, B, T, d, s)
-                self._timed("attn", 0.0, "dh_window_attn_prefill", _p(P), 3 * d, _p(Vb), d, B, T,
-                            H, hd, cfg.attn_window, s)
+                self._timed("attn", 0.0, "dh_window_attn_prefill_tc", _p(P), 3 * d, _p(Vb), d, B,
+                            T, H, hd, cfg.attn_window, _p(self.status), s)
             self._gemm("out", Vb, lay["w_out"], x, epi=1, residual=x, s=s)
             call("dh_rmsnorm_bf16", _p(x), d, _p(lay["norm2"]), _p(h), d, M, d, s)
             self._gemm("gate_up", h, lay["w_gu"], U, epi=2, s=s)

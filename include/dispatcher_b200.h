@@ -232,6 +232,15 @@ DH_API int dh_copy_rows(const void* src, int ld_src, void* dst, int ld_dst,
 DH_API int dh_window_attn_prefill(const void* qkv, int ld, void* out, int ldo, int batch, int T,
                                   int H, int hd, int window, void* stream);
 
+/* dh_window_attn_prefill on the 5th-gen tensor cores: S = Q K^T and O += P V
+ * with tcgen05.mma (accumulators and P in tensor memory), online softmax in
+ * fp32 over blocks of 128 keys.  Same arguments and result; status
+ * (nullable) is set to DH_ERR_TIMEOUT if a bounded pipeline wait gave up.
+ * ldo % 8 == 0. */
+DH_API int dh_window_attn_prefill_tc(const void* qkv, int ld, void* out, int ldo, int batch,
+                                     int T, int H, int hd, int window, int* status,
+                                     void* stream);
+
 /* ------------------------------------------------- persistent decode step */
 
 /* Per-layer weights and caches of the whole-step decode kernel.  Weights

@@ -119,13 +119,18 @@ def test_gate_preacts_op_matches_reference_semantics():
         assert max_err(got.float().cpu(), want) < 0.02 * want.abs().max().item() + 1e-2, name
 
 
-@pytest.mark.parametrize("T,window", [(100, 64), (300, 64), (256, 1024), (1100, 1024), (64, 0)])
-def test_window_attention(T, window):
+@pytest.mark.parametrize("tensor_cores", [True, False])
+@pytest.mark.parametrize("T,window", [(100, 64), (300, 64), (256, 1024), (1100, 1024), (64, 0),
+                                      (1, 64), (129, 128)])
+def test_window_attention(T, window, tensor_cores):
     B, H, hd = 2, 4, 64
     d = H * hd
     g = torch.Generator().manual_seed(T)
     qkv = torch.randn(B * T, 3 * d, generator=g).bfloat16()
-    got = ops.window_attention(qkv.cuda().clone(), B, H, window).float().cpu()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    got = ops.window_attention(qkv.cuda().clone(), B, H, window, tensor_cores=tensor_cores,
+                               status=status).float().cpu()
+    assert int(status.item()) == 0
     q, k, v = qkv.float().view(B, T, 3, H, hd).permute(2, 0, 3, 1, 4)
     cos, sin = oracle.rope_tables(T, hd)
     q, k = oracle.apply_rope(q, cos, sin), oracle.apply_rope(k, cos, sin)
