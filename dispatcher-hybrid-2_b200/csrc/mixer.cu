@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
                 // bf16 arithmetic as in the reference: (A + m*B) rounded once, relu, squared
                 __nv_bfloat162 x = __hfma2(m2, b2[e], a2[e]);
                 x = __hmax2(x, z2);
-                b2[e] = __hmul2(x, x);
+                b2[e] = __hmul2_rn(x, x);
               }
               hv[4 * j] = bv.x;
               hv[4 * j + 1] = bv.y;
@@ -482,11 +482,17 @@ __global__ void __launch_bounds__(kGateThreads, 1)
 // reference's order and rounding (modeling_dispatcher.py:116-120, bf16):
 //   msg(t) = r(t) * V(t)                      published to shared memory
 //   V(t)   = f(t) * V(t) + a(t) * msg(t - s)
-// in bf16x2 arithmetic, one rounding per product and per sum.  Each thread
+// in bf16x2 arithmetic, one rounding per product and per sum (the _rn forms:
+// no multiply-add contraction, as in the reference's separate bf16 ops), so
+// the sweep is bit-exact against the reference's loop.  Each thread
 // needs only the gates of its own positions: one 8-byte load (admit, forget,
 // transmit, 0) per position.  Consecutive threads touch consecutive 16-byte
 // rows of the message buffer (no bank conflicts).  The next level's gates
-// are loaded while the current level is computed.
+// are loaded while the current level is computed.  The message buffer is
+// double buffered (levels alternate halves), so one barrier per level
+// suffices: a half is rewritten two levels later, after a barrier that every
+// reader of it has passed.  Shifts of 1024 and 2048 stay inside each thread
+// (its positions are 1024 apart): no shared memory and no barrier.
 constexpr int kScanThreads = 1024;  // 32 warps hide the per-level barrier latency
 constexpr int kScanPer = 4;        // positions per thread (T <= 4096)
 
@@ -545,6 +551,30 @@ __device__ __forceinline__ __nv_bfloat162 bcast_hi(uint32_t w) {
   return *reinterpret_cast<const __nv_bfloat162*>(&x);
 }
 
+// A level whose shift is K x 1024: t - s is this thread's own position i - K,
+// not yet updated at this level when i runs downwards.
+template <int K>
+__device__ __forceinline__ void scan_level_in_thread(ScanState& st, const LevelGates& cur, int T,
+                                                     int tid) {
+#pragma unroll
+  for (int i = kScanPer - 1; i >= 0; --i) {
+    const int t = tid + i * kScanThreads;
+    if (t >= T) continue;
+    const __nv_bfloat162 a2 = bcast_lo(cur.g[i].x), f2 = bcast_hi(cur.g[i].x);
+    __nv_bfloat162* v = reinterpret_cast<__nv_bfloat162*>(&st.V[i]);
+    if (i >= K) {
+      const __nv_bfloat162 r2 = bcast_lo(cur.g[i - K].y);
+      const __nv_bfloat162* vs = reinterpret_cast<const __nv_bfloat162*>(&st.V[i - K]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        v[e] = __hadd2_rn(__hmul2_rn(f2, v[e]), __hmul2_rn(a2, __hmul2_rn(r2, vs[e])));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = __hmul2_rn(f2, v[e]);
+    }
+  }
+}
+
 // one level of the sweep; loads the next level's gates into `nxt` first
 __device__ __forceinline__ void scan_level(const ScanArgs& a, ScanState& st, uint4* sx,
                                            const __nv_bfloat16* gbase, int b, int col, int tid,
@@ -552,6 +582,15 @@ __device__ __forceinline__ void scan_level(const ScanArgs& a, ScanState& st, uin
                                            LevelGates& nxt) {
   const int T = a.T, s = 1 << l;
   if (l + 1 < nl) load_level(gbase + (size_t)(l + 1) * 4 * T, T, tid, nxt);
+  if (s >= kScanThreads) {
+    const int k = s / kScanThreads;  // a power of two
+    if (k == 1) scan_level_in_thread<1>(st, cur, T, tid);
+    else if (k == 2) scan_level_in_thread<2>(st, cur, T, tid);
+    else scan_level_in_thread<kScanPer>(st, cur, T, tid);
+    if (a.ring && l + 1 < a.L) write_ring(a, st, b, col, tid, l + 1);
+    return;
+  }
+  sx += (l & 1) * T;  // this level's half of the message buffer
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
     const int t = tid + i * kScanThreads;
@@ -560,7 +599,7 @@ __device__ __forceinline__ void scan_level(const ScanArgs& a, ScanState& st, uin
       uint4 m = st.V[i];
       __nv_bfloat162* mv = reinterpret_cast<__nv_bfloat162*>(&m);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) mv[e] = __hmul2(r2, mv[e]);  // msg = r * V
+      for (int e = 0; e < 4; ++e) mv[e] = __hmul2_rn(r2, mv[e]);  // msg = r * V
       sx[t] = m;
     }
   }
@@ -575,18 +614,17 @@ __device__ __forceinline__ void scan_level(const ScanArgs& a, ScanState& st, uin
       uint4 m = sx[t - s];
       const __nv_bfloat162* mv = reinterpret_cast<const __nv_bfloat162*>(&m);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = __hadd2(__hmul2(f2, v[e]), __hmul2(a2, mv[e]));
+      for (int e = 0; e < 4; ++e) v[e] = __hadd2_rn(__hmul2_rn(f2, v[e]), __hmul2_rn(a2, mv[e]));
     } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = __hmul2(f2, v[e]);
+      for (int e = 0; e < 4; ++e) v[e] = __hmul2_rn(f2, v[e]);
     }
   }
   if (a.ring && l + 1 < a.L) write_ring(a, st, b, col, tid, l + 1);
-  __syncthreads();
 }
 
 __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
-  extern __shared__ uint4 sx[];  // [T] x 8 bf16
+  extern __shared__ uint4 sx[];  // 2 x [T] x 8 bf16
   const int slices = a.hd / 8;
   const int cc = blockIdx.x % slices;
   const int h = (blockIdx.x / slices) % a.H;
@@ -594,17 +632,29 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
   const int col = h * a.hd + cc * 8;
   const int tid = threadIdx.x;
   const int T = a.T;
+  const __nv_bfloat16* gbase = a.gates + (((size_t)b * a.H + h) * a.L) * 4 * (size_t)T;
+  int nl = a.n_lv;
+  while (nl > 0 && (1 << (nl - 1)) > T) --nl;   // the reference stops at shift > T
+  if (tid == 0 && nl > 0) {
+    // every level's gates of this (sequence, head) are one contiguous block:
+    // pull it into L2 now, so that the per-level loads (one level ahead) hit
+    // L2 instead of waiting on HBM.  Start rounded down, length rounded down
+    // to 16 bytes: the range stays inside the gates buffer.
+    const uintptr_t p0 = reinterpret_cast<uintptr_t>(gbase) & ~uintptr_t(15);
+    const uintptr_t p1 = (reinterpret_cast<uintptr_t>(gbase) + (size_t)nl * T * 8) & ~uintptr_t(15);
+    for (uintptr_t p = p0; p < p1; p += 65536)
+      prefetch_l2(reinterpret_cast<const void*>(p), p1 - p < 65536 ? (uint32_t)(p1 - p) : 65536u);
+  }
   ScanState st;
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
     const int t = tid + i * kScanThreads;
-    st.V[i] = t < T ? *reinterpret_cast<const uint4*>(a.v0 + ((size_t)b * T + t) * a.ld_v0 + col)
-                    : make_uint4(0, 0, 0, 0);
+    // unconditional load (positions past the end read the last one, never
+    // used): a select on the loaded value would stall here
+    st.V[i] = *reinterpret_cast<const uint4*>(a.v0 + ((size_t)b * T + min(t, T - 1)) * a.ld_v0 +
+                                              col);
   }
   if (a.ring) write_ring(a, st, b, col, tid, 0);
-  const __nv_bfloat16* gbase = a.gates + (((size_t)b * a.H + h) * a.L) * 4 * (size_t)T;
-  int nl = a.n_lv;
-  while (nl > 0 && (1 << (nl - 1)) > T) --nl;   // the reference stops at shift > T
   LevelGates g0, g1;
   if (nl > 0) load_level(gbase, T, tid, g0);
   for (int l = 0; l < nl; l += 2) {
@@ -735,9 +785,9 @@ extern "C" int dh_level_scan(const void* v0, int ld_v0, const void* gates, void*
   cudaGetDevice(&dev);
   if (configured_dev != dev) {
     cudaFuncSetAttribute(scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kScanThreads * kScanPer * 16);
+                         2 * kScanThreads * kScanPer * 16);
     configured_dev = dev;
   }
-  scan_kernel<<<blocks, kScanThreads, (size_t)T * 16, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  scan_kernel<<<blocks, kScanThreads, (size_t)T * 32, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return check_launch("scan_kernel");
 }

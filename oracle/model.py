@@ -92,14 +92,23 @@ def mixer_internals(sd, p, H, L, x, mask):
     admit = heads_first(pre[0]) * mbh                              # :111
     forget = heads_first(pre[1]) * mbh + (1.0 - mbh)               # :113
     transmit = heads_first(pre[2])                                 # :114
-    for li, shift in enumerate(shifts[:n_lv]):                     # :116-120
+    V = level_sweep(V, admit, forget, transmit, n_lv)
+    Vout = V.view(batch, H, length, hd).transpose(1, 2).reshape(batch, length, d)
+    return dict(V0=V0, A=A, B=B, pre_i=pre[0], pre_f=pre[1], pre_r=pre[2],
+                admit=admit, forget=forget, transmit=transmit, V=Vout, n_lv=n_lv)
+
+
+def level_sweep(V, admit, forget, transmit, n_lv):
+    """The level loop (:116-120): V (B*H, T, hd), gates (B*H, T, n_lv) after
+    masking; in V's dtype, so bf16 inputs round after every product and sum."""
+    length = V.shape[1]
+    for li in range(n_lv):
+        shift = 2 ** li
         if shift > length:
             break
         msg = torch.roll(transmit[..., li:li + 1] * V, shifts=shift, dims=1)
         V = forget[..., li:li + 1] * V + admit[..., li:li + 1] * msg
-    Vout = V.view(batch, H, length, hd).transpose(1, 2).reshape(batch, length, d)
-    return dict(V0=V0, A=A, B=B, pre_i=pre[0], pre_f=pre[1], pre_r=pre[2],
-                admit=admit, forget=forget, transmit=transmit, V=Vout, n_lv=n_lv)
+    return V
 
 
 def mixer_forward(sd, p, H, L, x, mask):

@@ -78,6 +78,30 @@ def test_gates_and_scan_small(T, eot):
     assert max_err(V.float().cpu(), ref["V"]) < bound
 
 
+@pytest.mark.parametrize("T", [1000, 1024, 1500, 2048, 2049, 3000, 4096])
+def test_level_scan_bit_exact_long(T):
+    """The sweep alone at lengths where shifts of 1024 and 2048 occur (levels
+    that stay inside a thread), against the oracle's level loop in bf16:
+    same rounding points, so bit-exact.  The gates carry the level mask (admit
+    0, forget 1 before the shift), as the gate kernel writes them."""
+    B, H, hd, L = 2, 2, 64, 12
+    d = H * hd
+    n_lv = oracle.n_levels(L, T)
+    g = torch.Generator().manual_seed(T)
+    v0 = torch.randn(B * T, d, generator=g).bfloat16()
+    gates = torch.rand(B, H, L, T, 4, generator=g).bfloat16()
+    gates[..., 3] = 0
+    lm = oracle.level_mask(T, L)                                # (T, L), 1 where t >= 2^l
+    gates[..., 0] *= lm.t().bfloat16()
+    gates[..., 1] = torch.where(lm.t().bool(), gates[..., 1], torch.ones_like(gates[..., 1]))
+    got = ops.level_scan(v0.cuda(), gates.cuda().contiguous(), H, L, n_lv, B).cpu()
+    V = v0.view(B, T, H, hd).transpose(1, 2).reshape(B * H, T, hd)
+    gl = gates[:, :, :n_lv].permute(0, 1, 3, 2, 4).reshape(B * H, T, n_lv, 4)
+    want = oracle.level_sweep(V, gl[..., 0], gl[..., 1], gl[..., 2], n_lv)
+    want = want.view(B, H, T, hd).transpose(1, 2).reshape(B * T, d)
+    assert torch.equal(got, want)
+
+
 @pytest.mark.parametrize("nondeg", [False, True])
 def test_mixer_configuration_1(golden, nondeg):
     """Configuration 1 (one tree layer at the default width, B=2, T=1024,
