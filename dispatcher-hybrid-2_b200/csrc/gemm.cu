@@ -2,7 +2,7 @@
 // (A: M x K bf16 row-major activations, W: N x K bf16 row-major weights, as
 // nn.Linear stores them), fp32 accumulation in tensor memory.
 //
-// Warp roles (192 threads, one CTA per SM):
+// Warp roles (224 threads, one CTA per SM):
 //   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a
 //               STAGES-deep shared-memory ring, completion on mbarriers
 //   warp 1      allocates 2 x BN TMEM columns; one thread issues
@@ -10,6 +10,11 @@
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator (each warp owns its
 //               32-lane TMEM quadrant), fused op, staged through shared
 //               memory for coalesced global stores
+//   warp 6      waits on the stage-full and accumulator-empty mbarriers and
+//               hands each ready k-block to warp 1 through a named barrier:
+//               an mbarrier wait in the issuing thread stalls the tensor
+//               pipe (measured on B200: one satisfied try_wait per four
+//               MMAs nearly triples their time), a named barrier does not
 // The accumulator is double-buffered in TMEM so the epilogue of tile i
 // overlaps the main loop of tile i+1.  Tiles are rasterised in bands of
 // `band` column blocks so a band's weight slice stays resident in L2 while
@@ -23,6 +28,23 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kEpiWarps = 4;
+constexpr int kGemmThreads = 224;
+constexpr int kHandoffBar = 1;  // named barrier between the MMA warp and the waiter warp
+
+// Named barrier of the MMA and waiter warps that also ANDs a flag across
+// them (all 64 threads execute it, once per k-block, in lockstep).
+__device__ __forceinline__ bool handoff(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 64, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok), "n"(kHandoffBar)
+      : "memory");
+  return r != 0;
+}
 constexpr int kStgRow = 80;  // staging row pitch in bytes (64 B of data + pad)
 
 enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2 };
@@ -137,7 +159,7 @@ __device__ __forceinline__ void stage_and_store(const float (&v)[32], uint8_t* s
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                 GemmArgs g) {
   using C = Cfg<BN>;
@@ -209,19 +231,16 @@ __global__ void __launch_bounds__(192, 1)
         if (n_s > 0) mbar_wait(&full[s], (uint32_t)((n_s - 1) & 1), nullptr, 1u << 20);
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(BM, BN);
-      int stage = 0, acc = 0;
-      uint32_t phase = 0, acc_phase = 0;
-      bool okk = true;
-      for (int tile = blockIdx.x; tile < num_tiles && okk; tile += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, g.err)) break;
+  } else if (warp == 1) {  // ---------------- MMA issue (no mbarrier waits here)
+    constexpr uint32_t idesc = idesc_bf16(BM, BN);
+    int stage = 0, acc = 0;
+    bool okk = true;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        okk = handoff(okk);  // the waiter saw this stage full (and, at kb 0, the accumulator free)
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, g.err)) { okk = false; break; }
-          tc_fence_after();
+        if (okk && lane == 0) {
           const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
           const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
@@ -229,14 +248,30 @@ __global__ void __launch_bounds__(192, 1)
             umma_bf16(d_tmem, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), idesc,
                       (kb | k) != 0);
           umma_commit(&empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (kb == kblocks - 1) umma_commit(&tfull[acc]);
         }
-        umma_commit(&tfull[acc]);
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1;
+        __syncwarp();
+        if (++stage == STAGES) stage = 0;
       }
+      acc ^= 1;
     }
-  } else {
+  } else if (warp == 6) {  // ---------------- waiter: mbarrier waits for the MMA warp
+    int stage = 0, acc = 0;
+    uint32_t phase = 0, acc_phase = 0;
+    bool okk = true;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int kb = 0; kb < kblocks; ++kb) {
+        // after a failed (bounded) wait, skip every later wait but keep the
+        // handoffs, so the two warps stay in lockstep and nothing blocks
+        if (kb == 0) okk = okk && mbar_wait(&tempty[acc], acc_phase ^ 1, g.err);
+        okk = okk && mbar_wait(&full[stage], phase, g.err);
+        okk = handoff(okk);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  } else {  // ---------------- epilogue warps 2..5
     const int q = warp & 3;
     uint8_t* stg = sStg + (warp - 2) * 32 * kStgRow;
     int acc = 0;
@@ -315,7 +350,7 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, GemmArgs g, cuda
   const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
   int grid = sm_count();
   if (grid > tiles) grid = tiles;
-  gemm_kernel<BN><<<grid, 192, Cfg<BN>::SMEM, st>>>(ta, tb, g);
+  gemm_kernel<BN><<<grid, kGemmThreads, Cfg<BN>::SMEM, st>>>(ta, tb, g);
   return check_launch("gemm_kernel");
 }
 

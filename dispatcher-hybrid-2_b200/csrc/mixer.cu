@@ -4,9 +4,9 @@
 // Gate readout (replaces fused_gates.py:38-93 and the einsums of
 // modeling_dispatcher.py:100-109).  One CTA owns 128 positions of one
 // sequence.  For every 64-wide slice k of the gate-hidden width and every
-// level l, four builder warps form the hidden tile
+// level l, a group of four builder warps forms the hidden tile
 //      H[t, k] = relu(A[t, k] + m(t, l) * B[t - 2^l, k])^2          (bf16)
-// directly in shared memory in the tcgen05 operand layout, and one thread
+// directly in tensor memory (two groups take alternate tiles), and one thread
 // issues tcgen05.mma H x W_l^T into a per-level fp32 accumulator in TMEM
 // (W_l: the 3H gate rows of level l, padded to NP rows).  The (T, L, gh)
 // hidden tensor never exists in HBM.  Shifted B rows come straight from TMA:
@@ -100,7 +100,27 @@ constexpr int kABStages = 2;                  // A + B-region stages
 constexpr int kABBytes = 3 * kSBytes;         // A tile + 32 KB B region (window or two tiles)
 constexpr int kWLevels = 4;                   // levels of W per copy
 constexpr int kBuilderWarps = 8;              // 2 threads per tile row
-constexpr int kGateThreads = 64 + kBuilderWarps * 32;
+constexpr int kGateWaiterWarp = 2 + kBuilderWarps;  // mbarrier waits for the MMA warp
+constexpr int kGateThreads = 64 + kBuilderWarps * 32 + 32;
+constexpr int kGateHandoffBar = 4;                    // named barrier: MMA warp + waiter warp
+
+// Named barrier of the MMA and waiter warps that also ANDs a flag across them
+// (all 64 threads, once per hidden tile, in lockstep).  The MMA warp never
+// waits on an mbarrier itself: on B200 an mbarrier wait in the issuing thread
+// stalls the tensor pipe (a satisfied try_wait per four MMAs nearly triples
+// their time), a named barrier does not.
+__device__ __forceinline__ bool gate_handoff(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 64, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok), "n"(kGateHandoffBar)
+      : "memory");
+  return r != 0;
+}
 constexpr int kHBufs = 4;                     // hidden tiles in flight (TMEM)
 constexpr int kHCols = kSlice / 2;            // TMEM columns of one hidden tile (2 bf16 each)
 constexpr int kHCol0 = 512 - kHBufs * kHCols; // first hidden-tile column
@@ -191,7 +211,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
       mbar_init(&w_empty[i], 1);
     }
     for (int i = 0; i < kHBufs; ++i) {
-      mbar_init(&h_full[i], kBuilderWarps);
+      mbar_init(&h_full[i], kBuilderWarps / 2);  // one builder group per tile
       mbar_init(&h_empty[i], 1);
     }
     mbar_init(d_full, 1);
@@ -264,21 +284,19 @@ __global__ void __launch_bounds__(kGateThreads, 1)
         if (n > 0) mbar_wait(&w_full[i], (uint32_t)((n - 1) & 1), nullptr, 1u << 20);
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {  // ---------------- MMA issuer
-      const uint32_t idesc = idesc_bf16(kTileT, g.NP);
-      int ws = 0, hs = 0;
-      uint32_t wph = 0, hph = 0;
-      bool ok = true;
-      for (int grp = 0; grp < ngroups && ok; ++grp) {
-        int l0, l1;
-        gate_group(grp, g.n_calc, g.NP, l0, l1);
-        for (int kc = 0; kc < nk && ok; ++kc) {
-          for (int l = l0; l < l1; ++l) {
-            const int c0 = l0 + ((l - l0) / kWLevels) * kWLevels;
-            if (l == c0 && !mbar_wait(&w_full[ws], wph, g.err)) { ok = false; break; }
-            if (!mbar_wait(&h_full[hs], hph, g.err)) { ok = false; break; }
-            tc_fence_after();
+  } else if (warp == 1) {  // ---------------- MMA issue (no mbarrier waits here)
+    const uint32_t idesc = idesc_bf16(kTileT, g.NP);
+    int ws = 0, hs = 0;
+    bool ok = true;
+    for (int grp = 0; grp < ngroups; ++grp) {
+      int l0, l1;
+      gate_group(grp, g.n_calc, g.NP, l0, l1);
+      for (int kc = 0; kc < nk; ++kc) {
+        for (int l = l0; l < l1; ++l) {
+          const int c0 = l0 + ((l - l0) / kWLevels) * kWLevels;
+          ok = gate_handoff(ok);  // the waiter saw this tile built (and its W copy landed)
+          tc_fence_after();
+          if (ok && lane == 0) {
             const uint32_t hA = tmem_base + (uint32_t)(kHCol0 + hs * kHCols);
             const uint32_t wB = smem_u32(sW + ws * wbytes + (l - c0) * g.NP * 128);
             const uint32_t d = tmem_base + (uint32_t)((l - l0) * g.NP);
@@ -286,19 +304,43 @@ __global__ void __launch_bounds__(kGateThreads, 1)
             for (int k = 0; k < kSlice / 16; ++k)  // 16 bf16 of K = 8 TMEM columns
               umma_bf16_ts(d, hA + k * 8, sw128_desc(wB + k * 32), idesc, (kc | k) != 0);
             umma_commit(&h_empty[hs]);
-            if (++hs == kHBufs) { hs = 0; hph ^= 1; }
-            if (l + 1 == l1 || l + 1 == c0 + kWLevels) {  // last level of this W copy
-              umma_commit(&w_empty[ws]);
-              if (++ws == g.nws) { ws = 0; wph ^= 1; }
-            }
+          }
+          if (++hs == kHBufs) hs = 0;
+          if (l + 1 == l1 || l + 1 == c0 + kWLevels) {  // last level of this W copy
+            if (ok && lane == 0) umma_commit(&w_empty[ws]);
+            if (++ws == g.nws) ws = 0;
+          }
+          __syncwarp();
+        }
+      }
+      if (ok && lane == 0) umma_commit(d_full);
+      __syncwarp();
+    }
+  } else if (warp == kGateWaiterWarp) {  // ---------------- waiter for the MMA warp
+    int ws = 0, hs = 0;
+    uint32_t wph = 0, hph = 0;
+    bool ok = true;
+    for (int grp = 0; grp < ngroups; ++grp) {
+      int l0, l1;
+      gate_group(grp, g.n_calc, g.NP, l0, l1);
+      for (int kc = 0; kc < nk; ++kc) {
+        for (int l = l0; l < l1; ++l) {
+          const int c0 = l0 + ((l - l0) / kWLevels) * kWLevels;
+          // after a failed (bounded) wait, skip every later wait but keep the
+          // handoffs, so the two warps stay in lockstep and nothing blocks
+          if (l == c0) ok = ok && mbar_wait(&w_full[ws], wph, g.err);
+          ok = ok && mbar_wait(&h_full[hs], hph, g.err);
+          ok = gate_handoff(ok);
+          if (++hs == kHBufs) { hs = 0; hph ^= 1; }
+          if (l + 1 == l1 || l + 1 == c0 + kWLevels) {
+            if (++ws == g.nws) { ws = 0; wph ^= 1; }
           }
         }
-        if (ok) umma_commit(d_full);
       }
     }
   } else {  // ---------------- builders + epilogue (warps 2..9)
     const int q = warp & 3;               // TMEM lane quadrant of this warp
-    const int half = (warp - 2) >> 2;     // which 32 columns of a slice / which levels
+    const int half = (warp - 2) >> 2;     // builder group: alternate hidden tiles / epilogue levels
     const int r = q * 32 + lane;          // tile row == TMEM lane
     const int t = t0 + r;
     const bool row_ok = t < g.T;
@@ -309,13 +351,12 @@ __global__ void __launch_bounds__(kGateThreads, 1)
       if (g.mask) m = row_ok && g.mask[((size_t)b * g.T + t) * g.mask_L + l] != 0;
       mbits |= (m ? 1u : 0u) << l;
     }
-    int abs_ = 0, hs = 0;
+    int abs_ = 0, hs = 0, jt = 0;  // jt: hidden tiles so far (same count in every thread)
     uint32_t abph = 0, hph = 0, dph = 0;
     // A failed (bounded) wait clears `ok`; the thread then skips every
     // further wait but still walks the same loops, so each named barrier
     // below is reached by all builder threads and nothing can hang.
     bool ok = true;
-    const int coff = half * 4;  // first of this thread's four 16-byte chunks
     for (int grp = 0; grp < ngroups; ++grp) {
       int l0, l1;
       gate_group(grp, g.n_calc, g.NP, l0, l1);
@@ -324,49 +365,53 @@ __global__ void __launch_bounds__(kGateThreads, 1)
         for (int i = 0; i < nab; ++i) {
           ok = ok && mbar_wait(&ab_full[abs_], abph, g.err);
           const uint8_t* st = sAB + abs_ * kABBytes;
-          uint4 av[4];
+          uint4 av[8];  // this row of the A slice (64 columns)
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            av[j] = *reinterpret_cast<const uint4*>(st + r * 128 + (((coff + j) ^ (r & 7)) << 4));
+          for (int j = 0; j < 8; ++j)
+            av[j] = *reinterpret_cast<const uint4*>(st + r * 128 + ((j ^ (r & 7)) << 4));
           int a0, a1;
           gate_ab_levels(grp, i, l0, l1, a0, a1);
-          for (int l = a0; l < a1; ++l) {
-            ok = ok && mbar_wait(&h_empty[hs], hph ^ 1, g.err);
-            tc_fence_after();
-            // source row t - 2^l: row r + 128 - 2^l of the window (group 0) or
-            // row r of the level's own tile (group 1); rows before position 0
-            // arrive as TMA zeros, which is the wrap mask
-            const int bi = grp == 0 ? r + kTileT - (1 << l) : r;
-            const uint8_t* brow =
-                st + (grp == 0 ? kSBytes : (1 + l - a0) * kSBytes) + bi * 128;
-            // masked rows drop the shifted source
-            const float mf = g.mask ? (float)((mbits >> l) & 1u) : 1.f;
-            const __nv_bfloat162 m2 = __floats2bfloat162_rn(mf, mf);
-            const __nv_bfloat162 z2 = __floats2bfloat162_rn(0.f, 0.f);
-            uint32_t hv[16];  // this thread's 32 hidden values, two per TMEM column
+          for (int l = a0; l < a1; ++l, ++jt) {
+            // the two builder groups (warps 2-5, 6-9) take alternate tiles, so
+            // two tiles are in flight; each thread builds one whole row
+            if ((jt & 1) == half) {
+              ok = ok && mbar_wait(&h_empty[hs], hph ^ 1, g.err);
+              tc_fence_after();
+              // source row t - 2^l: row r + 128 - 2^l of the window (group 0) or
+              // row r of the level's own tile (group 1); rows before position 0
+              // arrive as TMA zeros, which is the wrap mask
+              const int bi = grp == 0 ? r + kTileT - (1 << l) : r;
+              const uint8_t* brow =
+                  st + (grp == 0 ? kSBytes : (1 + l - a0) * kSBytes) + bi * 128;
+              // masked rows drop the shifted source
+              const float mf = g.mask ? (float)((mbits >> l) & 1u) : 1.f;
+              const __nv_bfloat162 m2 = __floats2bfloat162_rn(mf, mf);
+              const __nv_bfloat162 z2 = __floats2bfloat162_rn(0.f, 0.f);
+              uint32_t hv[32];  // this row's 64 hidden values, two per TMEM column
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 bv = *reinterpret_cast<const uint4*>(brow + (((coff + j) ^ (bi & 7)) << 4));
-              const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&av[j]);
-              __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&bv);
+              for (int j = 0; j < 8; ++j) {
+                uint4 bv = *reinterpret_cast<const uint4*>(brow + ((j ^ (bi & 7)) << 4));
+                const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&av[j]);
+                __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&bv);
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                // bf16 arithmetic as in the reference: (A + m*B) rounded once, relu, squared
-                __nv_bfloat162 x = __hfma2(m2, b2[e], a2[e]);
-                x = __hmax2(x, z2);
-                b2[e] = __hmul2_rn(x, x);
+                for (int e = 0; e < 4; ++e) {
+                  // bf16 arithmetic as in the reference: (A + m*B) rounded once, relu, squared
+                  __nv_bfloat162 x = __hfma2(m2, b2[e], a2[e]);
+                  x = __hmax2(x, z2);
+                  b2[e] = __hmul2_rn(x, x);
+                }
+                hv[4 * j] = bv.x;
+                hv[4 * j + 1] = bv.y;
+                hv[4 * j + 2] = bv.z;
+                hv[4 * j + 3] = bv.w;
               }
-              hv[4 * j] = bv.x;
-              hv[4 * j + 1] = bv.y;
-              hv[4 * j + 2] = bv.z;
-              hv[4 * j + 3] = bv.w;
+              tmem_st32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(kHCol0 + hs * kHCols),
+                        hv);
+              tmem_st_wait();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&h_full[hs]);
             }
-            tmem_st16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(kHCol0 + hs * kHCols + half * 16),
-                      hv);
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&h_full[hs]);
             if (++hs == kHBufs) { hs = 0; hph ^= 1; }
           }
           __syncwarp();
@@ -635,16 +680,6 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
   const __nv_bfloat16* gbase = a.gates + (((size_t)b * a.H + h) * a.L) * 4 * (size_t)T;
   int nl = a.n_lv;
   while (nl > 0 && (1 << (nl - 1)) > T) --nl;   // the reference stops at shift > T
-  if (tid == 0 && nl > 0) {
-    // every level's gates of this (sequence, head) are one contiguous block:
-    // pull it into L2 now, so that the per-level loads (one level ahead) hit
-    // L2 instead of waiting on HBM.  Start rounded down, length rounded down
-    // to 16 bytes: the range stays inside the gates buffer.
-    const uintptr_t p0 = reinterpret_cast<uintptr_t>(gbase) & ~uintptr_t(15);
-    const uintptr_t p1 = (reinterpret_cast<uintptr_t>(gbase) + (size_t)nl * T * 8) & ~uintptr_t(15);
-    for (uintptr_t p = p0; p < p1; p += 65536)
-      prefetch_l2(reinterpret_cast<const void*>(p), p1 - p < 65536 ? (uint32_t)(p1 - p) : 65536u);
-  }
   ScanState st;
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {

@@ -94,7 +94,10 @@ def test_caches_and_ring_slots_match_oracle(small_nd):
     for i, (rc, mc) in enumerate(zip(ref.caches, dec.caches)):
         if hasattr(rc, "V_ring"):
             r_ring, m_ring = rc.V_ring, mc.V_ring.float().cpu()
-            assert torch.equal(r_ring != 0, m_ring != 0), f"layer {i}: ring slot pattern differs"
+            # written slots (rows), not elements: a bf16 f*V + a*msg can cancel
+            # to exactly zero in one channel where the fp32 oracle does not
+            assert torch.equal(r_ring.abs().sum(-1) != 0, m_ring.abs().sum(-1) != 0), \
+                f"layer {i}: ring slot pattern differs"
             assert max_err(m_ring, r_ring) < 0.05 * r_ring.abs().max().item() + 1e-2
             assert max_err(mc.B_hist[:, :T].float().cpu(), rc.B_hist[:, :T]) < 0.02 * rc.B_hist.abs().max().item() + 1e-3
             assert max_err(mc.rg_hist[:, :T].float().cpu(), rc.rg_hist[:, :T]) < 0.02
