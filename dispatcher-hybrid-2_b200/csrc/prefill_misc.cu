@@ -9,27 +9,56 @@ namespace {
 constexpr float kEps = 1.1920928955078125e-07f;  // torch RMSNorm eps=None in fp32
 
 // one warp per row; d % 256 == 0 handled with a strided loop of 16-byte chunks
+// One warp per row.  CHUNKS > 0: the row is CHUNKS x 256 elements and stays
+// in registers (all its loads in flight at once, read once); CHUNKS == 0: any
+// D that is a multiple of 8, two passes.  Same summation order either way.
+template <int CHUNKS>
 __global__ void rmsnorm_kernel(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w,
                                __nv_bfloat16* y, int ldy, int M, int D) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= M) return;
   const __nv_bfloat16* xr = x + (size_t)warp * ldx;
   float ss = 0.f;
-  for (int c = lane * 8; c < D; c += 256) {
-    float f[8];
-    unpack8(*reinterpret_cast<const uint4*>(xr + c), f);
+  if constexpr (CHUNKS > 0) {
+    uint4 xv[CHUNKS];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
-  }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)D + kEps);
-  for (int c = lane * 8; c < D; c += 256) {
-    float f[8], g[8];
-    unpack8(*reinterpret_cast<const uint4*>(xr + c), f);
-    unpack8(*reinterpret_cast<const uint4*>(w + c), g);
+    for (int i = 0; i < CHUNKS; ++i) xv[i] = *reinterpret_cast<const uint4*>(xr + i * 256 + lane * 8);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) f[e] = f[e] * r * g[e];
-    *reinterpret_cast<uint4*>(y + (size_t)warp * ldy + c) = pack8(f);
+    for (int i = 0; i < CHUNKS; ++i) {
+      float f[8];
+      unpack8(xv[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)D + kEps);
+#pragma unroll
+    for (int i = 0; i < CHUNKS; ++i) {
+      const int c = i * 256 + lane * 8;
+      float f[8], g[8];
+      unpack8(xv[i], f);
+      unpack8(*reinterpret_cast<const uint4*>(w + c), g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = f[e] * r * g[e];
+      *reinterpret_cast<uint4*>(y + (size_t)warp * ldy + c) = pack8(f);
+    }
+  } else {
+    for (int c = lane * 8; c < D; c += 256) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(xr + c), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)D + kEps);
+    for (int c = lane * 8; c < D; c += 256) {
+      float f[8], g[8];
+      unpack8(*reinterpret_cast<const uint4*>(xr + c), f);
+      unpack8(*reinterpret_cast<const uint4*>(w + c), g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = f[e] * r * g[e];
+      *reinterpret_cast<uint4*>(y + (size_t)warp * ldy + c) = pack8(f);
+    }
   }
 }
 
@@ -94,9 +123,17 @@ extern "C" int dh_rmsnorm_bf16(const void* x, int ldx, const void* w, void* y, i
   DH_REQUIRE(D % 8 == 0 && ldx % 8 == 0 && ldy % 8 == 0 && M > 0, DH_ERR_SHAPE,
              "dh_rmsnorm_bf16: bad sizes");
   const int threads = 256, rows_per_block = threads / 32;
-  rmsnorm_kernel<<<(M + rows_per_block - 1) / rows_per_block, threads, 0, STREAM(stream)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x), ldx, reinterpret_cast<const __nv_bfloat16*>(w),
-      reinterpret_cast<__nv_bfloat16*>(y), ldy, M, D);
+  const dim3 grid((M + rows_per_block - 1) / rows_per_block);
+  const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x);
+  const auto* wp = reinterpret_cast<const __nv_bfloat16*>(w);
+  auto* yp = reinterpret_cast<__nv_bfloat16*>(y);
+  switch (D % 256 == 0 ? D / 256 : 0) {
+    case 1: rmsnorm_kernel<1><<<grid, threads, 0, STREAM(stream)>>>(xp, ldx, wp, yp, ldy, M, D); break;
+    case 2: rmsnorm_kernel<2><<<grid, threads, 0, STREAM(stream)>>>(xp, ldx, wp, yp, ldy, M, D); break;
+    case 3: rmsnorm_kernel<3><<<grid, threads, 0, STREAM(stream)>>>(xp, ldx, wp, yp, ldy, M, D); break;
+    case 4: rmsnorm_kernel<4><<<grid, threads, 0, STREAM(stream)>>>(xp, ldx, wp, yp, ldy, M, D); break;
+    default: rmsnorm_kernel<0><<<grid, threads, 0, STREAM(stream)>>>(xp, ldx, wp, yp, ldy, M, D);
+  }
   return check_launch("rmsnorm_kernel");
 }
 
