@@ -249,6 +249,49 @@ def run_decode(model, cfg, batch, ctx, steps, warmup, seed, world):
     return ms, steps, dec.persistent
 
 
+def run_gate_backward(cfg, steps, warmup):
+    """The gate readout's backward (dh_gate_preacts_bwd, the reference op
+    gate_preacts_bwd) at one tree layer of the prefill workload: 8 x 4096
+    positions, all levels, synthetic bf16 inputs resident in HBM, fp32
+    gradient buffers allocated once (the kernel adds into them)."""
+    import ctypes
+    from dispatcher_b200 import ops
+    from dispatcher_b200._lib import call
+    b, T, gh, H, L = PREFILL_B, PREFILL_T, cfg.d_model, cfg.num_heads, cfg.levels
+    n_lv = min(L, T.bit_length())
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = (torch.randn(b, T, gh, device="cuda", generator=g) * 0.5).bfloat16()
+    B = (torch.randn(b, T, gh, device="cuda", generator=g) * 0.5).bfloat16()
+    W = [(torch.randn(L, H, gh, device="cuda", generator=g) * 0.05).bfloat16() for _ in range(3)]
+    dP = [torch.randn(b, T, n_lv, H, device="cuda", generator=g).bfloat16() for _ in range(3)]
+    wt = ops.pack_gate_weights_t(*W, n_lv)
+    outs = [torch.zeros(b, T, gh, device="cuda") for _ in range(2)]
+    outs += [torch.zeros(n_lv, H, gh, device="cuda") for _ in range(3)]
+    outs += [torch.zeros(n_lv, H, device="cuda") for _ in range(3)]
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def launch():
+        call("dh_gate_preacts_bwd", p(A), gh, p(B), gh, p(wt), None, n_lv, b, T, H, n_lv, gh,
+             *(p(x) for x in dP), *(p(x) for x in outs), p(st), stream)
+
+    for _ in range(warmup):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    if int(st.item()) != 0:
+        raise RuntimeError("gate backward: bounded wait timed out")
+    ms = e0.elapsed_time(e1) / steps
+    flops = 4.0 * 3 * H * gh * n_lv * b * T   # dh = dP W and dW = dP^T h, 2 flop per MAC
+    return ms, flops
+
+
 def prefill_config(world):
     return {"workload": "configs[1]: parallel-forward prefill, 8 x 4096 tokens per GPU, "
                         "uniform ids (EOT kept, doc-reset mask live)",
@@ -379,6 +422,9 @@ def main():
     flat[str(DECODE_CTX)] = round(dec_lines["b1"]["ms_per_step"], 4)
     dec_lines["b1_ms_per_step_by_ctx"] = flat
 
+    gb_ms, gb_flops = run_gate_backward(cfg, 5, args.warmup)
+    gb_tf = gb_flops / (gb_ms * 1e-3) / 1e12
+
     line = {
         "metric": METRIC, "value": world * tokens * 1000.0 / ms, "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -394,6 +440,11 @@ def main():
                      "algorithmic_flops_per_token": flop_tok},
         "per_op_ms_per_step": {k: round(v[1] / args.steps, 3) for k, v in per_op.items()},
         "decode": dec_lines,
+        "gate_backward": {
+            "what": "dh_gate_preacts_bwd, one tree layer of the prefill workload (8 x 4096, "
+                    "12 levels): dA, dB, dW, db", "ms_per_call": gb_ms,
+            "roofline": {"bound": "tensor", "achieved": gb_tf, "peak": peak_t, "unit": "TFLOP/s",
+                         "frac": gb_tf / peak_t, "algorithmic_flops": gb_flops}},
         "clocks": clk,
         "e2e": {"value": e2e_v, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},

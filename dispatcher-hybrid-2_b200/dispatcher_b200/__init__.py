@@ -16,5 +16,6 @@ from .config import DispatcherConfig, small_config  # noqa: F401
 from .weights import make_state_dict  # noqa: F401
 from .modeling import DispatcherHybridForCausalLM  # noqa: F401
 from .decoding import FusedGraphedHybridDecoder, GraphedHybridDecoder  # noqa: F401
+from .fused_gates import fused_gate_preacts  # noqa: F401
 
 __version__ = "0.1.0"

@@ -127,6 +127,44 @@ def gate_preacts_fwd(A, B, Wi, Wf, Wr, bi, bf, br, n_lv, mask=None):
     return outs[0], outs[1], outs[2]
 
 
+def pack_gate_weights_t(wi, wf, wr, n_lv):
+    """(L, H, gh) x 3 -> bf16 (n_lv*gh, 64): per level W^T with the 3H gate
+    rows (i, f, r) as columns, zero padded to 64 (the backward's K-major
+    operand)."""
+    H, gh = wi.shape[1], wi.shape[2]
+    w = torch.cat([wi[:n_lv], wf[:n_lv], wr[:n_lv]], dim=1).to(torch.bfloat16)  # (n_lv, 3H, gh)
+    wt = torch.zeros(n_lv, gh, 64, device=wi.device, dtype=torch.bfloat16)
+    wt[:, :, :3 * H] = w.transpose(1, 2)
+    return wt.reshape(n_lv * gh, 64).contiguous()
+
+
+def gate_preacts_bwd(A, B, Wi, Wf, Wr, dPi, dPf, dPr, n_lv, mask=None, status=None):
+    """Drop-in for the reference's backward op (fused_gates.py:225-263): the
+    gradients of gate_preacts_fwd given dPi, dPf, dPr (b, T, n_lv, H).
+    Returns [dA, dB, dWi, dWf, dWr, dbi, dbf, dbr], fp32: dA, dB (b, T, gh),
+    dW_x (n_lv, H, gh), db_x (n_lv, H)."""
+    b_, T, gh = A.shape
+    H = Wi.shape[1]
+    dev = A.device
+    A2 = A.to(torch.bfloat16).contiguous()
+    B2 = B.to(torch.bfloat16).contiguous()
+    wt = pack_gate_weights_t(Wi, Wf, Wr, n_lv)
+    dps = [d.to(torch.bfloat16).contiguous() for d in (dPi, dPf, dPr)]
+    dps = [d if d.data_ptr() % 16 == 0 else d.clone() for d in dps]  # 16-byte row loads
+    m8 = None
+    if mask is not None:
+        m8 = (mask[..., :n_lv] != 0).to(torch.uint8).contiguous()
+    f32 = torch.float32
+    dA = torch.zeros(b_, T, gh, device=dev, dtype=f32)
+    dB = torch.zeros(b_, T, gh, device=dev, dtype=f32)
+    dW = [torch.zeros(n_lv, H, gh, device=dev, dtype=f32) for _ in range(3)]
+    db = [torch.zeros(n_lv, H, device=dev, dtype=f32) for _ in range(3)]
+    _lib.call("dh_gate_preacts_bwd", _p(A2), gh, _p(B2), gh, _p(wt), _p(m8), n_lv, b_, T, H,
+              n_lv, gh, _p(dps[0]), _p(dps[1]), _p(dps[2]), _p(dA), _p(dB), _p(dW[0]),
+              _p(dW[1]), _p(dW[2]), _p(db[0]), _p(db[1]), _p(db[2]), _p(status), _stream())
+    return [dA, dB, *dW, *db]
+
+
 def level_scan(v0, gates, H, L, n_lv, batch, out=None, ring=None):
     """Level sweep over v0 rows (batch*T, d) -> V (batch*T, d) bf16."""
     _check(v0, "v0")

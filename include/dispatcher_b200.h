@@ -192,6 +192,25 @@ DH_API int dh_gate_preacts_fwd(const void* a, int lda, const void* bsrc, int ldb
                                int T, int H, int L, int NP, int gh, int n_lv, void* pre_i,
                                void* pre_f, void* pre_r, int* status, void* stream);
 
+/* Backward of dh_gate_preacts_fwd: the reference custom op
+ * dispatcher::gate_preacts_bwd (fused_gates.py:96-173, 225-263).  Given
+ * dpi/dpf/dpr bf16 (batch, T, n_lv, H), adds into caller-zeroed fp32 outputs
+ *   dA, dB (batch, T, gh):  dx = 2 relu(x) (dP . W_l), x = A + m*B(t-2^l);
+ *                           dA(t) += dx, dB(t - 2^l) += m dx
+ *   dWi/dWf/dWr (n_lv, H, gh) += dP^T . relu(x)^2;  dbi/dbf/dbr (n_lv, H) += sum_t dP
+ * (dA is written, not accumulated).  a, bsrc bf16 (batch, T, gh) with row
+ * strides lda, ldb; wt bf16 (n_lv*gh, 64): per level W^T with the 3H gate
+ * rows (i | f | r) as columns, zero padded; mask uint8 (batch, T, mask_L) or
+ * NULL (the wrap mask is always applied).  gh % 64 == 0, 3H <= 48,
+ * n_lv <= 16.  status (nullable) is set to DH_ERR_TIMEOUT if a bounded
+ * pipeline wait gave up. */
+DH_API int dh_gate_preacts_bwd(const void* a, int lda, const void* bsrc, int ldb, const void* wt,
+                               const uint8_t* mask, int mask_L, int batch, int T, int H,
+                               int n_lv, int gh, const void* dpi, const void* dpf,
+                               const void* dpr, float* dA, float* dB, float* dWi, float* dWf,
+                               float* dWr, float* dbi, float* dbf, float* dbr, int* status,
+                               void* stream);
+
 /* Dyadic level sweep (modeling_dispatcher.py:116-120): for l < n_lv,
  * V(t) <- f_l(t) V(t) + a_l(t) msg(t-2^l), msg = r_l V, in bf16 with the
  * reference's rounding points.  v0 bf16 (batch*T, hd*H)

@@ -18,7 +18,7 @@ them before any kernel is compared with it.
 """
 
 from .model import (level_mask, tree_mask, rmsnorm, mixer_forward,  # noqa: F401
-                    mixer_internals, level_sweep, rope_tables, apply_rope,
+                    mixer_internals, level_sweep, gate_preacts, rope_tables, apply_rope,
                     window_attention, swiglu, forward, n_levels)
 from .decoder import OracleDecoder, RING_OFFSETS, ring_slot  # noqa: F401
 from .generate import fast_generate  # noqa: F401

@@ -98,6 +98,23 @@ def mixer_internals(sd, p, H, L, x, mask):
                 admit=admit, forget=forget, transmit=transmit, V=Vout, n_lv=n_lv)
 
 
+def gate_preacts(A, B, Wi, Wf, Wr, bi, bf, br, n_lv, mask=None):
+    """The reference op's math (fused_gates.py:307-314, the einsums of
+    modeling_dispatcher.py:100-109): A, B (b, T, gh) -> pre_i, pre_f, pre_r
+    (b, T, n_lv, H) = W_x[l] . relu(A + m * roll(B, 2^l))^2 + b_x, m the wrap
+    mask times the optional (b, T, n_lv) doc mask.  Differentiable (plain
+    torch ops), the autograd oracle of the backward op."""
+    b, T, gh = A.shape
+    wrap = level_mask(T, n_lv, dtype=A.dtype)                 # (T, n_lv)
+    m = wrap.unsqueeze(0).expand(b, T, n_lv)
+    if mask is not None:
+        m = m * mask[..., :n_lv].to(A.dtype)
+    rolled = torch.stack([torch.roll(B, shifts=2 ** l, dims=1) for l in range(n_lv)], dim=2)
+    hidden = F.relu(A.unsqueeze(2) + rolled * m.unsqueeze(-1)) ** 2     # (b, T, n_lv, gh)
+    return tuple(torch.einsum("btld,lhd->btlh", hidden, w[:n_lv]) + bb[:n_lv]
+                 for w, bb in ((Wi, bi), (Wf, bf), (Wr, br)))
+
+
 def level_sweep(V, admit, forget, transmit, n_lv):
     """The level loop (:116-120): V (B*H, T, hd), gates (B*H, T, n_lv) after
     masking; in V's dtype, so bf16 inputs round after every product and sum."""
