@@ -95,3 +95,23 @@ def test_full_config_mixer_and_model(golden, tag, seed, nondeg):
     st = [dec.step(nexts[j:j + 1]) for j in range(4)]
     close(st[-1], golden[f"full_{tag}_dec_last_step_logits"])
     assert torch.equal(torch.stack(st, 1).argmax(-1), torch.from_numpy(golden[f"full_{tag}_dec_argmax"]))
+
+
+@pytest.mark.parametrize("tag,seed,nondeg", TAGS)
+def test_gate_preacts_oracle_matches_pinned_mixer(golden, tag, seed, nondeg):
+    """oracle.gate_preacts (the op-level restatement whose fp32 autograd is the
+    backward's oracle) equals the pre-activations of the golden-pinned mixer
+    restatement on the reference's own inputs."""
+    cfg = small_config()
+    sd = make_state_dict(cfg, seed=seed, nondegenerate=nondeg)
+    ids = torch.from_numpy(golden[f"small_{tag}_ids"])
+    x = torch.from_numpy(golden[f"small_{tag}_mix_x"])
+    mask = oracle.tree_mask(ids, cfg.levels, cfg.eot_token, cfg.doc_reset)
+    p = "blocks.0.mixer."
+    inner = oracle.mixer_internals(sd, p, cfg.num_heads, cfg.levels, x, mask)
+    outs = oracle.gate_preacts(inner["A"], inner["B"], sd[p + "gate_out"], sd[p + "forget_out"],
+                               sd[p + "reset_out"], sd[p + "gate_out_bias"],
+                               sd[p + "forget_out_bias"], sd[p + "reset_out_bias"],
+                               inner["n_lv"], mask)
+    for got, name in zip(outs, ("pre_i", "pre_f", "pre_r")):
+        close(got, inner[name])
