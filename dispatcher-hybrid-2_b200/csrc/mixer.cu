@@ -13,13 +13,14 @@
 // rows t - 2^l < 0 are out of bounds and arrive as zeros, which is exactly
 // the wrap mask.  The epilogue adds the bias, applies sigmoid and the
 // wrap/doc masks, and writes
-//   mode 0: gates (B, H, L, 3, T) bf16 — admit*m, forget*m + (1-m), transmit
+//   mode 0: gates (B, H, L, T, 4) bf16 — (admit*m, forget*m + (1-m), transmit, 0)
 //   mode 1: pre-activations (B, T, n_lv, H) x 3 bf16 (the reference op)
 // and optionally the transmit gates of every level into a decoder rg_hist.
 //
 // Level sweep (modeling_dispatcher.py:116-120): one CTA per (sequence, head,
-// 8-channel slice) keeps the slice of V for all positions, fp32 in registers,
-// and exchanges bf16 copies through shared memory once per level.
+// 8-channel slice) keeps the slice of V for all positions in registers (bf16)
+// and exchanges the messages by warp shuffles, within each thread or through
+// shared memory, depending on the shift.
 #include "common.cuh"
 #include "tma.cuh"
 
@@ -522,24 +523,28 @@ __global__ void __launch_bounds__(kGateThreads, 1)
 }
 
 // ------------------------------------------------------------------ scan
-// One CTA per (sequence, head, 8-channel slice).  Thread j owns positions
-// j, j+1024, j+2048, j+3072 of the slice.  Per level l (shift s = 2^l), in the
+// One CTA per (sequence, head, 8-channel slice); warp w owns the 128
+// consecutive positions [128 w, 128 w + 128), lane j the positions
+// 128 w + 32 i + j (i = 0..3).  Per level l (shift s = 2^l), in the
 // reference's order and rounding (modeling_dispatcher.py:116-120, bf16):
-//   msg(t) = r(t) * V(t)                      published to shared memory
+//   msg(t) = r(t) * V(t)
 //   V(t)   = f(t) * V(t) + a(t) * msg(t - s)
 // in bf16x2 arithmetic, one rounding per product and per sum (the _rn forms:
 // no multiply-add contraction, as in the reference's separate bf16 ops), so
-// the sweep is bit-exact against the reference's loop.  Each thread
-// needs only the gates of its own positions: one 8-byte load (admit, forget,
-// transmit, 0) per position.  Consecutive threads touch consecutive 16-byte
-// rows of the message buffer (no bank conflicts).  The next level's gates
-// are loaded while the current level is computed.  The message buffer is
-// double buffered (levels alternate halves), so one barrier per level
-// suffices: a half is rewritten two levels later, after a barrier that every
-// reader of it has passed.  Shifts of 1024 and 2048 stay inside each thread
-// (its positions are 1024 apart): no shared memory and no barrier.
+// the sweep is bit-exact against the reference's loop.  Where msg(t - s)
+// comes from depends on s:
+//   s < 32      lane j - s of the same warp (a shuffle), for the first s lanes
+//               of row 0 the previous warp's row 3 (through shared memory)
+//   s = 32, 64  this thread's own row i - s/32, for the first rows the
+//               previous warp's last rows (through shared memory)
+//   s >= 128    any warp: every message goes through shared memory
+// Each level has one barrier; the shared buffer is double buffered by level
+// parity (a half is rewritten two levels later, after a barrier every reader
+// of it has passed).  Each thread loads only its own positions' gates (one
+// 8-byte load per position, coalesced along the warp), a level ahead.
 constexpr int kScanThreads = 1024;  // 32 warps hide the per-level barrier latency
 constexpr int kScanPer = 4;        // positions per thread (T <= 4096)
+constexpr int kScanXch = 2048;     // minimum entries of a buffer half (the small exchanges)
 
 struct ScanArgs {
   const __nv_bfloat16* v0;
@@ -552,6 +557,11 @@ struct ScanArgs {
   int S;
 };
 
+// position of row i of this thread
+__device__ __forceinline__ int scan_pos(int tid, int i) {
+  return ((tid >> 5) << 7) + (i << 5) + (tid & 31);
+}
+
 struct LevelGates {
   uint2 g[kScanPer];  // (admit | forget << 16, transmit) of each owned position
 };
@@ -563,7 +573,7 @@ __device__ __forceinline__ void load_level(const __nv_bfloat16* __restrict__ gl,
   // the loads here instead of where the next level consumes them.
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
-    const int t = min(tid + i * kScanThreads, T - 1);
+    const int t = min(scan_pos(tid, i), T - 1);
     G.g[i] = __ldg(reinterpret_cast<const uint2*>(gl) + t);
   }
 }
@@ -578,7 +588,7 @@ __device__ __forceinline__ void write_ring(const ScanArgs& a, const ScanState& s
   const int lo = T - (2 << j);
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
-    const int t = tid + i * kScanThreads;
+    const int t = scan_pos(tid, i);
     if (t < T && t >= lo) {
       const int slot = ((2 << j) - 2) + (t & ((2 << j) - 1));
       *reinterpret_cast<uint4*>(a.ring + ((size_t)b * a.S + slot) * d + col) = st.V[i];
@@ -596,80 +606,123 @@ __device__ __forceinline__ __nv_bfloat162 bcast_hi(uint32_t w) {
   return *reinterpret_cast<const __nv_bfloat162*>(&x);
 }
 
-// A level whose shift is K x 1024: t - s is this thread's own position i - K,
-// not yet updated at this level when i runs downwards.
+// msg = r * V of one position (8 channels)
+__device__ __forceinline__ uint4 scan_msg(const uint4& v, uint32_t gy) {
+  const __nv_bfloat162 r2 = bcast_lo(gy);
+  uint4 m = v;
+  __nv_bfloat162* mv = reinterpret_cast<__nv_bfloat162*>(&m);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) mv[e] = __hmul2_rn(r2, mv[e]);
+  return m;
+}
+
+// V = f V + a m  (m = msg(t - s)), or V = f V where no source exists
+__device__ __forceinline__ void scan_update(uint4& v4, uint32_t gx, const uint4& m) {
+  const __nv_bfloat162 a2 = bcast_lo(gx), f2 = bcast_hi(gx);
+  __nv_bfloat162* v = reinterpret_cast<__nv_bfloat162*>(&v4);
+  const __nv_bfloat162* mv = reinterpret_cast<const __nv_bfloat162*>(&m);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) v[e] = __hadd2_rn(__hmul2_rn(f2, v[e]), __hmul2_rn(a2, mv[e]));
+}
+__device__ __forceinline__ void scan_forget_only(uint4& v4, uint32_t gx) {
+  const __nv_bfloat162 f2 = bcast_hi(gx);
+  __nv_bfloat162* v = reinterpret_cast<__nv_bfloat162*>(&v4);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) v[e] = __hmul2_rn(f2, v[e]);
+}
+
+__device__ __forceinline__ uint4 shfl4(const uint4& m, int src) {
+  return make_uint4(__shfl_sync(0xffffffffu, m.x, src), __shfl_sync(0xffffffffu, m.y, src),
+                    __shfl_sync(0xffffffffu, m.z, src), __shfl_sync(0xffffffffu, m.w, src));
+}
+
+// s < 32: lane j - s of the same warp; lanes j < s take row i - 1 of lane
+// j - s + 32, and at row 0 the previous warp's row 3
+__device__ __forceinline__ void scan_level_lanes(ScanState& st, const LevelGates& cur, uint4* xb,
+                                                 int T, int tid, int s) {
+  const int w = tid >> 5, j = tid & 31, src = (j - s) & 31;
+  const uint4 m3 = scan_msg(st.V[3], cur.g[3].y);
+  xb[w * 32 + j] = m3;
+  __syncthreads();
+  uint4 rprev = make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    // row i's message, taken before row i is updated (rows ascend)
+    const uint4 mi = i == kScanPer - 1 ? m3 : scan_msg(st.V[i], cur.g[i].y);
+    const uint4 rc = shfl4(mi, src);  // every lane takes part
+    const int t = scan_pos(tid, i);
+    if (t < T) {
+      if (t < s) {
+        scan_forget_only(st.V[i], cur.g[i].x);
+      } else {
+        const uint4 m = j >= s ? rc : (i > 0 ? rprev : xb[(w - 1) * 32 + src]);
+        scan_update(st.V[i], cur.g[i].x, m);
+      }
+    }
+    rprev = rc;
+  }
+}
+
+// s = 32 K (K = 1, 2): row i - K of this thread; rows i < K from the previous
+// warp's rows i - K + 4
 template <int K>
-__device__ __forceinline__ void scan_level_in_thread(ScanState& st, const LevelGates& cur, int T,
-                                                     int tid) {
+__device__ __forceinline__ void scan_level_rows(ScanState& st, const LevelGates& cur, uint4* xb,
+                                                int T, int tid) {
+  const int w = tid >> 5, j = tid & 31;
+  uint4 m[kScanPer];
 #pragma unroll
-  for (int i = kScanPer - 1; i >= 0; --i) {
-    const int t = tid + i * kScanThreads;
+  for (int i = 0; i < kScanPer; ++i) m[i] = scan_msg(st.V[i], cur.g[i].y);
+#pragma unroll
+  for (int q = 0; q < K; ++q) xb[(w * 2 + q) * 32 + j] = m[kScanPer - K + q];
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int t = scan_pos(tid, i);
     if (t >= T) continue;
-    const __nv_bfloat162 a2 = bcast_lo(cur.g[i].x), f2 = bcast_hi(cur.g[i].x);
-    __nv_bfloat162* v = reinterpret_cast<__nv_bfloat162*>(&st.V[i]);
-    if (i >= K) {
-      const __nv_bfloat162 r2 = bcast_lo(cur.g[i - K].y);
-      const __nv_bfloat162* vs = reinterpret_cast<const __nv_bfloat162*>(&st.V[i - K]);
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        v[e] = __hadd2_rn(__hmul2_rn(f2, v[e]), __hmul2_rn(a2, __hmul2_rn(r2, vs[e])));
+    if (t < 32 * K) {
+      scan_forget_only(st.V[i], cur.g[i].x);
     } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = __hmul2_rn(f2, v[e]);
+      const uint4 mm = i >= K ? m[i >= K ? i - K : 0] : xb[((w - 1) * 2 + i) * 32 + j];
+      scan_update(st.V[i], cur.g[i].x, mm);
     }
   }
 }
 
+// s >= 128: through shared memory, indexed by position
+__device__ __forceinline__ void scan_level_smem(ScanState& st, const LevelGates& cur, uint4* xb,
+                                                int T, int tid, int s) {
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int t = scan_pos(tid, i);
+    if (t < T) xb[t] = scan_msg(st.V[i], cur.g[i].y);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    const int t = scan_pos(tid, i);
+    if (t >= T) continue;
+    if (t >= s) scan_update(st.V[i], cur.g[i].x, xb[t - s]);
+    else scan_forget_only(st.V[i], cur.g[i].x);
+  }
+}
+
 // one level of the sweep; loads the next level's gates into `nxt` first
-__device__ __forceinline__ void scan_level(const ScanArgs& a, ScanState& st, uint4* sx,
+__device__ __forceinline__ void scan_level(const ScanArgs& a, ScanState& st, uint4* sx, int half,
                                            const __nv_bfloat16* gbase, int b, int col, int tid,
                                            int l, int nl, const LevelGates& cur,
                                            LevelGates& nxt) {
   const int T = a.T, s = 1 << l;
   if (l + 1 < nl) load_level(gbase + (size_t)(l + 1) * 4 * T, T, tid, nxt);
-  if (s >= kScanThreads) {
-    const int k = s / kScanThreads;  // a power of two
-    if (k == 1) scan_level_in_thread<1>(st, cur, T, tid);
-    else if (k == 2) scan_level_in_thread<2>(st, cur, T, tid);
-    else scan_level_in_thread<kScanPer>(st, cur, T, tid);
-    if (a.ring && l + 1 < a.L) write_ring(a, st, b, col, tid, l + 1);
-    return;
-  }
-  sx += (l & 1) * T;  // this level's half of the message buffer
-#pragma unroll
-  for (int i = 0; i < kScanPer; ++i) {
-    const int t = tid + i * kScanThreads;
-    if (t < T) {
-      const __nv_bfloat162 r2 = bcast_lo(cur.g[i].y);
-      uint4 m = st.V[i];
-      __nv_bfloat162* mv = reinterpret_cast<__nv_bfloat162*>(&m);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) mv[e] = __hmul2_rn(r2, mv[e]);  // msg = r * V
-      sx[t] = m;
-    }
-  }
-  __syncthreads();
-#pragma unroll
-  for (int i = 0; i < kScanPer; ++i) {
-    const int t = tid + i * kScanThreads;
-    if (t >= T) continue;
-    const __nv_bfloat162 a2 = bcast_lo(cur.g[i].x), f2 = bcast_hi(cur.g[i].x);
-    __nv_bfloat162* v = reinterpret_cast<__nv_bfloat162*>(&st.V[i]);
-    if (t >= s) {
-      uint4 m = sx[t - s];
-      const __nv_bfloat162* mv = reinterpret_cast<const __nv_bfloat162*>(&m);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = __hadd2_rn(__hmul2_rn(f2, v[e]), __hmul2_rn(a2, mv[e]));
-    } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = __hmul2_rn(f2, v[e]);
-    }
-  }
+  uint4* xb = sx + (l & 1) * half;  // this level's half of the message buffer
+  if (s < 32) scan_level_lanes(st, cur, xb, T, tid, s);
+  else if (s == 32) scan_level_rows<1>(st, cur, xb, T, tid);
+  else if (s == 64) scan_level_rows<2>(st, cur, xb, T, tid);
+  else scan_level_smem(st, cur, xb, T, tid, s);
   if (a.ring && l + 1 < a.L) write_ring(a, st, b, col, tid, l + 1);
 }
 
 __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
-  extern __shared__ uint4 sx[];  // 2 x [T] x 8 bf16
+  extern __shared__ uint4 sx[];  // 2 x [max(T, kScanXch)] x 8 bf16
   const int slices = a.hd / 8;
   const int cc = blockIdx.x % slices;
   const int h = (blockIdx.x / slices) % a.H;
@@ -677,13 +730,14 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
   const int col = h * a.hd + cc * 8;
   const int tid = threadIdx.x;
   const int T = a.T;
+  const int half = T > kScanXch ? T : kScanXch;
   const __nv_bfloat16* gbase = a.gates + (((size_t)b * a.H + h) * a.L) * 4 * (size_t)T;
   int nl = a.n_lv;
   while (nl > 0 && (1 << (nl - 1)) > T) --nl;   // the reference stops at shift > T
   ScanState st;
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
-    const int t = tid + i * kScanThreads;
+    const int t = scan_pos(tid, i);
     // unconditional load (positions past the end read the last one, never
     // used): a select on the loaded value would stall here
     st.V[i] = *reinterpret_cast<const uint4*>(a.v0 + ((size_t)b * T + min(t, T - 1)) * a.ld_v0 +
@@ -693,14 +747,14 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(ScanArgs a) {
   LevelGates g0, g1;
   if (nl > 0) load_level(gbase, T, tid, g0);
   for (int l = 0; l < nl; l += 2) {
-    scan_level(a, st, sx, gbase, b, col, tid, l, nl, g0, g1);
-    if (l + 1 < nl) scan_level(a, st, sx, gbase, b, col, tid, l + 1, nl, g1, g0);
+    scan_level(a, st, sx, half, gbase, b, col, tid, l, nl, g0, g1);
+    if (l + 1 < nl) scan_level(a, st, sx, half, gbase, b, col, tid, l + 1, nl, g1, g0);
   }
   if (a.ring)
     for (int j = a.n_lv + 1; j < a.L; ++j) write_ring(a, st, b, col, tid, j);
 #pragma unroll
   for (int i = 0; i < kScanPer; ++i) {
-    const int t = tid + i * kScanThreads;
+    const int t = scan_pos(tid, i);
     if (t < T) *reinterpret_cast<uint4*>(a.out + ((size_t)b * T + t) * a.ld_out + col) = st.V[i];
   }
 }
@@ -823,6 +877,7 @@ extern "C" int dh_level_scan(const void* v0, int ld_v0, const void* gates, void*
                          2 * kScanThreads * kScanPer * 16);
     configured_dev = dev;
   }
-  scan_kernel<<<blocks, kScanThreads, (size_t)T * 32, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  const size_t half = (size_t)(T > kScanXch ? T : kScanXch);
+  scan_kernel<<<blocks, kScanThreads, half * 32, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return check_launch("scan_kernel");
 }
