@@ -45,15 +45,25 @@ __host__ __device__ constexpr uint32_t idesc_bf16_bmn(int M, int N) {
   return idesc_bf16(M, N) | (1u << 16);
 }
 
+// three-input maximum (one instruction on sm_100)
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Key k is visible from query q when 0 <= q - k < W; qk = q - (first key of
 // the 32).  Keys past the sequence end never pass for a stored row q < T.
 template <bool kMasked>
 __device__ __forceinline__ void max32(const uint32_t (&v)[32], float (&mx)[8], int qk, int W) {
 #pragma unroll
-  for (int e = 0; e < 32; ++e) {
-    float x = __uint_as_float(v[e]);
-    if (kMasked && (unsigned)(qk - e) >= (unsigned)W) x = -INFINITY;
-    mx[e & 7] = fmaxf(mx[e & 7], x);
+  for (int e = 0; e < 32; e += 2) {
+    float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
+    if (kMasked) {
+      if ((unsigned)(qk - e) >= (unsigned)W) x0 = -INFINITY;
+      if ((unsigned)(qk - e - 1) >= (unsigned)W) x1 = -INFINITY;
+    }
+    mx[(e >> 1) & 7] = fmax3f(mx[(e >> 1) & 7], x0, x1);
   }
 }
 
