@@ -437,6 +437,52 @@ __global__ void __launch_bounds__(kGateThreads, 1)
         const float m = (float)((mbits >> l) & 1u);
         const int H3 = 3 * H;
         const bool mode0 = g.mode == 0;
+        if (mode0 && H == 16) {
+          // 16 heads: the three 16-column chunks are the admit, forget and
+          // transmit gates; each thread writes its own position's (a, f, r, 0)
+          // per head, straight from registers (consecutive lanes are
+          // consecutive positions, so a warp's 8-byte stores form one
+          // contiguous run): no staging and no barriers
+          uint32_t pk[3][8];
+#pragma unroll
+          for (int c = 0; c < 3; ++c) {
+            uint32_t v[16];
+            tmem_ld16(base + c * 16, v);
+            tmem_ld_wait();
+            float sg[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) sg[e] = sigmoidf_(__uint_as_float(v[e]) + bias[c * 16 + e]);
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              float x0 = sg[e], x1 = sg[e + 1];
+              if (c == 0) {
+                x0 *= m;
+                x1 *= m;
+              } else if (c == 1) {
+                x0 = fmaf(x0, m, 1.f - m);
+                x1 = fmaf(x1, m, 1.f - m);
+              }
+              pk[c][e / 2] = pack2(x0, x1);
+            }
+            if (c == 2 && g.rg_hist && row_ok) {  // transmit gates into the decoder cache
+              __nv_bfloat16* rg = g.rg_hist + (((size_t)b * g.rg_T + t) * g.L + l) * 16;
+#pragma unroll
+              for (int e = 0; e < 16; ++e) rg[e] = f2bf(sg[e]);
+            }
+          }
+          if (l < g.n_lv && row_ok) {
+#pragma unroll
+            for (int hh = 0; hh < 16; ++hh) {
+              const int sh = (hh & 1) * 16;
+              const uint32_t ga = (pk[0][hh >> 1] >> sh) & 0xffffu;
+              const uint32_t gf = (pk[1][hh >> 1] >> sh) & 0xffffu;
+              const uint32_t gr = (pk[2][hh >> 1] >> sh) & 0xffffu;
+              *reinterpret_cast<uint2*>(g.gates + ((((size_t)b * 16 + hh) * g.L + l) * g.T + t) * 4) =
+                  make_uint2(ga | (gf << 16), gr);
+            }
+          }
+          continue;
+        }
         for (int c = 0; c < H3; c += 16) {
           uint32_t v[16];
           tmem_ld16(base + c, v);

@@ -78,6 +78,24 @@ def test_gates_and_scan_small(T, eot):
     assert max_err(V.float().cpu(), ref["V"]) < bound
 
 
+def test_gates_default_width():
+    """The gate kernel at the default width (16 heads: the epilogue writes each
+    position's (admit, forget, transmit, 0) straight from registers) against
+    the oracle's masked sigmoid gates, with a document separator live."""
+    cfg = DispatcherConfig()
+    B, T = 2, 300
+    sd, x, ids, mask = mixer_setup(cfg, 3, True, B, T, ((0, 77), (1, 201)))
+    p = "blocks.0.mixer."
+    ref = oracle.mixer_internals(sd, p, cfg.num_heads, cfg.levels, x, mask)
+    gates, V, n_lv = _gpu_internals(sd, p, cfg, x, mask, B, T)
+    H = cfg.num_heads
+    g = gates.float().cpu()[:, :, :n_lv]                        # (B, H, n_lv, T, 4)
+    for gi, name in enumerate(("admit", "forget", "transmit")):
+        want = ref[name].view(B, H, T, n_lv).permute(0, 1, 3, 2)
+        assert max_err(g[..., gi], want) < 2e-2, name
+    assert torch.equal(g[..., 3], torch.zeros_like(g[..., 3]))
+
+
 @pytest.mark.parametrize("T", [1000, 1024, 1500, 2048, 2049, 3000, 4096])
 def test_level_scan_bit_exact_long(T):
     """The sweep alone at lengths where shifts of 1024 and 2048 occur (levels
