@@ -63,11 +63,6 @@ def interleave_swiglu(w_gate, w_up, block=128):
 
 
 # ------------------------------------------------------------------ mixer ops
-def _levels(L, T):
-    import math
-    return min(L, int(math.log2(T)) + 1) if T > 1 else 1
-
-
 def tree_mask(ids, L, eot_token, doc_reset=True):
     """uint8 (B, T, L) wrap + doc-reset mask (modeling_dispatcher.py:282-323)."""
     if not ids.is_cuda:

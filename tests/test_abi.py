@@ -37,6 +37,24 @@ def test_errors_are_reported_not_trapped():
     assert rc == 2 and b"null" in lib.dh_last_error()
 
 
+def _status_entry_points():
+    return [(n, args) for n, (res, args) in _lib.parse_header().items()
+            if res is ctypes.c_int and args]
+
+
+@pytest.mark.parametrize("name,args", _status_entry_points(), ids=lambda v: v if isinstance(v, str) else "")
+def test_every_entry_point_rejects_null_pointers_on_the_host(name, args):
+    """With every pointer null (sizes 1), each status-returning entry point
+    answers DH_ERR_ARG with a message naming itself, before any CUDA call,
+    so the check is safe on a machine with or without a GPU."""
+    lib = _lib.load()
+    vals = [None if a is ctypes.c_void_p else 1 for a in args]
+    rc = getattr(lib, name)(*vals)
+    assert rc == 2, (name, rc)
+    msg = lib.dh_last_error()
+    assert msg.startswith(name.encode()) and b"null" in msg, msg
+
+
 def test_library_is_built_for_sm100a_only():
     assert build.ARCH_FLAGS == ["-gencode", "arch=compute_100a,code=sm_100a"]
     assert os.path.exists(build.LIB_PATH)
