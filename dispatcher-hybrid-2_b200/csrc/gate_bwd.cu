@@ -16,14 +16,18 @@
 //   warp 1      tcgen05.mma, no mbarrier waits (a named-barrier handoff from
 //               warp 10): dh = dP . W_l^T (M=128 positions, N=64, K=48) and
 //               dW^T = dP^T . h^T (M=128 gate rows, 48 used, N=64, K=128
-//               positions), both into TMEM
-//   warps 2-9   two threads per position (32 columns each): write dP and its
-//               transpose into shared memory, recompute x, relu(x) and h^T;
+//               positions), both into TMEM; dW^T reads the dP tile and the h
+//               tile MN-major, i.e. with positions as K, so no transposed
+//               copy is ever written
+//   warps 2-9   two threads per position (32 columns each): write the
+//               position's dP row and h row into shared memory (16-byte
+//               stores), recompute x and relu(x);
 //               then, one stage later, read dh back and accumulate dA in
 //               registers over the levels (stored once per slice: only this
 //               CTA writes these positions), add dB, dW and db atomically
 //   warp 10     mbarrier waits for warp 1
-// All operands are K-major with the 128-byte swizzle.  Every wait is
+// dh's operands are K-major, dW^T's MN-major, all with the 128-byte swizzle
+// (rows of 128 bytes, 16-byte chunk c of row r at c ^ (r & 7)).  Every wait is
 // bounded; after a failed wait a thread skips later waits but keeps every
 // handoff, so nothing blocks.
 #include "common.cuh"
@@ -39,8 +43,9 @@ constexpr int kGbThreads = 352;
 constexpr int kGbWaiterWarp = 10;
 constexpr int kGbHandoffBar = 1;
 constexpr int kGbTile = kGbT * 128;            // 16 KB: 128 rows of 128 bytes
-// per stage: dP (t x j) 16 KB, dP^T (j x t) 2 atoms x 16 KB, h^T (k x t) 2 atoms x 8 KB
-constexpr int kGbStageBytes = kGbTile + 2 * kGbTile + 2 * (kGbK * 128);
+// per stage: dP (t x j) 16 KB, a zero tile 16 KB (gate rows 64..127 of the
+// dW^T MMA's M = 128), h (t x k) 16 KB
+constexpr int kGbStageBytes = 3 * kGbTile;
 constexpr int kGbSmem = 1024 + 2 * kGbStageBytes + 2 * kGbTile /*A*/ + 2 * kGbTile /*B*/ +
                         2 * (kGbK * 128) /*W^T*/ + 256;
 constexpr int kGbTmemCols = 256;               // per stage: dh 64 + dW^T 64 (x2 stages)
@@ -85,7 +90,14 @@ __device__ __forceinline__ bool gb_handoff(bool ok) {
   return r != 0;
 }
 
-// shared memory: two stages of [dP | dP^T (2 atoms) | h^T (2 atoms)], then the
+// MN-major 128B-swizzled operand: each 128-byte row is one K index (here a
+// position) holding 64 MN elements; 8-row groups are 1024 B apart (SBO) and
+// the next 64 MN elements start lbo bytes on (LBO)
+__device__ __forceinline__ uint64_t mn_sw128_desc(uint32_t smem_addr, uint32_t lbo) {
+  return (sw128_desc(smem_addr) & ~(uint64_t(0x3FFF) << 16)) | ((uint64_t)(lbo >> 4) << 16);
+}
+
+// shared memory: two stages of [dP | zero tile | h], then the
 // A tiles, the B tiles and the W^T tiles (two of each), then the barriers
 struct GbSmem {
   uint8_t* base;
@@ -103,8 +115,8 @@ struct GbSmem {
 };
 
 __device__ __forceinline__ uint8_t* st_dp(uint8_t* s) { return s; }
-__device__ __forceinline__ uint8_t* st_dpt(uint8_t* s) { return s + kGbTile; }
-__device__ __forceinline__ uint8_t* st_ht(uint8_t* s) { return s + 3 * kGbTile; }
+__device__ __forceinline__ uint8_t* st_zero(uint8_t* s) { return s + kGbTile; }
+__device__ __forceinline__ uint8_t* st_h(uint8_t* s) { return s + 2 * kGbTile; }
 
 __global__ void __launch_bounds__(kGbThreads, 1)
     gate_bwd_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -117,7 +129,7 @@ __global__ void __launch_bounds__(kGbThreads, 1)
   uint64_t* a_full = bars;          // [2] A tile of slice kc, by kc & 1
   uint64_t* a_empty = bars + 2;     // [2]
   uint64_t* tb_full = bars + 4;     // [2] B tile + W^T of iteration i, by i & 1
-  uint64_t* ops_full = bars + 6;    // [2] dP, dP^T, h^T written
+  uint64_t* ops_full = bars + 6;    // [2] dP and h written
   uint64_t* mma_done = bars + 8;    // [2] both contractions of iteration i complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
 
@@ -136,10 +148,11 @@ __global__ void __launch_bounds__(kGbThreads, 1)
     }
     fence_barrier_init();
   }
-  // rows >= 3H of dP^T stay zero (the MMA reads all 128 rows of its M)
+  // dP columns >= 3H and the zero tile stay zero: the dW^T MMA reads all 128
+  // gate rows of its M (rows 64..127 from the zero tile)
   for (int s = 0; s < 2; ++s) {
-    uint4* z = reinterpret_cast<uint4*>(st_dpt(S.stage(s)));
-    for (int i = threadIdx.x; i < 2 * kGbTile / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
+    uint4* z = reinterpret_cast<uint4*>(st_zero(S.stage(s)));
+    for (int i = threadIdx.x; i < kGbTile / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
     uint4* zp = reinterpret_cast<uint4*>(st_dp(S.stage(s)));
     for (int i = threadIdx.x; i < kGbTile / 16; i += blockDim.x) zp[i] = make_uint4(0, 0, 0, 0);
   }
@@ -183,7 +196,7 @@ __global__ void __launch_bounds__(kGbThreads, 1)
     }
   } else if (warp == 1) {  // ---------------- MMA issue
     const uint32_t id_dh = idesc_bf16(kGbT, kGbK);
-    const uint32_t id_dw = idesc_bf16(128, kGbK);
+    const uint32_t id_dw = idesc_bf16(128, kGbK) | (1u << 15) | (1u << 16);  // A, B MN-major
     bool ok = true;
     for (int i = 0; i < iters; ++i) {
       const int s = i & 1;
@@ -191,18 +204,15 @@ __global__ void __launch_bounds__(kGbThreads, 1)
       tc_fence_after();
       if (ok && lane == 0) {
         uint8_t* st = S.stage(s);
-        const uint32_t dp = smem_u32(st_dp(st)), dpt = smem_u32(st_dpt(st));
-        const uint32_t ht = smem_u32(st_ht(st)), wt = smem_u32(S.wt(s));
+        const uint32_t dp = smem_u32(st_dp(st)), hp = smem_u32(st_h(st)), wt = smem_u32(S.wt(s));
         const uint32_t d_dh = tmem + (uint32_t)(s * 128), d_dw = d_dh + 64;
 #pragma unroll
         for (int kk = 0; kk < 3; ++kk)  // K = 48 gate rows (3H <= 48; rows past 3H are 0)
           umma_bf16(d_dh, sw128_desc(dp + kk * 32), sw128_desc(wt + kk * 32), id_dh, kk != 0);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // K = 128 positions, two 64-wide atoms
-          const uint32_t o = (uint32_t)((kk >> 2) * kGbTile + (kk & 3) * 32);
-          const uint32_t oh = (uint32_t)((kk >> 2) * (kGbK * 128) + (kk & 3) * 32);
-          umma_bf16(d_dw, sw128_desc(dpt + o), sw128_desc(ht + oh), id_dw, kk != 0);
-        }
+        for (int kk = 0; kk < 8; ++kk)  // K = 128 positions, 16 rows (2 KB) per instruction
+          umma_bf16(d_dw, mn_sw128_desc(dp + kk * 2048, kGbTile), mn_sw128_desc(hp + kk * 2048, kGbTile),
+                    id_dw, kk != 0);
         umma_commit(&mma_done[s]);
       }
       __syncwarp();
@@ -279,12 +289,6 @@ __global__ void __launch_bounds__(kGbThreads, 1)
         for (int c = 0; c < 3; ++c)
           *reinterpret_cast<uint4*>(dpb + sw_off(r, half * 24 + c * 8)) =
               make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-        // column r of dP^T (j x t), atom r / 64
-        uint8_t* dptb = st_dpt(st) + (r >> 6) * kGbTile;
-#pragma unroll
-        for (int e = 0; e < 24; ++e)
-          *reinterpret_cast<unsigned short*>(dptb + sw_off(half * 24 + e, r & 63)) =
-              (unsigned short)(v[e >> 1] >> ((e & 1) * 16));
         // db_l: column sums over the tile's rows, once per level (slice 0)
         if (kc == 0) {
 #pragma unroll
@@ -300,13 +304,13 @@ __global__ void __launch_bounds__(kGbThreads, 1)
           }
         }
       }
-      // x = A + m B(t - 2^l) in bf16, relu, h = relu^2 -> column r of h^T
+      // x = A + m B(t - 2^l) in bf16, relu, h = relu^2 -> row r of h
       {
         const uint8_t* arow = S.a(kc & 1) + r * 128;
         const uint8_t* brow = S.b(s) + r * 128;
         const __nv_bfloat162 m2 = __floats2bfloat162_rn(m ? 1.f : 0.f, m ? 1.f : 0.f);
         const __nv_bfloat162 z2 = __floats2bfloat162_rn(0.f, 0.f);
-        uint8_t* htb = st_ht(st) + (r >> 6) * (kGbK * 128);
+        uint8_t* hrow = st_h(st);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int chunk = half * 4 + c;
@@ -314,17 +318,15 @@ __global__ void __launch_bounds__(kGbThreads, 1)
           uint4 bv = *reinterpret_cast<const uint4*>(brow + ((chunk ^ (r & 7)) << 4));
           const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&av);
           const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bv);
+          uint32_t hb[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             __nv_bfloat162 x = __hfma2(m2, b2[e], a2[e]);
             x = __hmax2(x, z2);
-            const uint32_t xb = b2u(x);
-            rx[c * 4 + e] = xb;
-            const uint32_t hb = b2u(__hmul2_rn(x, x));
-            const int k = chunk * 8 + e * 2;
-            *reinterpret_cast<unsigned short*>(htb + sw_off(k, r & 63)) = (unsigned short)hb;
-            *reinterpret_cast<unsigned short*>(htb + sw_off(k + 1, r & 63)) = (unsigned short)(hb >> 16);
+            rx[c * 4 + e] = b2u(x);
+            hb[e] = b2u(__hmul2_rn(x, x));
           }
+          *reinterpret_cast<uint4*>(hrow + sw_off(r, chunk * 8)) = make_uint4(hb[0], hb[1], hb[2], hb[3]);
         }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
