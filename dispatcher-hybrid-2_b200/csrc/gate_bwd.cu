@@ -12,7 +12,8 @@
 // width outermost, levels innermost, two pipeline stages.  Warp roles:
 //   warp 0      TMA: the A tile of a slice, the B tile shifted by 2^l and the
 //               W_l^T slice (W pre-transposed and padded to 64 gate rows) of
-//               each (slice, level)
+//               each (slice, level), and at 16 heads the step's dP rows
+//               (3 x 128 positions x 32 bytes)
 //   warp 1      tcgen05.mma, no mbarrier waits (a named-barrier handoff from
 //               warp 10): dh = dP . W_l^T (M=128 positions, N=64, K=48) and
 //               dW^T = dP^T . h^T (M=128 gate rows, 48 used, N=64, K=128
@@ -46,8 +47,9 @@ constexpr int kGbTile = kGbT * 128;            // 16 KB: 128 rows of 128 bytes
 // per stage: dP (t x j) 16 KB, a zero tile 16 KB (gate rows 64..127 of the
 // dW^T MMA's M = 128), h (t x k) 16 KB
 constexpr int kGbStageBytes = 3 * kGbTile;
+constexpr int kGbDpIn = 3 * kGbT * 32;         // 12 KB: dP rows of one step (16 heads)
 constexpr int kGbSmem = 1024 + 2 * kGbStageBytes + 2 * kGbTile /*A*/ + 2 * kGbTile /*B*/ +
-                        2 * (kGbK * 128) /*W^T*/ + 256;
+                        2 * (kGbK * 128) /*W^T*/ + 2 * kGbDpIn + 256;
 constexpr int kGbTmemCols = 256;               // per stage: dh 64 + dW^T 64 (x2 stages)
 
 struct GbArgs {
@@ -98,7 +100,8 @@ __device__ __forceinline__ uint64_t mn_sw128_desc(uint32_t smem_addr, uint32_t l
 }
 
 // shared memory: two stages of [dP | zero tile | h], then the
-// A tiles, the B tiles and the W^T tiles (two of each), then the barriers
+// A tiles, the B tiles, the W^T tiles and the dP row copies (two of each),
+// then the barriers
 struct GbSmem {
   uint8_t* base;
   __device__ __forceinline__ uint8_t* stage(int s) const { return base + s * kGbStageBytes; }
@@ -109,8 +112,11 @@ struct GbSmem {
   __device__ __forceinline__ uint8_t* wt(int s) const {
     return base + 2 * kGbStageBytes + 4 * kGbTile + s * (kGbK * 128);
   }
+  __device__ __forceinline__ uint8_t* dpin(int s) const {
+    return base + 2 * kGbStageBytes + 4 * kGbTile + 2 * (kGbK * 128) + s * kGbDpIn;
+  }
   __device__ __forceinline__ uint8_t* end() const {
-    return base + 2 * kGbStageBytes + 4 * kGbTile + 2 * (kGbK * 128);
+    return base + 2 * kGbStageBytes + 4 * kGbTile + 2 * (kGbK * 128) + 2 * kGbDpIn;
   }
 };
 
@@ -120,7 +126,10 @@ __device__ __forceinline__ uint8_t* st_h(uint8_t* s) { return s + 2 * kGbTile; }
 
 __global__ void __launch_bounds__(kGbThreads, 1)
     gate_bwd_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmW, GbArgs g) {
+                    const __grid_constant__ CUtensorMap tmW,
+                    const __grid_constant__ CUtensorMap tmDi,
+                    const __grid_constant__ CUtensorMap tmDf,
+                    const __grid_constant__ CUtensorMap tmDr, GbArgs g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -128,7 +137,7 @@ __global__ void __launch_bounds__(kGbThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(S.end());
   uint64_t* a_full = bars;          // [2] A tile of slice kc, by kc & 1
   uint64_t* a_empty = bars + 2;     // [2]
-  uint64_t* tb_full = bars + 4;     // [2] B tile + W^T of iteration i, by i & 1
+  uint64_t* tb_full = bars + 4;     // [2] B tile + W^T (+ dP rows) of iteration i, by i & 1
   uint64_t* ops_full = bars + 6;    // [2] dP and h written
   uint64_t* mma_done = bars + 8;    // [2] both contractions of iteration i complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
@@ -137,6 +146,7 @@ __global__ void __launch_bounds__(kGbThreads, 1)
   const int t0 = blockIdx.x * kGbT, b = blockIdx.y;
   const int nk = g.gh / kGbK, nl = g.n_lv, H = g.H, H3 = 3 * g.H;
   const int iters = nk * nl;
+  const bool dp_tma = H == 16;      // dP rows arrive by TMA (32-byte rows)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -165,6 +175,11 @@ __global__ void __launch_bounds__(kGbThreads, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmW);
+    if (dp_tma) {
+      prefetch_tmap(&tmDi);
+      prefetch_tmap(&tmDf);
+      prefetch_tmap(&tmDr);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -185,9 +200,14 @@ __global__ void __launch_bounds__(kGbThreads, 1)
         // stage s was last used by iteration i - 2: its MMAs must be done
         if (i >= 2) ok = ok && mbar_wait(&mma_done[s], (uint32_t)(((i >> 1) - 1) & 1), g.err);
         if (!ok) break;
-        mbar_arrive_expect_tx(&tb_full[s], kGbTile + kGbK * 128);
+        mbar_arrive_expect_tx(&tb_full[s], kGbTile + kGbK * 128 + (dp_tma ? kGbDpIn : 0));
         tma_load_3d(&tmB, &tb_full[s], S.b(s), kc * kGbK, t0 - (1 << l), b);
         tma_load_2d(&tmW, &tb_full[s], S.wt(s), 0, l * g.gh + kc * kGbK);
+        if (dp_tma) {  // box (16 heads, 1 level, 128 positions, 1 sequence), rows past T read 0
+          tma_load_4d(&tmDi, &tb_full[s], S.dpin(s), 0, l, t0, b);
+          tma_load_4d(&tmDf, &tb_full[s], S.dpin(s) + kGbT * 32, 0, l, t0, b);
+          tma_load_4d(&tmDr, &tb_full[s], S.dpin(s) + 2 * kGbT * 32, 0, l, t0, b);
+        }
       }
       // drain: every issued copy has landed before exit
       if (iters > 0) mbar_wait(&tb_full[(iters - 1) & 1], (uint32_t)(((iters - 1) >> 1) & 1), nullptr, 1u << 20);
@@ -252,13 +272,13 @@ __global__ void __launch_bounds__(kGbThreads, 1)
         uint32_t v[12];
 #pragma unroll
         for (int e = 0; e < 12; ++e) v[e] = 0u;
-        if (row_ok && H == 16) {
-          // the three 32-byte dP rows of this position: half 0 takes dPi and
-          // the first half of dPf, half 1 the rest (three 16-byte loads)
-          const size_t o = (((size_t)b * g.T + t) * nl + l) * 16;
-          const uint4* pi = reinterpret_cast<const uint4*>(g.dpi + o);
-          const uint4* pf = reinterpret_cast<const uint4*>(g.dpf + o);
-          const uint4* pr = reinterpret_cast<const uint4*>(g.dpr + o);
+        if (row_ok && dp_tma) {
+          // the three 32-byte dP rows of this position, copied in by TMA: half
+          // 0 takes dPi and the first half of dPf, half 1 the rest
+          const uint8_t* rows = S.dpin(s) + r * 32;
+          const uint4* pi = reinterpret_cast<const uint4*>(rows);
+          const uint4* pf = reinterpret_cast<const uint4*>(rows + kGbT * 32);
+          const uint4* pr = reinterpret_cast<const uint4*>(rows + 2 * kGbT * 32);
           const uint4 u0 = half ? pf[1] : pi[0], u1 = half ? pr[0] : pi[1], u2 = half ? pr[1] : pf[0];
           v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
           v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
@@ -438,7 +458,7 @@ extern "C" int dh_gate_preacts_bwd(const void* a, int lda, const void* bsrc, int
   DH_REQUIRE(aligned16(dpi) && aligned16(dpf) && aligned16(dpr) && aligned16(dA) &&
                  aligned16(dB) && aligned16(dWi) && aligned16(dWf) && aligned16(dWr),
              DH_ERR_ARG, "dh_gate_preacts_bwd: dP and gradient buffers must be 16-byte aligned");
-  CUtensorMap ta, tb, tw;
+  CUtensorMap ta, tb, tw, tdi, tdf, tdr;
   const uint64_t da[3] = {(uint64_t)gh, (uint64_t)T, (uint64_t)batch};
   const uint64_t sa[2] = {(uint64_t)lda * 2, (uint64_t)lda * 2 * T};
   const uint64_t sb[2] = {(uint64_t)ldb * 2, (uint64_t)ldb * 2 * T};
@@ -452,6 +472,17 @@ extern "C" int dh_gate_preacts_bwd(const void* a, int lda, const void* bsrc, int
   const uint32_t bw[2] = {kGbJ, kGbK};
   rc = make_tmap_bf16(&tw, wt, 2, dw, sw, bw, true);
   if (rc) return rc;
+  if (H == 16) {  // dP (batch, T, n_lv, 16): one 32-byte row per (position, level)
+    const uint64_t dd[4] = {16, (uint64_t)n_lv, (uint64_t)T, (uint64_t)batch};
+    const uint64_t sd[3] = {32, (uint64_t)n_lv * 32, (uint64_t)n_lv * 32 * T};
+    const uint32_t bd[4] = {16, 1, kGbT, 1};
+    rc = make_tmap_bf16(&tdi, dpi, 4, dd, sd, bd, false);
+    if (!rc) rc = make_tmap_bf16(&tdf, dpf, 4, dd, sd, bd, false);
+    if (!rc) rc = make_tmap_bf16(&tdr, dpr, 4, dd, sd, bd, false);
+    if (rc) return rc;
+  } else {  // not read by the kernel at other head counts
+    tdi = tdf = tdr = tw;
+  }
   GbArgs g{batch, T, H, n_lv, gh, mask_L, mask,
            reinterpret_cast<const __nv_bfloat16*>(dpi), reinterpret_cast<const __nv_bfloat16*>(dpf),
            reinterpret_cast<const __nv_bfloat16*>(dpr), dA, dB, dWi, dWf, dWr, dbi, dbf, dbr,
@@ -464,7 +495,7 @@ extern "C" int dh_gate_preacts_bwd(const void* a, int lda, const void* bsrc, int
     configured_dev = dev;
   }
   dim3 grid((T + kGbT - 1) / kGbT, batch);
-  gate_bwd_kernel<<<grid, kGbThreads, kGbSmem, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, tw,
-                                                                                       g);
+  gate_bwd_kernel<<<grid, kGbThreads, kGbSmem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      ta, tb, tw, tdi, tdf, tdr, g);
   return check_launch("gate_bwd_kernel");
 }
