@@ -202,7 +202,8 @@ DH_API int dh_gate_preacts_fwd(const void* a, int lda, const void* bsrc, int ldb
  * strides lda, ldb; wt bf16 (n_lv*gh, 64): per level W^T with the 3H gate
  * rows (i | f | r) as columns, zero padded; mask uint8 (batch, T, mask_L) or
  * NULL (the wrap mask is always applied).  gh % 64 == 0, 3H <= 48,
- * n_lv <= 16.  status (nullable) is set to DH_ERR_TIMEOUT if a bounded
+ * n_lv <= 16; dpi/dpf/dpr, dA, dB and dW* 16-byte aligned (DH_ERR_ARG
+ * otherwise).  status (nullable) is set to DH_ERR_TIMEOUT if a bounded
  * pipeline wait gave up. */
 DH_API int dh_gate_preacts_bwd(const void* a, int lda, const void* bsrc, int ldb, const void* wt,
                                const uint8_t* mask, int mask_L, int batch, int T, int H,
