@@ -40,10 +40,12 @@ def _autograd(A, B, W, bias, dP, mask, n_lv):
     return torch.autograd.grad(loss, leaves)
 
 
-@pytest.mark.parametrize("T,with_mask", [(200, False), (200, True), (64, False), (1, False),
-                                         (300, True), (1024, False)])
-def test_gate_preacts_bwd_matches_autograd(T, with_mask):
-    A, B, W, bias, dP, mask, n_lv = _case(T, with_mask)
+@pytest.mark.parametrize("T,with_mask,H", [(200, False, 16), (200, True, 16), (64, False, 16),
+                                           (1, False, 16), (300, True, 16), (1024, False, 16),
+                                           (200, True, 8), (130, False, 5)])
+def test_gate_preacts_bwd_matches_autograd(T, with_mask, H):
+    """16 heads: dP rows arrive by TMA; other head counts: per-thread loads."""
+    A, B, W, bias, dP, mask, n_lv = _case(T, with_mask, H=H)
     want = _autograd(A, B, W, bias, dP, mask, n_lv)
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     got = ops.gate_preacts_bwd(A.cuda(), B.cuda(), *(w.cuda() for w in W),
