@@ -433,7 +433,12 @@ def main():
         "config": prefill_config(world),
         "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05, all prefill projections)",
                      "achieved": gemm_tf, "peak": peak_t, "unit": "TFLOP/s",
-                     "frac": gemm_tf / peak_t, "traffic": None, "peak_kind": f"{pk_kind} sustained",
+                     "frac": gemm_tf / peak_t, "traffic": None,
+                     "traffic_note": "achieved averages 73 launches of five shapes per step; "
+                                     "DRAM bytes per shape come from one ncu capture each "
+                                     "(gate/up at 4 x 4096: 123.8 MB read + written against "
+                                     "137 MB algorithmic, profiles/gemm_kernel__gate_up_4x4096.md)",
+                     "peak_kind": f"{pk_kind} sustained",
                      "launches_timed": g_n,
                      "whole_step_tflops": flop_tok * tokens / (ms * 1e-3) / 1e12,
                      "whole_step_frac": flop_tok * tokens / (ms * 1e-3) / 1e12 / peak_t,
