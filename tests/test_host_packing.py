@@ -1,7 +1,7 @@
 """CPU checks of the host-side weight layouts the kernels read: the SwiGLU
 row interleave of the gate/up GEMM, the gate-weight packs of the forward and
-backward gate kernels, the level count of the parallel forward, and the
-single-document rule of the incremental decoders.  No GPU is needed: these
+backward gate kernels, the decode step's packs, the level count of the
+parallel forward, and the single-document rule of the incremental decoders.  No GPU is needed: these
 are the torch reshapes that run once before any launch."""
 
 import pytest
@@ -96,3 +96,34 @@ def test_config_validation_and_levels():
     cfg = DispatcherConfig()
     assert cfg.levels == 12 and cfg.head_dim == 64 and cfg.attn_slots() == {7, 16}
     assert DispatcherConfig(attn_window=0).attn_slots() == set()
+
+
+def test_decode_step_weight_packs():
+    """Decode packs: gate/up as (ff, 2, d) row pairs, the three gate readouts
+    of a tree layer as (L*H, 3, gh) with biases (L*H, 3) fp32 — one
+    contiguous 3-row group per (level, head) for the tree step's GEMV."""
+    from types import SimpleNamespace
+    from dispatcher_b200.step_params import pack_step_weights
+    g = torch.Generator().manual_seed(3)
+    ff, d, L, H, gh = 384, 128, 8, 2, 64
+    W, b = _gate_weights(L, H, gh, seed=3)
+    tree = dict(kind="tree", w_gate=torch.randn(ff, d, generator=g).bfloat16(),
+                w_up=torch.randn(ff, d, generator=g).bfloat16(),
+                wi=W[0], wf=W[1], wr=W[2], bi=b[0], bf=b[1], br=b[2])
+    attn = dict(kind="attn", w_gate=torch.randn(ff, d, generator=g).bfloat16(),
+                w_up=torch.randn(ff, d, generator=g).bfloat16())
+    packed = SimpleNamespace(layers=[tree, attn])
+    pack_step_weights(packed)
+    for lay in (tree, attn):
+        gu = lay["w_gu_pairs"]
+        assert gu.shape == (ff, 2, d) and gu.is_contiguous()
+        assert torch.equal(gu[:, 0], lay["w_gate"]) and torch.equal(gu[:, 1], lay["w_up"])
+    assert "w_gates3" not in attn
+    w3, b3 = tree["w_gates3"], tree["b_gates3"]
+    assert w3.shape == (L * H, 3, gh) and b3.shape == (L * H, 3) and b3.dtype == torch.float32
+    for gi in range(3):
+        assert torch.equal(w3[:, gi].reshape(L, H, gh), W[gi])
+        assert torch.equal(b3[:, gi].reshape(L, H), b[gi])
+    before = w3.data_ptr()
+    pack_step_weights(packed)            # built once: a second call keeps the packs
+    assert tree["w_gates3"].data_ptr() == before
