@@ -830,12 +830,16 @@ extern "C" int dh_tree_mask(const int64_t* ids, int batch, int T, int L, int64_t
 static int launch_gates(const void* a, int lda, const void* bsrc, int ldb, const void* wg,
                         GateArgs g, cudaStream_t st) {
   DH_REQUIRE(a && bsrc && wg && g.bias, DH_ERR_ARG, "mixer gates: null pointer");
+  DH_REQUIRE(g.B > 0 && g.T > 0 && g.H > 0, DH_ERR_SHAPE, "mixer gates: batch=%d T=%d H=%d",
+             g.B, g.T, g.H);
   DH_REQUIRE(g.gh % kSlice == 0 && g.NP % 16 == 0 && g.NP <= 64 && 3 * g.H <= g.NP,
              DH_ERR_SHAPE, "mixer gates: gh=%d NP=%d H=%d unsupported", g.gh, g.NP, g.H);
   DH_REQUIRE(g.n_calc >= 1 && g.n_calc <= g.L && g.n_lv <= g.n_calc && g.L * g.NP <= kBiasMax,
              DH_ERR_SHAPE,
              "mixer gates: level counts n_lv=%d n_calc=%d L=%d", g.n_lv, g.n_calc, g.L);
   DH_REQUIRE(lda % 8 == 0 && ldb % 8 == 0, DH_ERR_SHAPE, "mixer gates: row strides must be multiples of 8");
+  DH_REQUIRE(!g.mask || g.mask_L >= g.n_calc, DH_ERR_SHAPE,
+             "mixer gates: mask has %d levels per position, %d are read", g.mask_L, g.n_calc);
   g.nws = g.NP <= 48 ? 3 : 2;
   const int smem = gate_smem(g.NP, g.nws);
   CUtensorMap ta, tb, tbw, tw;
@@ -908,8 +912,9 @@ extern "C" int dh_level_scan(const void* v0, int ld_v0, const void* gates, void*
   DH_REQUIRE(v0 && gates && out, DH_ERR_ARG, "dh_level_scan: null pointer");
   DH_REQUIRE(T > 0 && T <= kScanThreads * kScanPer, DH_ERR_SHAPE,
              "dh_level_scan: T=%d exceeds %d", T, kScanThreads * kScanPer);
-  DH_REQUIRE(hd % 8 == 0 && ld_v0 % 8 == 0 && ld_out % 8 == 0 && n_lv <= L, DH_ERR_SHAPE,
-             "dh_level_scan: bad sizes");
+  DH_REQUIRE(batch > 0 && H > 0 && hd > 0 && hd % 8 == 0 && ld_v0 % 8 == 0 && ld_out % 8 == 0 &&
+                 L >= 1 && L < 30 && n_lv >= 0 && n_lv <= L,
+             DH_ERR_SHAPE, "dh_level_scan: bad sizes");
   ScanArgs a{reinterpret_cast<const __nv_bfloat16*>(v0), ld_v0,
              reinterpret_cast<const __nv_bfloat16*>(gates),
              reinterpret_cast<__nv_bfloat16*>(out), ld_out, batch, T, H, hd, L, n_lv,

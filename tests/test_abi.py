@@ -96,3 +96,29 @@ def test_step_params_layout_matches_header(tmp_path):
     want = [ctypes.sizeof(LayerParams), ctypes.sizeof(StepParams), StepParams.tokens.offset,
             StepParams.layers.offset, StepParams.status.offset]
     assert got == want
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="host-only argument checks; run without a GPU")
+def test_shape_errors_are_reported_before_any_launch():
+    """Sizes a kernel cannot take are refused with DH_ERR_SHAPE on the host.
+    The pointers are never dereferenced (the checks run first), and the test
+    is skipped where a GPU is present."""
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(1 << 12)
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    # gate pre-activations: 12 levels computed over a mask that holds 3 per position
+    rc = lib.dh_gate_preacts_fwd(p, 1024, p, 1024, p, p, p, 3, 1, 128, 16, 12, 48, 1024, 12,
+                                 p, p, p, None, None)
+    assert rc == 1 and b"mask has 3 levels" in lib.dh_last_error()
+    # more levels than the layer has, empty batch
+    rc = lib.dh_mixer_gates(p, 3072, p, 3072, p, p, p, 1, 128, 16, 4, 48, 1024, 12, p, p, 4096,
+                            None, None)
+    assert rc == 1 and b"level counts" in lib.dh_last_error()
+    rc = lib.dh_mixer_gates(p, 3072, p, 3072, p, p, None, 0, 128, 16, 12, 48, 1024, 12, p,
+                            None, 0, None, None)
+    assert rc == 1 and b"batch=0" in lib.dh_last_error()
+    for args in ((0, 128, 16, 64, 12, 12), (1, 128, 0, 64, 12, 12), (1, 128, 16, 64, 0, 0),
+                 (1, 128, 16, 64, 12, 13), (1, 128, 16, 60, 12, 12)):
+        batch, T, H, hd, L, n_lv = args
+        rc = lib.dh_level_scan(p, 3072, p, p, 1024, batch, T, H, hd, L, n_lv, None, None)
+        assert rc == 1 and b"dh_level_scan" in lib.dh_last_error(), args
