@@ -321,6 +321,30 @@ def cpu_prefill_sample(cfg, T=1024, steps=1):
                       f"of the same synthetic distribution, {steps} timed pass(es)"}
 
 
+def cpu_decode_sample(cfg, prompt=256, steps=8):
+    """The reference's incremental decoder (oracle restatement of
+    IncrementalDecoder), fp32 on the host cores: batch 1, greedy steps after a
+    short prompt.  A step streams every weight once and reads a window of at
+    most 1024 keys, so its cost barely depends on the context length."""
+    import oracle
+    from dispatcher_b200 import make_state_dict
+    torch.set_num_threads(os.cpu_count() or 1)
+    sd = make_state_dict(cfg, seed=0)
+    ids = prompt_ids(1, prompt, 1, cfg.vocab_size, cfg.eot_token)
+    dec = oracle.OracleDecoder(sd, cfg)
+    with torch.no_grad():
+        tok = dec.prefill(ids)[:, -1].argmax(-1)
+        tok = dec.step(tok).argmax(-1)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            tok = dec.step(tok).argmax(-1)
+        dt = (time.perf_counter() - t0) / steps
+    return {"value": 1.0 / dt, "unit": "tok/s", "ms_per_step": dt * 1e3,
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"oracle IncrementalDecoder (eager restatement of the reference), fp32, "
+                      f"batch 1, {steps} greedy steps after a {prompt}-token prompt"}
+
+
 def reference_arm(args, world, rank, cfg):
     """The reference's own algorithm on the host cores (the oracle restates the
     reference's eager PyTorch forward op for op): each step is a bounded
@@ -457,6 +481,10 @@ def main():
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_prefill_sample(cfg)
+        try:
+            line["decode"]["b1"]["cpu_baseline"] = cpu_decode_sample(cfg)
+        except Exception as exc:  # a reported baseline: never the reason a bench line is lost
+            line["decode"]["b1"]["cpu_baseline"] = {"error": repr(exc)[:200]}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
