@@ -186,6 +186,7 @@ def run_prefill(engine, ids, steps, warmup, world, logits_buf):
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(s.elapsed_time(e), world) / steps
+    engine.check_status(sync=True)   # a timed-out wait anywhere in the window raises here
     engine.record_events = []
     for _ in range(steps):
         engine.forward(ids, logits_out=logits_buf)
@@ -244,8 +245,7 @@ def run_decode(model, cfg, batch, ctx, steps, warmup, seed, world):
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(s.elapsed_time(e), world) / steps
-    if int(dec.status.item()) != 0:
-        raise RuntimeError(f"decode kernel reported status {int(dec.status.item())}")
+    dec.check_status(sync=True)
     return ms, steps, dec.persistent
 
 
@@ -379,6 +379,46 @@ def reference_arm(args, world, rank, cfg):
         torch.distributed.destroy_process_group()
 
 
+def profile_case(a):
+    """A fixed, small workload to run under a profiler (never a bench value):
+
+        python bench.py --profile-case prefill --batch 4 --seq 4096 --iters 1
+        python bench.py --profile-case decode --batch 1 --ctx 3900 --iters 3
+        python bench.py --profile-case gate_bwd --batch 4 --seq 4096 --iters 2
+
+    Default 292M config, seeded random-init bf16 weights, uniform token ids."""
+    from dispatcher_b200 import (DispatcherConfig, DispatcherHybridForCausalLM,
+                                 FusedGraphedHybridDecoder, ops)
+    from dispatcher_b200.engine import PrefillEngine
+    cfg = DispatcherConfig()
+    g = torch.Generator().manual_seed(0)
+    if a.profile_case == "gate_bwd":  # one tree layer's gate readout backward, all levels
+        b, T, gh, H, L = a.batch, a.seq, cfg.d_model, cfg.num_heads, cfg.levels
+        n_lv = min(L, T.bit_length())
+        A, B = ((torch.randn(b, T, gh, generator=g) * 0.5).bfloat16().cuda() for _ in range(2))
+        W = [(torch.randn(L, H, gh, generator=g) * 0.05).bfloat16().cuda() for _ in range(3)]
+        dP = [torch.randn(b, T, n_lv, H, generator=g).bfloat16().cuda() for _ in range(3)]
+        for _ in range(a.iters):
+            ops.gate_preacts_bwd(A, B, *W, *dP, n_lv)
+    else:
+        model = DispatcherHybridForCausalLM(cfg, seed=0).to("cuda", torch.bfloat16)
+        if a.profile_case == "prefill":
+            ids = torch.randint(0, cfg.vocab_size, (a.batch, a.seq), generator=g).cuda()
+            eng = PrefillEngine(model)
+            for _ in range(a.iters):
+                eng.forward(ids)
+            eng.check_status(sync=True)
+        else:
+            ids = torch.randint(0, cfg.eot_token, (a.batch, a.ctx), generator=g).cuda()
+            dec = FusedGraphedHybridDecoder(model, step_kernel=a.step_kernel)
+            tok = dec.prefill(ids)[:, -1].argmax(-1)
+            for _ in range(a.iters):
+                tok = dec.step(tok).argmax(-1)
+            dec.check_status(sync=True)
+    torch.cuda.synchronize()
+    print("ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -387,7 +427,16 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--decode-steps", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", choices=["prefill", "decode", "gate_bwd"],
+                    help="run a small fixed workload for a profiler and exit (no JSON line)")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--ctx", type=int, default=1024)
+    ap.add_argument("--iters", type=int, default=2)
+    ap.add_argument("--step-kernel", default="graph")
     args = ap.parse_args()
+    if args.profile_case:
+        return profile_case(args)
     args.warmup = max(3, args.warmup)
 
     world, rank, local = dist_setup()

@@ -25,6 +25,12 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 int sm_count();
 
+// Poll limit of the bounded waits that report a timeout (host side, read at
+// each launch and passed to the kernel): kDefaultWaitLimit unless
+// dh_set_wait_limit chose another (0 makes every such wait give up at once).
+constexpr uint32_t kDefaultWaitLimit = 1u << 26;
+uint32_t wait_limit();
+
 // ---------------------------------------------------------------------------
 // numerics
 // ---------------------------------------------------------------------------
@@ -124,7 +130,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
 // try_wait itself suspends for a hardware-defined interval per poll, so the
 // bound corresponds to far more than any legitimate pipeline stall.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, int* err,
-                                          uint32_t limit = (1u << 26)) {
+                                          uint32_t limit = kDefaultWaitLimit) {
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, phase)) return true;
   }

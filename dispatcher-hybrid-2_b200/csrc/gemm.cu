@@ -59,6 +59,7 @@ struct GemmArgs {
   int n_out;
   int band;
   int* err;
+  uint32_t wait_limit;  // polls of each bounded wait before it reports a timeout
 };
 
 template <int BN>
@@ -216,7 +217,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int mb, nb;
         tile_coords(tile, m_blocks, n_blocks, band, mb, nb);
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, g.err)) { okk = false; break; }
+          if (!mbar_wait(&empty[stage], phase ^ 1, g.err, g.wait_limit)) { okk = false; break; }
           mbar_arrive_expect_tx(&full[stage], C::A_BYTES + C::B_BYTES);
           tma_load_2d(&ta, &full[stage], sA + stage * C::A_BYTES, kb * BK, mb * BM);
           tma_load_2d(&tb, &full[stage], sB + stage * C::B_BYTES, kb * BK, nb * BN);
@@ -263,8 +264,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int kb = 0; kb < kblocks; ++kb) {
         // after a failed (bounded) wait, skip every later wait but keep the
         // handoffs, so the two warps stay in lockstep and nothing blocks
-        if (kb == 0) okk = okk && mbar_wait(&tempty[acc], acc_phase ^ 1, g.err);
-        okk = okk && mbar_wait(&full[stage], phase, g.err);
+        if (kb == 0) okk = okk && mbar_wait(&tempty[acc], acc_phase ^ 1, g.err, g.wait_limit);
+        okk = okk && mbar_wait(&full[stage], phase, g.err, g.wait_limit);
         okk = handoff(okk);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
@@ -279,7 +280,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mb, nb;
       tile_coords(tile, m_blocks, n_blocks, band, mb, nb);
-      if (!mbar_wait(&tfull[acc], acc_phase, g.err)) break;
+      if (!mbar_wait(&tfull[acc], acc_phase, g.err, g.wait_limit)) break;
       tc_fence_after();
       const int row0 = mb * BM + q * 32;
       const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
@@ -370,7 +371,8 @@ extern "C" int dh_gemm_bf16(const void* A, int lda, const void* W, int ldw, void
   DH_REQUIRE(epilogue >= 0 && epilogue <= 2, DH_ERR_ARG, "dh_gemm_bf16: epilogue %d", epilogue);
   DH_REQUIRE(epilogue != EPI_RESIDUAL || R, DH_ERR_ARG, "dh_gemm_bf16: residual pointer missing");
   GemmArgs g{M, N, K, reinterpret_cast<__nv_bfloat16*>(C), ldc,
-             reinterpret_cast<const __nv_bfloat16*>(R), ldr, epilogue, N, 16, status};
+             reinterpret_cast<const __nv_bfloat16*>(R), ldr, epilogue, N, 16, status,
+             wait_limit()};
   if (epilogue == EPI_SWIGLU) {
     DH_REQUIRE(N % 256 == 0, DH_ERR_SHAPE,
                "dh_gemm_bf16: SwiGLU needs N (= 2 ff) a multiple of 256, got %d", N);

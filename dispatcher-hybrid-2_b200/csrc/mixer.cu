@@ -141,6 +141,7 @@ struct GateArgs {
   __nv_bfloat16* rg_hist;
   int rg_T;
   int* err;
+  uint32_t wait_limit;  // polls of each bounded wait before it reports a timeout
 };
 
 __host__ __device__ constexpr int gate_wbytes(int NP) { return kWLevels * NP * 128; }
@@ -248,7 +249,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
           const int x = kc * kSlice;
           // W of the group's levels, kWLevels levels per copy
           for (int c0 = l0; c0 < l1 && ok; c0 += kWLevels) {
-            if (!mbar_wait(&w_empty[ws], wph ^ 1, g.err)) { ok = false; break; }
+            if (!mbar_wait(&w_empty[ws], wph ^ 1, g.err, g.wait_limit)) { ok = false; break; }
             mbar_arrive_expect_tx(&w_full[ws], (uint32_t)wbytes);
             tma_load_2d(&tmW, &w_full[ws], sW + ws * wbytes, x, c0 * g.NP);
             ++fills_w;
@@ -256,7 +257,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
           }
           // A tile + the B rows of the stage's levels
           for (int i = 0; i < nab && ok; ++i) {
-            if (!mbar_wait(&ab_empty[abs_], abph ^ 1, g.err)) { ok = false; break; }
+            if (!mbar_wait(&ab_empty[abs_], abph ^ 1, g.err, g.wait_limit)) { ok = false; break; }
             uint8_t* st = sAB + abs_ * kABBytes;
             int a0, a1;
             gate_ab_levels(grp, i, l0, l1, a0, a1);
@@ -329,8 +330,8 @@ __global__ void __launch_bounds__(kGateThreads, 1)
           const int c0 = l0 + ((l - l0) / kWLevels) * kWLevels;
           // after a failed (bounded) wait, skip every later wait but keep the
           // handoffs, so the two warps stay in lockstep and nothing blocks
-          if (l == c0) ok = ok && mbar_wait(&w_full[ws], wph, g.err);
-          ok = ok && mbar_wait(&h_full[hs], hph, g.err);
+          if (l == c0) ok = ok && mbar_wait(&w_full[ws], wph, g.err, g.wait_limit);
+          ok = ok && mbar_wait(&h_full[hs], hph, g.err, g.wait_limit);
           ok = gate_handoff(ok);
           if (++hs == kHBufs) { hs = 0; hph ^= 1; }
           if (l + 1 == l1 || l + 1 == c0 + kWLevels) {
@@ -364,7 +365,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
       const int nab = gate_nab(grp, l0, l1);
       for (int kc = 0; kc < nk; ++kc) {
         for (int i = 0; i < nab; ++i) {
-          ok = ok && mbar_wait(&ab_full[abs_], abph, g.err);
+          ok = ok && mbar_wait(&ab_full[abs_], abph, g.err, g.wait_limit);
           const uint8_t* st = sAB + abs_ * kABBytes;
           uint4 av[8];  // this row of the A slice (64 columns)
 #pragma unroll
@@ -376,7 +377,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
             // the two builder groups (warps 2-5, 6-9) take alternate tiles, so
             // two tiles are in flight; each thread builds one whole row
             if ((jt & 1) == half) {
-              ok = ok && mbar_wait(&h_empty[hs], hph ^ 1, g.err);
+              ok = ok && mbar_wait(&h_empty[hs], hph ^ 1, g.err, g.wait_limit);
               tc_fence_after();
               // source row t - 2^l: row r + 128 - 2^l of the window (group 0) or
               // row r of the level's own tile (group 1); rows before position 0
@@ -424,7 +425,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
       // All MMAs of the group are complete: half k stages each level's
       // (3H x 128) gate tile in staging buffer k, column-major, and the half
       // then writes it as 16-byte runs along T.
-      ok = ok && mbar_wait(d_full, dph, g.err);
+      ok = ok && mbar_wait(d_full, dph, g.err, g.wait_limit);
       dph ^= 1;
       tc_fence_after();
       const int H = g.H;
@@ -841,6 +842,7 @@ static int launch_gates(const void* a, int lda, const void* bsrc, int ldb, const
   DH_REQUIRE(!g.mask || g.mask_L >= g.n_calc, DH_ERR_SHAPE,
              "mixer gates: mask has %d levels per position, %d are read", g.mask_L, g.n_calc);
   g.nws = g.NP <= 48 ? 3 : 2;
+  g.wait_limit = wait_limit();
   const int smem = gate_smem(g.NP, g.nws);
   CUtensorMap ta, tb, tbw, tw;
   const uint64_t da[3] = {(uint64_t)g.gh, (uint64_t)g.T, (uint64_t)g.B};

@@ -2,6 +2,8 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace dh {
@@ -20,6 +22,15 @@ int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(DH_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return DH_OK;
+}
+
+// process-wide; negative = the default limit
+static std::atomic<long long> g_wait_limit{-1};
+
+uint32_t wait_limit() {
+  const long long v = g_wait_limit.load(std::memory_order_relaxed);
+  if (v < 0) return kDefaultWaitLimit;
+  return v > 0xffffffffll ? 0xffffffffu : (uint32_t)v;
 }
 
 int sm_count() {
@@ -45,5 +56,10 @@ extern "C" const char* dh_last_error(void) { return dh::g_err; }
 extern "C" int dh_sm_count(int* out) {
   if (!out) return dh::set_error(DH_ERR_ARG, "dh_sm_count: null output");
   *out = dh::sm_count();
+  return DH_OK;
+}
+
+extern "C" int dh_set_wait_limit(long long polls) {
+  dh::g_wait_limit.store(polls < 0 ? -1 : polls, std::memory_order_relaxed);
   return DH_OK;
 }

@@ -25,6 +25,7 @@ import torch
 
 from . import _lib
 from .packing import PackedModel, config_of
+from .status import StatusWord
 
 
 def _ptr(t):
@@ -163,7 +164,10 @@ class FusedGraphedHybridDecoder:
         self.nsplit = max(1, min(16, math.ceil(2 * sm / max(1, min(batch, 16) * H))))
         self.part = torch.zeros(batch, H, self.nsplit, hd + 2, device=dev, dtype=f32)
         self.counters = torch.zeros(H + batch * H, device=dev, dtype=torch.int32)
-        self.status = torch.zeros(1, device=dev, dtype=torch.int32)
+        # bounded waits and bad token ids report here; read back without a
+        # host sync after each call and raised at the next (check_status)
+        self.status_word = StatusWord(dev)
+        self.status = self.status_word.tensor
         self.barrier = torch.zeros(2, device=dev, dtype=torch.int64)
         self.graph = None
         # one persistent kernel per step for lockstep batches of up to 16 rows
@@ -250,6 +254,13 @@ class FusedGraphedHybridDecoder:
         self.graph = g
 
     # ------------------------------------------------------------ public
+    def check_status(self, sync=False):
+        """Raise DispatcherB200Error if a kernel of an earlier step or prefill
+        reported a failed bounded wait or an out-of-range token; sync=True
+        waits for the last call's report."""
+        if self.caches is not None:
+            self.status_word.check("FusedGraphedHybridDecoder", sync=sync)
+
     def _prepare_prompt(self, idx):
         self._squeeze = idx.dim() == 1
         ids = idx.view(1, -1) if self._squeeze else idx
@@ -261,6 +272,7 @@ class FusedGraphedHybridDecoder:
         if T < 1:
             raise ValueError("empty prompt")
         ids = ids.to(self.device)
+        self.check_status()
         self._alloc(ids.shape[0])
         return ids, T
 
@@ -291,6 +303,7 @@ class FusedGraphedHybridDecoder:
             self.last_tok.copy_(ids[:, T - 1])
         self.t = T
         self.t_buf.fill_(T)
+        self.status_word.arm()
         return out[0] if self._squeeze else out
 
     @torch.no_grad()
@@ -309,6 +322,7 @@ class FusedGraphedHybridDecoder:
             self.graph.replay()
             out[:, p].copy_(self.logits_out)
         self.t = T
+        self.status_word.arm()
         return out[0] if self._squeeze else out
 
     @torch.no_grad()
@@ -321,10 +335,12 @@ class FusedGraphedHybridDecoder:
         toks = tokens.view(-1)
         if toks.shape[0] != self.batch:
             raise ValueError(f"got {toks.shape[0]} tokens for batch {self.batch}")
+        self.check_status()
         self.token_buf.copy_(toks)
         self.graph.replay()
         self.t += 1
         out = self.logits_out.clone()
+        self.status_word.arm()
         return out[0] if self._squeeze else out
 
 

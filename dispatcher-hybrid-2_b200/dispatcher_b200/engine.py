@@ -26,6 +26,7 @@ import torch
 from . import _lib
 from .ops import interleave_swiglu
 from .packing import PackedModel, config_of
+from .status import StatusWord
 
 
 def _p(t):
@@ -63,12 +64,20 @@ class PrefillEngine:
         self.rope_cos = ang.cos().to(self.device).contiguous()
         self.rope_sin = ang.sin().to(self.device).contiguous()
         self._bufs = {}
-        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # every kernel's bounded waits report here; read back without a host
+        # sync after each forward and raised at the next one (check_status)
+        self.status_word = StatusWord(self.device)
+        self.status = self.status_word.tensor
         self.record_events = None   # optional list collecting (name, start, end) events
         self.calls = 0              # C-ABI launches issued (each starts one kernel)
 
     def stale(self):
         return self.w.stale()
+
+    def check_status(self, sync=False):
+        """Raise DispatcherB200Error if a kernel of an earlier forward reported
+        a failed bounded wait or a bad input; sync=True waits for the last one."""
+        self.status_word.check("PrefillEngine.forward", sync=sync)
 
     def _buffers(self, B, T):
         key = (B, T)
@@ -115,6 +124,7 @@ class PrefillEngine:
         if ids.dim() == 1:
             ids = ids.view(1, -1)
         ids = ids.to(self.device, torch.long).contiguous()
+        self.check_status()
         cfg, W = self.cfg, self.w
         B, T = ids.shape
         if T > cfg.max_len:
@@ -179,4 +189,5 @@ class PrefillEngine:
         self._timed("lm_head", 2.0 * M_ * N_ * K_, "dh_gemm_bf16", _p(h), h.stride(0),
                     _p(W.lm_head), W.lm_head.stride(0), _p(lo), lo.stride(0), None, 0, M_, N_,
                     K_, 0, _p(self.status), s)
+        self.status_word.arm()
         return lo.view(B, T, lo.shape[1])[..., :Vv]

@@ -11,6 +11,22 @@ import torch.nn.functional as F
 
 from .decoding import FusedGraphedHybridDecoder
 
+def masked_logits(logits, temperature=1.0, top_k=None):
+    """fp32 logits over max(T, 1e-6) with every logit below the k-th largest
+    set to -inf (modeling_dispatcher.py:427-430)."""
+    logits = logits.float() / max(temperature, 1e-6)
+    if top_k is not None:
+        kth = torch.topk(logits, top_k, dim=-1).values[:, -1:]
+        logits = logits.masked_fill(logits < kth, float("-inf"))
+    return logits
+
+
+def sampling_distribution(logits, temperature=1.0, top_k=None):
+    """(B, vocab) probabilities a sampled next token is drawn from
+    (modeling_dispatcher.py:427-432)."""
+    return F.softmax(masked_logits(logits, temperature, top_k), dim=-1)
+
+
 DECODERS = {"fused": FusedGraphedHybridDecoder, "graphed": FusedGraphedHybridDecoder,
             "eager": FusedGraphedHybridDecoder, "b200": FusedGraphedHybridDecoder}
 
@@ -39,10 +55,7 @@ def fast_generate(model, input_ids, max_new_tokens=50, do_sample=False, temperat
     finished = torch.zeros(Bb, dtype=torch.bool, device=ids.device)
     out = [ids]
     for _ in range(max_new_tokens):
-        logits = logits.float() / max(temperature, 1e-6)
-        if top_k is not None:
-            kth = torch.topk(logits, top_k, dim=-1).values[:, -1:]
-            logits = logits.masked_fill(logits < kth, float("-inf"))
+        logits = masked_logits(logits, temperature, top_k)
         nxt = (torch.multinomial(F.softmax(logits, dim=-1), 1)[:, 0] if do_sample
                else logits.argmax(-1))
         nxt = nxt.to(ids.device)

@@ -178,9 +178,9 @@ def rope_tables(max_len, hd, device):
     return ang.cos().to(device).contiguous(), ang.sin().to(device).contiguous()
 
 
-def window_attention(qkv, batch, H, window, rope=True, out=None, tensor_cores=True, status=None):
-    """qkv (batch*T, 3d) bf16 (q, k rotated in place when rope) -> (batch*T, d).
-    tensor_cores: the tcgen05 kernel (else the mma.sync one)."""
+def window_attention(qkv, batch, H, window, rope=True, out=None, status=None):
+    """qkv (batch*T, 3d) bf16 (q, k rotated in place when rope) -> (batch*T, d)
+    on the tcgen05 attention kernel."""
     _check(qkv, "qkv")
     M, d3 = qkv.shape
     d = d3 // 3
@@ -191,10 +191,6 @@ def window_attention(qkv, batch, H, window, rope=True, out=None, tensor_cores=Tr
         _lib.call("dh_rope_qk", _p(qkv), qkv.stride(0), M, T, d, hd, _p(cos), _p(sin), _stream())
     if out is None:
         out = torch.empty(M, d, device=qkv.device, dtype=torch.bfloat16)
-    if tensor_cores:
-        _lib.call("dh_window_attn_prefill_tc", _p(qkv), qkv.stride(0), _p(out), out.stride(0),
-                  batch, T, H, hd, window, _p(status), _stream())
-    else:
-        _lib.call("dh_window_attn_prefill", _p(qkv), qkv.stride(0), _p(out), out.stride(0), batch,
-                  T, H, hd, window, _stream())
+    _lib.call("dh_window_attn_prefill_tc", _p(qkv), qkv.stride(0), _p(out), out.stride(0),
+              batch, T, H, hd, window, _p(status), _stream())
     return out

@@ -46,6 +46,18 @@ DH_API const char* dh_version(void);
 DH_API const char* dh_last_error(void);
 DH_API int dh_sm_count(int* out);
 
+/* Poll limit of the bounded device-side waits that report DH_ERR_TIMEOUT
+ * (TMA and MMA pipeline waits of the GEMM and gate kernels, the cross-CTA
+ * waits of the persistent decode step), read at each launch; polls < 0
+ * restores the default (2^26 polls of mbarrier.try_wait, far beyond any
+ * legitimate stall), 0 makes every such wait give up at once.  A kernel
+ * whose wait gives up skips its later waits, issues no further copies or
+ * MMAs, drains what it issued, and returns with *status set: the output is
+ * invalid but the context stays usable.  Process-wide; meant for tests of
+ * the failure path.  The reference has no counterpart (its Triton kernels
+ * have no device-side waits). */
+DH_API int dh_set_wait_limit(long long polls);
+
 /* ---------------------------------------------------------------- decode */
 
 /* x[b,:] = fp32(E[tokens[b],:]).  Replaces the embedding lookup of the
@@ -248,15 +260,11 @@ DH_API int dh_copy_rows(const void* src, int ld_src, void* dst, int ld_dst,
 /* Sliding-window causal attention over a (batch*T, ld) qkv projection with
  * q, k already rotated: keys s with t - window < s <= t (all s <= t when
  * window <= 0 or window >= T), scale 1/sqrt(hd), hd = 64; out bf16
- * (batch*T, ldo) (modeling_dispatcher.py:168-185). */
-DH_API int dh_window_attn_prefill(const void* qkv, int ld, void* out, int ldo, int batch, int T,
-                                  int H, int hd, int window, void* stream);
-
-/* dh_window_attn_prefill on the 5th-gen tensor cores: S = Q K^T and O += P V
- * with tcgen05.mma (accumulators and P in tensor memory), online softmax in
- * fp32 over blocks of 128 keys.  Same arguments and result; status
- * (nullable) is set to DH_ERR_TIMEOUT if a bounded pipeline wait gave up.
- * ldo % 8 == 0. */
+ * (batch*T, ldo), ldo % 8 == 0 (modeling_dispatcher.py:168-185).  Runs on
+ * the 5th-gen tensor cores: S = Q K^T and O += P V with tcgen05.mma
+ * (accumulators and P in tensor memory), online softmax in fp32 over blocks
+ * of 128 keys.  status (nullable) is set to DH_ERR_TIMEOUT if a bounded
+ * pipeline wait gave up. */
 DH_API int dh_window_attn_prefill_tc(const void* qkv, int ld, void* out, int ldo, int batch,
                                      int T, int H, int hd, int window, int* status,
                                      void* stream);

@@ -21,4 +21,4 @@ from .model import (level_mask, tree_mask, rmsnorm, mixer_forward,  # noqa: F401
                     mixer_internals, level_sweep, gate_preacts, rope_tables, apply_rope,
                     window_attention, swiglu, forward, n_levels)
 from .decoder import OracleDecoder, RING_OFFSETS, ring_slot  # noqa: F401
-from .generate import fast_generate  # noqa: F401
+from .generate import fast_generate, masked_logits, sampling_probs  # noqa: F401

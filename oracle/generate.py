@@ -8,6 +8,21 @@ import torch
 import torch.nn.functional as F
 
 
+def masked_logits(logits, temperature=1.0, top_k=None):
+    """fp32 logits over max(T, 1e-6), every logit below the k-th largest set
+    to -inf (modeling_dispatcher.py:427-430)."""
+    logits = logits.float() / max(temperature, 1e-6)
+    if top_k is not None:
+        kth = torch.topk(logits, top_k, dim=-1).values[:, -1:]
+        logits = logits.masked_fill(logits < kth, float("-inf"))
+    return logits
+
+
+def sampling_probs(logits, temperature=1.0, top_k=None):
+    """The distribution a sampled token is drawn from (:427-432)."""
+    return F.softmax(masked_logits(logits, temperature, top_k), dim=-1)
+
+
 @torch.no_grad()
 def fast_generate(dec, input_ids, max_new_tokens=50, do_sample=False,
                   temperature=1.0, top_k=None, eos_token_id=None,
@@ -25,10 +40,7 @@ def fast_generate(dec, input_ids, max_new_tokens=50, do_sample=False,
     finished = torch.zeros(Bb, dtype=torch.bool, device=ids.device)
     out = [ids]
     for _ in range(max_new_tokens):                                     # :426-441
-        logits = logits.float() / max(temperature, 1e-6)
-        if top_k is not None:
-            kth = torch.topk(logits, top_k, dim=-1).values[:, -1:]
-            logits = logits.masked_fill(logits < kth, float("-inf"))
+        logits = masked_logits(logits, temperature, top_k)
         nxt = (torch.multinomial(F.softmax(logits, dim=-1), 1)[:, 0] if do_sample
                else logits.argmax(-1))
         if eos_token_id is not None:

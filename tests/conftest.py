@@ -21,3 +21,20 @@ def pytest_configure(config):
 def golden():
     import numpy as np
     return np.load(GOLDEN)
+
+
+def reference_package():
+    """Import the reference package (dispatcher_hybrid) when its source tree
+    is available: from $DISPATCHER_REFERENCE, or a `reference` directory next
+    to this repository.  Returns None otherwise (the GPU box never has it)."""
+    import importlib
+    for d in (os.environ.get("DISPATCHER_REFERENCE", ""),
+              os.path.join(os.path.dirname(ROOT), "reference")):
+        if d and os.path.isdir(os.path.join(d, "dispatcher_hybrid")):
+            if d not in sys.path:
+                sys.path.append(d)
+            break
+    try:
+        return importlib.import_module("dispatcher_hybrid")
+    except Exception:
+        return None

@@ -39,7 +39,14 @@ def test_errors_are_reported_not_trapped():
 
 def _status_entry_points():
     return [(n, args) for n, (res, args) in _lib.parse_header().items()
-            if res is ctypes.c_int and args]
+            if res is ctypes.c_int and ctypes.c_void_p in args]
+
+
+def test_wait_limit_setting_needs_no_device():
+    """dh_set_wait_limit only records a host-side value for later launches."""
+    lib = _lib.load()
+    assert lib.dh_set_wait_limit(12345) == 0
+    assert lib.dh_set_wait_limit(-1) == 0
 
 
 @pytest.mark.parametrize("name,args", _status_entry_points(), ids=lambda v: v if isinstance(v, str) else "")

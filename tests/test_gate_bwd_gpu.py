@@ -40,12 +40,15 @@ def _autograd(A, B, W, bias, dP, mask, n_lv):
     return torch.autograd.grad(loss, leaves)
 
 
-@pytest.mark.parametrize("T,with_mask,H", [(200, False, 16), (200, True, 16), (64, False, 16),
-                                           (1, False, 16), (300, True, 16), (1024, False, 16),
-                                           (200, True, 8), (130, False, 5)])
-def test_gate_preacts_bwd_matches_autograd(T, with_mask, H):
+@pytest.mark.parametrize("T,with_mask,H,gh", [
+    (200, False, 16, 128), (200, True, 16, 128), (64, False, 16, 128), (1, False, 16, 128),
+    (300, True, 16, 128), (1024, False, 16, 128), (200, True, 8, 128), (130, False, 5, 128),
+    # the default gate-hidden width (16 slices of 64 columns): dA kept in
+    # registers across all levels of a slice, dW / db summed over 16 slices
+    (512, False, 16, 1024), (512, True, 16, 1024), (77, True, 8, 1024)])
+def test_gate_preacts_bwd_matches_autograd(T, with_mask, H, gh):
     """16 heads: dP rows arrive by TMA; other head counts: per-thread loads."""
-    A, B, W, bias, dP, mask, n_lv = _case(T, with_mask, H=H)
+    A, B, W, bias, dP, mask, n_lv = _case(T, with_mask, H=H, gh=gh)
     want = _autograd(A, B, W, bias, dP, mask, n_lv)
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     got = ops.gate_preacts_bwd(A.cuda(), B.cuda(), *(w.cuda() for w in W),

@@ -161,17 +161,15 @@ def test_gate_preacts_op_matches_reference_semantics():
         assert max_err(got.float().cpu(), want) < 0.02 * want.abs().max().item() + 1e-2, name
 
 
-@pytest.mark.parametrize("tensor_cores", [True, False])
 @pytest.mark.parametrize("T,window", [(100, 64), (300, 64), (256, 1024), (1100, 1024), (64, 0),
                                       (1, 64), (129, 128)])
-def test_window_attention(T, window, tensor_cores):
+def test_window_attention(T, window):
     B, H, hd = 2, 4, 64
     d = H * hd
     g = torch.Generator().manual_seed(T)
     qkv = torch.randn(B * T, 3 * d, generator=g).bfloat16()
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    got = ops.window_attention(qkv.cuda().clone(), B, H, window, tensor_cores=tensor_cores,
-                               status=status).float().cpu()
+    got = ops.window_attention(qkv.cuda().clone(), B, H, window, status=status).float().cpu()
     assert int(status.item()) == 0
     q, k, v = qkv.float().view(B, T, 3, H, hd).permute(2, 0, 3, 1, 4)
     cos, sin = oracle.rope_tables(T, hd)
