@@ -1,23 +1,41 @@
 // Whole decode step as ONE persistent cooperative kernel (one CTA per SM).
 //
-// A step is a fixed sequence of phases (embedding; per block: input
-// projection, mixer or attention, output projection + residual, FFN input,
-// FFN down + residual; logits).  Every weight matrix of a phase is split into
-// contiguous row ranges, one per CTA, so each weight byte crosses HBM once per
-// step.  Weights never depend on activations: each CTA runs a weight stream —
-// its slices of all phases, in phase order, cut into chunks and copied by
-// bulk async copies (cp.async.bulk) into a ring of shared-memory slots — that
-// runs ahead of the grid barriers.  After a barrier a phase only reads the
-// (small) activation vector of the lockstep batch from L2 and computes from
-// shared memory.
+// Roles.  The last H CTAs are "head" CTAs (one per attention head of the
+// mixer); the others are "GEMV" CTAs.  A tree block is three dependent
+// phases:
+//   A  (GEMV CTAs)  h = RMSNorm(x); [v0 | A | B_hist[t]] = W3 h
+//   B  (head CTAs)  head h: the gate readouts of all levels
+//                   (relu^2(A + B_hist[t - 2^l]) . W_l), the level recurrence
+//                   over the ring buffers, and the head's share of the output
+//                   projection, added into the residual with vector atomics
+//   C  (GEMV CTAs)  h2 = RMSNorm(x); u = silu(Wg h2) * (Wu h2) for this CTA's
+//                   slice of the FFN width; x += Wd[:, slice] u (vector atomics)
+// An attention block is A (q, k, v with RoPE, cache write), B (window
+// attention split over the GEMV CTAs, last-arriver combine), O (output
+// projection, rows owned) and C.  The step ends with the logits on all CTAs.
+// This follows the reference's fused step (decoding.py:457-488 with
+// fused_step.py:26-88) and attention step (decoding.py:411-435).
 //
-// The tree block's gates + level recurrence keep the structure of the
-// per-op kernel (fused_step.py:26-88 semantics): CTAs own (level, head)
-// items, and the last CTA to finish a head runs that head's recurrence.
+// Weights never depend on activations, so each CTA's producer warp streams
+// its slices of every phase of the step, in consumption order, by bulk async
+// copies (cp.async.bulk) into a ring of shared-memory slots that runs ahead
+// of the phase waits; history rows the head CTAs need (B_hist at t - 2^l)
+// travel in the same stream, and ring slots, transmit gates at the source
+// positions and the attention window's keys and values (all written by
+// earlier steps) are loaded before each wait.  After a wait a phase reads
+// only the small activation vector and computes from shared memory.
 //
-// Grid barrier: a monotonically increasing 64-bit arrival counter; every
-// wait is bounded and a timeout sets *status, after which the kernel keeps
-// going without waiting (wrong data, but it always terminates).
+// Hand-off: a phase's CTAs add 1 to its own monotonically increasing 64-bit
+// counter with release semantics after their writes; waiters spin on it with
+// acquire loads up to a bounded number of polls.  The residual stream lives in
+// two fp32 buffers: xb accumulates (C adds into it, the next A reads it), xa
+// is the input of C (A copies xb into it, B or O adds into both).
+//
+// Failure path: every wait is bounded.  A wait that gives up sets *status to
+// DH_ERR_TIMEOUT and an abort flag in shared memory; from then on the CTA
+// skips its waits (computing garbage but always arriving, so the counters
+// stay consistent), its producer issues no further copies and, before the
+// CTA exits, waits (with a fixed bound) for the copies it issued.
 #include <math.h>
 
 #include "common.cuh"
@@ -25,55 +43,53 @@
 namespace dh {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+constexpr int kWarps = 8;                    // consumer warps
+constexpr int kCons = kWarps * 32;           // consumer threads
+constexpr int kThreads = kCons + 32;         // + the producer warp
+constexpr int kSlotBytes = 32 * 1024;
+// ring depth: 5 slots up to 4 lockstep rows, 4 for 8 rows (their staging needs the room)
+template <int MAXB>
+constexpr int slots_for() { return MAXB >= 8 ? 4 : 5; }
+constexpr int kKvPos = 128;                  // window positions staged per attention item
+constexpr int kLmax = 16;
+constexpr int kMaxUpc = 32;                  // FFN elements per GEMV CTA
 constexpr float kEps = 1.1920928955078125e-07f;  // torch RMSNorm eps=None in fp32
-constexpr uint32_t kSpinLimit = 1u << 22;
-constexpr int kSlots = 3;          // weight-stream slots in shared memory
-constexpr int kSlotBytes = 40960;  // bytes per slot (a chunk is whole units)
+constexpr uint32_t kDrainLimit = 1u << 20;
+constexpr int kSyncStride = 32;              // uint64 words between two phase counters
 
-// ------------------------------------------------------------------ ctx
-struct Ctx {
-  const dh_step_params& p;  // the kernel's __grid_constant__ parameter
-  int G, cta;
-  unsigned long long base;  // barrier counter value at launch
-  int nbar;                 // barriers passed so far in this launch
-  long long t;              // position of this step
-  __nv_bfloat16* xs;        // staged input activations [batch][K]
-  float* red;               // small CTA-wide scratch
-  uint8_t* slots;           // weight-stream slots, kSlots x kSlotBytes
-  uint64_t* full;           // one mbarrier per slot
-  int* cursor;              // producer state in shared memory: phase, next unit, issued
-  int consumed;             // chunks consumed so far (same on every thread)
-};
+enum { PH_A = 0, PH_B = 1, PH_O = 2, PH_C = 3, PH_N = 4 };
 
-__device__ __forceinline__ void grid_sync(Ctx& c) {
-  c.nbar += 1;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned long long target = c.base + (unsigned long long)c.nbar * c.G;
-    __threadfence();
-    atomicAdd(c.p.barrier, 1ull);
-    unsigned long long v = 0;
-    uint32_t it = 0;
-    while (true) {
-      asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(c.p.barrier) : "memory");
-      if (v >= target) break;
-      if (++it > kSpinLimit) {
-        atomicExch(c.p.status, DH_ERR_TIMEOUT);
-        break;
-      }
-      __nanosleep(32);
-    }
-    __threadfence();
-  }
-  __syncthreads();
+__device__ __forceinline__ void split_range(int n, int parts, int i, int& a, int& b) {
+  a = (int)((long long)n * i / parts);
+  b = (int)((long long)n * (i + 1) / parts);
 }
 
-__device__ __forceinline__ void split_range(int n, int G, int c, int& a, int& b) {
-  a = (int)((long long)n * c / G);
-  b = (int)((long long)n * (c + 1) / G);
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kCons) : "memory"); }
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
+__device__ __forceinline__ void red_release_u64(unsigned long long* p) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(p) : "memory");
+}
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // After this, lane l holds the warp-wide sum of v[l % NV] (NV a power of two <= 32).
 template <int NV>
@@ -96,242 +112,303 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[NV]) {
   return r;
 }
 
-// ------------------------------------------------------------------ input staging
-// xs[b][k] = bf16(x[b][k] * rsqrt(mean(x[b]^2) + eps) * w[k]) for the lockstep rows.
-// The rows are spread over all threads (one L2 round trip), squares are
-// summed per row with shared-memory atomics, and the values stay in registers.
-constexpr int kStageV = 16;  // float4 per thread: batch * K <= 16 * 1024
-template <int NV>  // float4 per thread, NV * 1024 >= batch * K
-__device__ __forceinline__ void stage_norm(Ctx& c, const float* x, const __nv_bfloat16* w, int K) {
-  const int B = c.p.batch, k4 = K / 4, n4 = B * k4;
-  float* ssum = c.red;  // [16]
-  if (threadIdx.x < 16) ssum[threadIdx.x] = 0.f;
-  __syncthreads();
+// ------------------------------------------------------------------ the plan
+// A segment is a run of equal units of one weight matrix (or of history rows)
+// that this CTA streams for one phase; chunks are whole units, <= one slot.
+enum { SEG_ROWS = 0, SEG_GATES = 1 };
+struct Seg {
+  const uint8_t* base;
+  uint32_t unit_bytes;  // SEG_GATES: bytes of one level's weights (3 gh bf16)
+  int units;
+  int kind;
+  size_t limit;         // bytes readable from base (the last unit may be short)
+};
+
+struct Ctx {
+  const dh_step_params& p;
+  int G, cta, NG, head;  // head >= 0 on head CTAs
+  int B, d, gh, L, H, hd, ff;
+  long long t;
+  unsigned long long gen;
+  uint32_t wait_limit;
+  int nsplit;            // attention splits per (row, head)
+  int lg;                // levels per gate chunk
+  int nslots;            // ring slots
+  // shared memory
+  uint8_t* slots;
+  uint64_t* full;
+  uint64_t* empty;
+  volatile int* abort;
+  __nv_bfloat16* xs;     // staged activation rows [MAXB][1024]
+  float* red;            // reductions
+  float* misc;           // small per-phase arrays
+  __nv_bfloat16* kv;     // [2][kKvPos][hd]
+  int consumed;          // chunks consumed (same in every consumer thread)
+};
+
+__device__ __forceinline__ const dh_layer_params& layer(const Ctx& c, int li) { return c.p.layers[li]; }
+
+// number of segments of (layer li, phase ph) for this CTA, and segment si
+__device__ int seg_count(const Ctx& c, int li, int ph) {
+  if (ph == PH_N) return 1;
+  const bool tree = layer(c, li).kind == 0;
+  if (c.head >= 0) return (tree && ph == PH_B) ? 2 : 0;
+  if (ph == PH_A || ph == PH_O) return (ph == PH_O && tree) ? 0 : 1;
+  if (ph == PH_C) return 2;
+  return 0;
+}
+
+__device__ Seg get_seg(const Ctx& c, int li, int ph, int si) {
+  Seg s{nullptr, 1, 0, SEG_ROWS, 0};
+  const int d = c.d;
+  if (ph == PH_N) {  // lm_head row pairs, split over every CTA
+    int u0, u1;
+    const int units = (c.p.vocab + 1) / 2;
+    split_range(units, c.G, c.cta, u0, u1);
+    s.base = static_cast<const uint8_t*>(c.p.emb) + (size_t)u0 * 4 * d;
+    s.unit_bytes = 4 * d;
+    s.units = u1 - u0;
+    s.limit = (size_t)c.p.vocab * d * 2 - (size_t)u0 * 4 * d;
+    return s;
+  }
+  const dh_layer_params& lp = layer(c, li);
+  if (c.head >= 0) {  // tree block B: gates (+ history rows), then the out-projection block
+    if (si == 0) {
+      s.base = static_cast<const uint8_t*>(lp.w_gates) + (size_t)c.head * c.L * 3 * c.gh * 2;
+      s.unit_bytes = 3 * c.gh * 2;
+      s.units = c.L;
+      s.kind = SEG_GATES;
+    } else {
+      s.base = static_cast<const uint8_t*>(lp.w_out) + (size_t)c.head * d * c.hd * 2;
+      s.unit_bytes = 32 * c.hd * 2;  // 32 output rows of this head's columns
+      s.units = d / 32;
+    }
+    s.limit = (size_t)s.units * s.unit_bytes;
+    return s;
+  }
+  const int gi = c.cta;
+  int u0, u1;
+  if (ph == PH_A || ph == PH_O) {  // row pairs of W3 / Wqkv / W_out
+    const int units = ph == PH_A ? 3 * d / 2 : d / 2;
+    split_range(units, c.NG, gi, u0, u1);
+    s.base = static_cast<const uint8_t*>(ph == PH_A ? lp.w_in3 : lp.w_out) + (size_t)u0 * 4 * d;
+    s.unit_bytes = 4 * d;
+  } else {  // PH_C: (gate, up) row pairs, then rows of Wd^T, for the same FFN slice
+    split_range(c.ff, c.NG, gi, u0, u1);
+    if (si == 0) {
+      s.base = static_cast<const uint8_t*>(lp.w_gu) + (size_t)u0 * 4 * d;
+      s.unit_bytes = 4 * d;
+    } else {
+      s.base = static_cast<const uint8_t*>(lp.w_down) + (size_t)u0 * 2 * d;
+      s.unit_bytes = 2 * d;
+    }
+  }
+  s.units = u1 - u0;
+  s.limit = (size_t)s.units * s.unit_bytes;
+  return s;
+}
+
+__device__ __forceinline__ int units_per_chunk(const Ctx& c, const Seg& s) {
+  if (s.kind == SEG_GATES) return c.lg;
+  const int n = kSlotBytes / (int)s.unit_bytes;
+  return n < 1 ? 1 : n;
+}
+
+// bytes of a gate chunk: levels [l0, l1) of weights, then the history rows
+// B_hist[b, t - 2^l] of those levels for every lockstep row
+__device__ __forceinline__ uint32_t gate_chunk_bytes(const Ctx& c, int l0, int l1) {
+  return (uint32_t)(l1 - l0) * 3 * c.gh * 2 + (uint32_t)(l1 - l0) * c.B * c.gh * 2;
+}
+
+// ------------------------------------------------------------------ producer
+// One lane walks the whole step's plan and keeps the ring full.
+__device__ void producer(Ctx& c) {
+  int slot = 0;
+  uint32_t eph = 0;
+  long issued = 0;
+  bool ok = true;
+  const int nl = c.p.n_layers;
+  for (int li = 0; li <= nl && ok; ++li) {
+    for (int ph = 0; ph < 5 && ok; ++ph) {
+      if ((li == nl) != (ph == PH_N)) continue;
+      const int ns = seg_count(c, li, ph);
+      for (int si = 0; si < ns && ok; ++si) {
+        const Seg s = get_seg(c, li, ph, si);
+        const int upc = units_per_chunk(c, s);
+        for (int u = 0; u < s.units && ok; u += upc) {
+          const int n = min(upc, s.units - u);
+          if (issued >= c.nslots && !mbar_wait(&c.empty[slot], eph ^ 1, c.p.status, c.wait_limit)) {
+            *c.abort = 1;
+          }
+          if (*c.abort) { ok = false; break; }
+          uint8_t* dst = c.slots + (size_t)slot * kSlotBytes;
+          if (s.kind == SEG_GATES) {
+            const dh_layer_params& lp = layer(c, li);
+            const uint32_t wbytes = (uint32_t)n * s.unit_bytes;
+            uint32_t total = wbytes;
+            for (int l = u; l < u + n; ++l)
+              if (c.t - (1ll << l) >= 0) total += (uint32_t)c.B * c.gh * 2;
+            mbar_arrive_expect_tx(&c.full[slot], total);
+            bulk_g2s(dst, s.base + (size_t)u * s.unit_bytes, wbytes, &c.full[slot]);
+            const __nv_bfloat16* bh = static_cast<const __nv_bfloat16*>(lp.b_hist);
+            for (int l = u; l < u + n; ++l) {
+              const long long src = c.t - (1ll << l);
+              if (src < 0) continue;
+              for (int b = 0; b < c.B; ++b)
+                bulk_g2s(dst + wbytes + ((size_t)(l - u) * c.B + b) * c.gh * 2,
+                         bh + ((size_t)b * c.p.max_len + src) * c.gh, (uint32_t)c.gh * 2,
+                         &c.full[slot]);
+            }
+          } else {
+            const size_t off = (size_t)u * s.unit_bytes;
+            size_t bytes = (size_t)n * s.unit_bytes;
+            if (off + bytes > s.limit) bytes = s.limit - off;
+            mbar_arrive_expect_tx(&c.full[slot], (uint32_t)bytes);
+            bulk_g2s(dst, s.base + off, (uint32_t)bytes, &c.full[slot]);
+          }
+          ++issued;
+          if (++slot == c.nslots) { slot = 0; eph ^= 1; }
+        }
+      }
+    }
+  }
+  // no copy may still be writing shared memory when the CTA exits
+  for (int s = 0; s < c.nslots; ++s) {
+    const long n_s = issued / c.nslots + (s < issued % c.nslots ? 1 : 0);
+    if (n_s > 0) mbar_wait(&c.full[s], (uint32_t)((n_s - 1) & 1), nullptr, kDrainLimit);
+  }
+}
+
+// ------------------------------------------------------------------ consumer helpers
+__device__ __forceinline__ const uint8_t* chunk_acquire(Ctx& c) {
+  const int slot = c.consumed % c.nslots;
+  if (!*c.abort) {
+    if (!mbar_wait(&c.full[slot], (uint32_t)((c.consumed / c.nslots) & 1), c.p.status, c.wait_limit))
+      *c.abort = 1;
+  }
+  return c.slots + (size_t)slot * kSlotBytes;
+}
+
+__device__ __forceinline__ void chunk_release(Ctx& c) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&c.empty[c.consumed % c.nslots]);
+  c.consumed += 1;
+}
+
+__device__ __forceinline__ unsigned long long* phase_ctr(const Ctx& c, int li, int ph) {
+  return c.p.barrier + (size_t)(1 + li * 5 + ph) * kSyncStride;
+}
+
+// all consumer threads: wait until `arrivals` CTAs have finished phase (li, ph)
+__device__ __forceinline__ void grid_wait(Ctx& c, int li, int ph, int arrivals) {
+  if (threadIdx.x == 0 && !*c.abort) {
+    const unsigned long long* ctr = phase_ctr(c, li, ph);
+    const unsigned long long target = (c.gen + 1) * (unsigned long long)arrivals;
+    // each poll is an L2 round trip (~1 us): 1/32 of the mbarrier poll limit
+    // (2^21 polls, about two seconds, at the default)
+    const uint32_t limit = c.wait_limit >> 5;
+    uint32_t it = 0;
+    while (ld_acquire_u64(ctr) < target) {
+      if (++it > limit) {
+        atomicExch(c.p.status, DH_ERR_TIMEOUT);
+        *c.abort = 1;
+        break;
+      }
+    }
+  }
+  csync();
+}
+
+// all consumer threads: this CTA has finished phase (li, ph)
+__device__ __forceinline__ void grid_arrive(Ctx& c, int li, int ph) {
+  csync();
+  if (threadIdx.x == 0) red_release_u64(phase_ctr(c, li, ph));
+}
+
+// xs[b][k] = bf16(x[b][k] * rsqrt(mean(x[b]^2) + eps) * w[k]) for every lockstep row;
+// x comes from `xf` (fp32, read through L2) or, for the first block, from the
+// embedding rows of the step's tokens
+template <int MAXB>
+__device__ void stage_norm(Ctx& c, const float* xf, const __nv_bfloat16* w) {
+  const int B = c.B, d = c.d, d4 = d / 4, n4 = B * d4;
+  constexpr int NV = (MAXB * 1024 + kCons * 4 - 1) / (kCons * 4);
+  float* ssum = c.red;  // [MAXB]
+  if (threadIdx.x < MAXB) ssum[threadIdx.x] = 0.f;
+  csync();
   float4 v[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const int i = threadIdx.x + j * kThreads;
+    const int i = threadIdx.x + j * kCons;
     float sq = 0.f;
     if (i < n4) {
-      v[j] = __ldcg(reinterpret_cast<const float4*>(x) + i);
+      const int b = i / d4, k = (i - b * d4) * 4;
+      if (xf) {
+        v[j] = __ldcg(reinterpret_cast<const float4*>(xf + (size_t)b * d + k));
+      } else {
+        long long tok = c.p.tokens[b];
+        if (tok < 0 || tok >= c.p.vocab) tok = 0;  // reported by the embedding writer
+        const uint2 e = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(c.p.emb) +
+                                                        (size_t)tok * d + k);
+        const float2 e01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e.x));
+        const float2 e23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e.y));
+        v[j] = make_float4(e01.x, e01.y, e23.x, e23.y);
+      }
       sq = v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
     }
-    if ((k4 & 31) == 0) {  // a warp's 32 float4 lie in one row: reduce, one atomic
+    if ((d4 & 31) == 0) {  // a warp's 32 float4 lie in one row: reduce, one atomic
       sq = warp_sum(sq);
-      if ((threadIdx.x & 31) == 0 && i < n4) atomicAdd(&ssum[i / k4], sq);
+      if ((threadIdx.x & 31) == 0 && i < n4) atomicAdd(&ssum[i / d4], sq);
     } else if (i < n4) {
-      atomicAdd(&ssum[i / k4], sq);
+      atomicAdd(&ssum[i / d4], sq);
     }
   }
-  __syncthreads();
+  csync();
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const int i = threadIdx.x + j * kThreads;
+    const int i = threadIdx.x + j * kCons;
     if (i < n4) {
-      const int b = i / k4, k = (i - b * k4) * 4;
-      const float r = rsqrtf(ssum[b] / (float)K + kEps);
+      const int b = i / d4, k = (i - b * d4) * 4;
+      const float r = rsqrtf(ssum[b] / (float)d + kEps);
       const uint2 wv = *reinterpret_cast<const uint2*>(w + k);
       const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.x));
       const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.y));
       uint2 pk;
       pk.x = pack2(v[j].x * r * w01.x, v[j].y * r * w01.y);
       pk.y = pack2(v[j].z * r * w23.x, v[j].w * r * w23.y);
-      *reinterpret_cast<uint2*>(c.xs + (size_t)b * K + k) = pk;
+      *reinterpret_cast<uint2*>(c.xs + (size_t)b * 1024 + k) = pk;
     }
   }
-  __syncthreads();
+  csync();
 }
 
-// xs = src (bf16, batch rows of K)
-__device__ __forceinline__ void stage_copy(Ctx& c, const __nv_bfloat16* src, int K) {
-  const int n = c.p.batch * K / 8;
-  const uint4* s4 = reinterpret_cast<const uint4*>(src);
-  uint4* d4 = reinterpret_cast<uint4*>(c.xs);
-  for (int i0 = threadIdx.x; i0 < n; i0 += 8 * kThreads) {  // 8 loads in flight per thread
-    uint4 v[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int i = i0 + j * kThreads;
-      if (i < n) v[j] = __ldcg(s4 + i);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int i = i0 + j * kThreads;
-      if (i < n) d4[i] = v[j];
-    }
+// xs[b][0:K] = src[b][0:K] (bf16 produced by another CTA)
+__device__ void stage_copy(Ctx& c, const __nv_bfloat16* src, int K) {
+  const int k8 = K / 8, n = c.B * k8;
+  for (int i = threadIdx.x; i < n; i += kCons) {
+    const int b = i / k8, k = (i - b * k8) * 8;
+    *reinterpret_cast<uint4*>(c.xs + (size_t)b * 1024 + k) =
+        __ldcg(reinterpret_cast<const uint4*>(src + (size_t)b * K + k));
   }
-  __syncthreads();
+  csync();
 }
 
-// ------------------------------------------------------------------ weight stream
-// Phase pi (0 .. 5*n_layers) of a step: per block 0 = input projection, 1 =
-// mixer gates (tree) / attention (no weights), 2 = output projection, 3 = FFN
-// input (gate/up pairs), 4 = FFN down; the last phase is the logits.  A unit
-// is the smallest contiguous weight piece one warp consumes.
-struct PhaseW {
-  const uint8_t* base;
-  int unit_bytes, units;
-  size_t total;  // bytes of the whole matrix (the last unit may be short)
-};
-
-__device__ PhaseW phase_weights(const dh_step_params& p, int pi) {
-  const int d = p.d, nl = p.n_layers;
-  PhaseW w{nullptr, 1, 0, 0};
-  if (pi >= 5 * nl) {
-    w.base = static_cast<const uint8_t*>(p.emb);
-    w.unit_bytes = 4 * d;
-    w.units = (p.vocab + 1) / 2;
-    w.total = (size_t)p.vocab * d * 2;
-    return w;
-  }
-  const dh_layer_params& lp = p.layers[pi / 5];
-  switch (pi % 5) {
-    case 0: w.base = static_cast<const uint8_t*>(lp.w_in3); w.unit_bytes = 4 * d; w.units = 3 * d / 2; break;
-    case 1:
-      if (lp.kind == 0) {
-        w.base = static_cast<const uint8_t*>(lp.w_gates);
-        w.unit_bytes = 6 * d;
-        w.units = p.L * p.H;
-      }
-      break;
-    case 2: w.base = static_cast<const uint8_t*>(lp.w_out); w.unit_bytes = 4 * d; w.units = d / 2; break;
-    case 3: w.base = static_cast<const uint8_t*>(lp.w_gu); w.unit_bytes = 4 * d; w.units = p.ff; break;
-    default: w.base = static_cast<const uint8_t*>(lp.w_down); w.unit_bytes = 4 * p.ff; w.units = d / 2; break;
-  }
-  w.total = (size_t)w.units * w.unit_bytes;
-  return w;
-}
-
-__device__ __forceinline__ int units_per_chunk(int unit_bytes) {
-  int n = kSlotBytes / unit_bytes;
-  if (n >= kWarps) n -= n % kWarps;  // whole rounds of warps
-  return n < 1 ? 1 : n;
-}
-
-__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
-                                              uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Issue the next chunk of this CTA's weight stream (called by thread 0 only,
-// each time a slot is free).  Returns false when the stream is exhausted.
-__device__ bool issue_next(Ctx& c) {
-  int pi = c.cursor[0], u = c.cursor[1];
-  const int np = 5 * c.p.n_layers + 1;
-  while (pi < np) {
-    const PhaseW w = phase_weights(c.p, pi);
-    int u0, u1;
-    split_range(w.units, c.G, c.cta, u0, u1);
-    if (u < u0) u = u0;
-    if (u < u1) {
-      const int n = min(units_per_chunk(w.unit_bytes), u1 - u);
-      const size_t off = (size_t)u * w.unit_bytes;
-      size_t bytes = (size_t)n * w.unit_bytes;
-      if (off + bytes > w.total) bytes = w.total - off;
-      const int slot = c.cursor[2] % kSlots;
-      mbar_arrive_expect_tx(&c.full[slot], (uint32_t)bytes);
-      bulk_copy_g2s(c.slots + (size_t)slot * kSlotBytes, w.base + off, (uint32_t)bytes,
-                    &c.full[slot]);
-      c.cursor[0] = pi;
-      c.cursor[1] = u + n;
-      c.cursor[2] += 1;
-      return true;
-    }
-    ++pi;
-    u = 0;
-  }
-  c.cursor[0] = pi;
-  c.cursor[1] = 0;
-  return false;
-}
-
-// Consumer side: wait for the next chunk; returns its shared-memory base.
-__device__ __forceinline__ const uint8_t* chunk_wait(Ctx& c) {
-  const int slot = c.consumed % kSlots;
-  mbar_wait(&c.full[slot], (uint32_t)((c.consumed / kSlots) & 1), c.p.status, 1u << 22);
-  return c.slots + (size_t)slot * kSlotBytes;
-}
-
-// All threads are done with the current chunk: refill its slot.
-__device__ __forceinline__ void chunk_release(Ctx& c) {
-  __syncthreads();
-  if (threadIdx.x == 0) issue_next(c);
-  c.consumed += 1;
-}
-
-// ------------------------------------------------------------------ GEMV phases
-enum { E_MIXIN = 0, E_QKV = 1, E_RESID = 2, E_FFNIN = 3, E_LOGITS = 4 };
-
-struct GemvPhase {
-  int epi;
-  int K;                        // input width
-  int N;                        // output rows of the weight (RESID / LOGITS)
-  const __nv_bfloat16* norm_w;  // staging: RMSNorm of x with this weight, or
-  const __nv_bfloat16* src;     // staging: copy this bf16 (batch, K) buffer
-  float* x;                     // residual stream (RESID)
-  __nv_bfloat16 *o0, *o1, *o2;  // outputs (see store_unit)
-};
-
-// value v of output row `row` (0/1) of unit u for batch row b; `other` is the
-// partner row's value (SwiGLU and RoPE pairs)
-__device__ __forceinline__ void store_unit(const Ctx& c, const GemvPhase& g, int u, int b, int row,
-                                           float v, float other, bool has1) {
-  const int d = c.p.d;
-  switch (g.epi) {
-    case E_MIXIN: {  // [W_in; W1x; W1s] -> v0, A, B_hist[:, t]
-      const int n = 2 * u + row, seg = n / d, col = n - seg * d;
-      if (seg == 0) g.o0[(size_t)b * d + col] = f2bf(v);
-      else if (seg == 1) g.o1[(size_t)b * d + col] = f2bf(v);
-      else g.o2[((size_t)b * c.p.max_len + c.t) * d + col] = f2bf(v);
-      break;
-    }
-    case E_QKV: {  // [Wq; Wk; Wv], RoPE at t on q and k; k, v into the caches
-      const int n = 2 * u + row, seg = n / d, col = n - seg * d, hd = c.p.hd;
-      float out = v;
-      if (seg < 2) {
-        const int j = (col % hd) >> 1;
-        const float cs = c.p.rope_cos[c.t * (hd / 2) + j], sn = c.p.rope_sin[c.t * (hd / 2) + j];
-        const float x1 = row == 0 ? v : other, x2 = row == 0 ? other : v;
-        out = row == 0 ? (x1 * cs - x2 * sn) : (x1 * sn + x2 * cs);
-      }
-      if (seg == 0) g.o0[(size_t)b * d + col] = f2bf(out);
-      else if (seg == 1) g.o1[((size_t)b * c.p.max_len + c.t) * d + col] = f2bf(out);
-      else g.o2[((size_t)b * c.p.max_len + c.t) * d + col] = f2bf(out);
-      break;
-    }
-    case E_RESID: {  // x += W . input (this CTA owns these rows)
-      float* p = g.x + (size_t)b * g.N + 2 * u + row;
-      *p = __ldcg(p) + v;
-      break;
-    }
-    case E_FFNIN:  // unit j = (gate_j, up_j): u_j = silu(g) * up
-      if (row == 0) g.o0[(size_t)b * c.p.ff + u] = f2bf(v / (1.0f + expf(-v)) * other);
-      break;
-    default:  // logits
-      if (row == 1 && !has1) break;
-      g.o0[(size_t)b * g.N + 2 * u + row] = f2bf(v);
-  }
-}
-
+// acc[0..MAXB) += row r0 . xs[b], acc[MAXB..2MAXB) += row r1 . xs[b]  (this lane's k slice)
 template <int MAXB>
-__device__ __forceinline__ void dot_pair_smem(const __nv_bfloat16* r0, const __nv_bfloat16* r1,
-                                              int K, const __nv_bfloat16* xs, int batch,
-                                              float (&acc)[2 * MAXB]) {
+__device__ __forceinline__ void dot_pair(const __nv_bfloat16* r0, const __nv_bfloat16* r1, int K,
+                                         const __nv_bfloat16* xs, int B, float (&acc)[2 * MAXB]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int i = 0; i < 2 * MAXB; ++i) acc[i] = 0.f;
+#pragma unroll 2
   for (int k = lane * 8; k < K; k += 256) {
     float fa[8], fb[8];
     unpack8(*reinterpret_cast<const uint4*>(r0 + k), fa);
     unpack8(*reinterpret_cast<const uint4*>(r1 + k), fb);
 #pragma unroll
     for (int b = 0; b < MAXB; ++b) {
-      if (b < batch) {
+      if (b < B) {
         float fx[8];
-        unpack8(*reinterpret_cast<const uint4*>(xs + (size_t)b * K + k), fx);
+        unpack8(*reinterpret_cast<const uint4*>(xs + (size_t)b * 1024 + k), fx);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           acc[b] = fmaf(fa[j], fx[j], acc[b]);
@@ -342,216 +419,337 @@ __device__ __forceinline__ void dot_pair_smem(const __nv_bfloat16* r0, const __n
   }
 }
 
-// grid barrier, stage the input, then consume this CTA's chunks of phase pi
-template <int MAXB>
-__device__ __noinline__ void gemv_phase(Ctx& c, int pi, const GemvPhase& g) {
+// Consume segment `s` (row pairs of a K-wide matrix) against xs; `store(u, b,
+// row, v, other, has1)` receives unit u's row `row` for lockstep row b.
+template <int MAXB, class Store>
+__device__ void gemv_segment(Ctx& c, const Seg& s, int K, int unit0, Store store) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const PhaseW w = phase_weights(c.p, pi);
-  int u0, u1;
-  split_range(w.units, c.G, c.cta, u0, u1);
-  grid_sync(c);
-  if (g.norm_w) stage_norm<MAXB>(c, c.p.x, g.norm_w, g.K);
-  else stage_copy(c, g.src, g.K);
-  const int upc = units_per_chunk(w.unit_bytes);
-  for (int cu0 = u0; cu0 < u1; cu0 += upc) {
-    const int cu1 = min(cu0 + upc, u1);
-    const uint8_t* chunk = chunk_wait(c);
-    for (int u = cu0 + warp; u < cu1; u += kWarps) {
-      const __nv_bfloat16* r0 =
-          reinterpret_cast<const __nv_bfloat16*>(chunk + (size_t)(u - cu0) * w.unit_bytes);
-      const bool has1 = (size_t)(u + 1) * w.unit_bytes <= w.total;
-      const __nv_bfloat16* r1 = has1 ? r0 + g.K : r0;
+  const int upc = units_per_chunk(c, s);
+  for (int cu = 0; cu < s.units; cu += upc) {
+    const int n = min(upc, s.units - cu);
+    const uint8_t* chunk = chunk_acquire(c);
+    for (int u = warp; u < n; u += kWarps) {
+      const size_t off = (size_t)(cu + u) * s.unit_bytes;
+      const __nv_bfloat16* r0 = reinterpret_cast<const __nv_bfloat16*>(chunk + (size_t)u * s.unit_bytes);
+      const bool has1 = off + s.unit_bytes <= s.limit;
+      const __nv_bfloat16* r1 = has1 ? r0 + K : r0;
       float acc[2 * MAXB];
-      dot_pair_smem<MAXB>(r0, r1, g.K, c.xs, c.p.batch, acc);
+      dot_pair<MAXB>(r0, r1, K, c.xs, c.B, acc);
       const float r = transpose_reduce<2 * MAXB>(acc);
       const float other = __shfl_xor_sync(0xffffffffu, r, MAXB);
       const int b = lane % MAXB, row = (lane / MAXB) & 1;
-      if (lane < 2 * MAXB && b < c.p.batch) store_unit(c, g, u, b, row, r, other, has1);
+      if (lane < 2 * MAXB && b < c.B && (row == 0 || has1)) store(unit0 + cu + u, b, row, r, other);
     }
     chunk_release(c);
   }
 }
 
-// ------------------------------------------------------------------ tree phase
-// Items (level, head); the two 128-thread halves of the CTA take alternate
-// items of each chunk.  Each item: the three gate readouts of every lockstep
-// row (fused_step.py:26-59), then the last CTA to finish a head runs that
-// head's level recurrence (fused_step.py:62-88, fp32 state).
+// ------------------------------------------------------------------ phases
 template <int MAXB>
-__device__ __noinline__ void tree_phase(Ctx& c, int pi, const dh_layer_params& lp) {
-  const int L = c.p.L, H = c.p.H, hd = c.p.hd, gh = c.p.d, d = H * hd, B = c.p.batch;
-  const int S = (1 << (L + 1)) - 2;
-  const int half = threadIdx.x >> 7, gt = threadIdx.x & 127, hw = gt >> 5, lane = threadIdx.x & 31;
-  const PhaseW w = phase_weights(c.p, pi);
-  int i0, i1;
-  split_range(w.units, c.G, c.cta, i0, i1);
-  const __nv_bfloat16* a_in = static_cast<const __nv_bfloat16*>(c.p.a);
-  const __nv_bfloat16* bh = static_cast<const __nv_bfloat16*>(lp.b_hist);
-  __nv_bfloat16* rg = static_cast<__nv_bfloat16*>(lp.rg_hist);
-  __nv_bfloat16* ring = static_cast<__nv_bfloat16*>(lp.v_ring);
-  const __nv_bfloat16* v0 = static_cast<const __nv_bfloat16*>(c.p.v0);
-  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(c.p.y);
-  float* red = c.red + 16 + half * (4 * 3 * 16 + 8);  // [4 warps][3*16] + flag
-  int* flag = reinterpret_cast<int*>(red + 4 * 3 * 16);
+__device__ void phase_a(Ctx& c, int li) {
+  const dh_layer_params& lp = layer(c, li);
+  const bool tree = lp.kind == 0;
+  const int d = c.d, B = c.B;
+  if (li > 0) grid_wait(c, li - 1, PH_C, c.NG);
+  // the residual: layer 0 starts it from the embedding rows; a tree block
+  // copies its accumulated value into xa (the input of C, which B adds into)
+  {
+    int e0, e1;
+    split_range(B * d / 4, c.NG, c.cta, e0, e1);
+    for (int i = e0 + threadIdx.x; i < e1; i += kCons) {
+      const int b = i / (d / 4), k = (i - b * (d / 4)) * 4;
+      float4 v;
+      if (li == 0) {
+        long long tok = c.p.tokens[b];
+        if (tok < 0 || tok >= c.p.vocab) {
+          atomicExch(c.p.status, DH_ERR_ARG);
+          tok = 0;
+        }
+        const uint2 e = *reinterpret_cast<const uint2*>(
+            static_cast<const __nv_bfloat16*>(c.p.emb) + (size_t)tok * d + k);
+        const float2 e01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e.x));
+        const float2 e23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e.y));
+        v = make_float4(e01.x, e01.y, e23.x, e23.y);
+        *reinterpret_cast<float4*>(c.p.x + (size_t)b * d + k) = v;
+      } else if (tree) {
+        v = __ldcg(reinterpret_cast<const float4*>(c.p.x + (size_t)b * d + k));
+      } else {
+        continue;
+      }
+      *reinterpret_cast<float4*>(c.p.x_in + (size_t)b * d + k) = v;
+    }
+  }
+  stage_norm<MAXB>(c, li == 0 ? nullptr : c.p.x, static_cast<const __nv_bfloat16*>(lp.norm1));
+  const Seg s = get_seg(c, li, PH_A, 0);
+  int u0, u1;
+  split_range(3 * d / 2, c.NG, c.cta, u0, u1);
   const long long t = c.t;
-  grid_sync(c);
-  const int upc = units_per_chunk(w.unit_bytes);
-  for (int cu0 = i0; cu0 < i1; cu0 += upc) {
-    const int cu1 = min(cu0 + upc, i1);
-    const uint8_t* chunk = chunk_wait(c);
-    for (int item = cu0 + half; item < cu1; item += 2) {
-      const int l = item / H, h = item - l * H;
-      const long long src = t - (1ll << l);
-      const bool ok = src >= 0;
-      const long long srcc = ok ? src : 0;
-      const __nv_bfloat16* wi =
-          reinterpret_cast<const __nv_bfloat16*>(chunk + (size_t)(item - cu0) * w.unit_bytes);
-      float acc[MAXB][3];
+  if (tree) {
+    __nv_bfloat16* v0 = static_cast<__nv_bfloat16*>(c.p.v0);
+    __nv_bfloat16* a = static_cast<__nv_bfloat16*>(c.p.a);
+    __nv_bfloat16* bh = static_cast<__nv_bfloat16*>(lp.b_hist);
+    const int ml = c.p.max_len;
+    gemv_segment<MAXB>(c, s, d, u0, [&](int u, int b, int row, float v, float) {
+      const int n = 2 * u + row, seg = n / d, col = n - seg * d;
+      if (seg == 0) v0[(size_t)b * d + col] = f2bf(v);
+      else if (seg == 1) a[(size_t)b * d + col] = f2bf(v);
+      else bh[((size_t)b * ml + t) * d + col] = f2bf(v);
+    });
+  } else {
+    __nv_bfloat16* q = static_cast<__nv_bfloat16*>(c.p.q);
+    __nv_bfloat16* kc = static_cast<__nv_bfloat16*>(lp.k_cache);
+    __nv_bfloat16* vc = static_cast<__nv_bfloat16*>(lp.v_cache);
+    const int ml = c.p.max_len, hd = c.hd;
+    const float* cosT = c.p.rope_cos;
+    const float* sinT = c.p.rope_sin;
+    gemv_segment<MAXB>(c, s, d, u0, [&](int u, int b, int row, float v, float other) {
+      const int n = 2 * u + row, seg = n / d, col = n - seg * d;
+      float out = v;
+      if (seg < 2) {  // rotate the pair (2j, 2j+1) of q and k at position t
+        const int j = (col % hd) >> 1;
+        const float cs = cosT[t * (hd / 2) + j], sn = sinT[t * (hd / 2) + j];
+        const float x1 = row == 0 ? v : other, x2 = row == 0 ? other : v;
+        out = row == 0 ? (x1 * cs - x2 * sn) : (x1 * sn + x2 * cs);
+      }
+      if (seg == 0) q[(size_t)b * d + col] = f2bf(out);
+      else if (seg == 1) kc[((size_t)b * ml + t) * d + col] = f2bf(out);
+      else vc[((size_t)b * ml + t) * d + col] = f2bf(out);
+    });
+  }
+  grid_arrive(c, li, PH_A);
+}
+
+// head CTA: gates of every level, level recurrence, out-projection share
+template <int MAXB>
+__device__ void phase_b_tree(Ctx& c, int li) {
+  const dh_layer_params& lp = layer(c, li);
+  const int B = c.B, L = c.L, H = c.H, hd = c.hd, gh = c.gh, d = c.d, h = c.head;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long t = c.t;
+  const int ml = c.p.max_len;
+  const int S = (1 << (L + 1)) - 2;
+  __nv_bfloat16* ring = static_cast<__nv_bfloat16*>(lp.v_ring);
+  __nv_bfloat16* rg = static_cast<__nv_bfloat16*>(lp.rg_hist);
+  // small arrays in c.misc
+  float* s_f = c.misc;                        // [MAXB][kLmax]
+  float* s_c = s_f + MAXB * kLmax;            // [MAXB][kLmax]
+  float* s_rg = s_c + MAXB * kLmax;           // [MAXB][kLmax] transmit gate at the source
+  float* s_y = s_rg + MAXB * kLmax;           // [MAXB][64]
+  __nv_bfloat16* s_ring = reinterpret_cast<__nv_bfloat16*>(s_y + MAXB * 64);  // [MAXB][kLmax][64]
+  // history written by earlier steps: ring slots of the source positions and
+  // their transmit gates (one round trip, before the wait)
+  for (int i = tid; i < B * L * 8; i += kCons) {
+    const int b = i / (L * 8), r = i - b * (L * 8), l = r / 8, g = r - l * 8;
+    const long long src = t - (1ll << l);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (src >= 0) {
+      const long long slot = ((2ll << l) - 2) + (src & ((2ll << l) - 1));
+      v = *reinterpret_cast<const uint4*>(ring + ((size_t)b * S + slot) * d + h * hd + g * 8);
+    }
+    *reinterpret_cast<uint4*>(s_ring + ((size_t)b * kLmax + l) * 64 + g * 8) = v;
+    if (g == 0)
+      s_rg[b * kLmax + l] = src >= 0 ? bf2f(rg[(((size_t)b * ml + src) * L + l) * H + h]) : 0.f;
+  }
+  grid_wait(c, li, PH_A, c.NG);
+  stage_copy(c, static_cast<const __nv_bfloat16*>(c.p.a), gh);
+  // gate readouts: thread tid owns columns [4 tid, 4 tid + 4) of the hidden
+  // width for every level and row; per chunk, partial sums of its levels are
+  // reduced across the warp (transpose reduction) into red[warp][...]
+  float* red = c.red;  // [kWarps][MAXB][kLmax * 3]
+  const int k = tid * 4;
+  const bool kin = k < gh;
+  float av[MAXB][4];
 #pragma unroll
-      for (int b = 0; b < MAXB; ++b) acc[b][0] = acc[b][1] = acc[b][2] = 0.f;
-      for (int k = gt * 8; k < gh; k += 1024) {
-        float fw[3][8];
+  for (int b = 0; b < MAXB; ++b) {
+    if (b < B && kin) {
+      const uint2 u = *reinterpret_cast<const uint2*>(c.xs + (size_t)b * 1024 + k);
+      const float2 a01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      const float2 a23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+      av[b][0] = a01.x; av[b][1] = a01.y; av[b][2] = a23.x; av[b][3] = a23.y;
+    } else {
+      av[b][0] = av[b][1] = av[b][2] = av[b][3] = 0.f;
+    }
+  }
+  const Seg sg = get_seg(c, li, PH_B, 0);
+  for (int l0 = 0; l0 < L; l0 += c.lg) {
+    const int l1 = min(L, l0 + c.lg);
+    const uint8_t* chunk = chunk_acquire(c);
+    const uint32_t wbytes = (uint32_t)(l1 - l0) * sg.unit_bytes;
+    for (int l = l0; l < l1; ++l) {
+      const bool ok = t - (1ll << l) >= 0;
+      const __nv_bfloat16* wl = reinterpret_cast<const __nv_bfloat16*>(chunk + (size_t)(l - l0) * sg.unit_bytes);
+      float w3[3][4];
 #pragma unroll
-        for (int g = 0; g < 3; ++g) unpack8(*reinterpret_cast<const uint4*>(wi + (size_t)g * gh + k), fw[g]);
-#pragma unroll
-        for (int b = 0; b < MAXB; ++b) {
-          if (b < B) {
-            float fa[8], fs[8];
-            unpack8(__ldcg(reinterpret_cast<const uint4*>(a_in + (size_t)b * gh + k)), fa);
-            if (ok) {
-              unpack8(__ldcg(reinterpret_cast<const uint4*>(bh + ((size_t)b * c.p.max_len + srcc) * gh + k)), fs);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) fs[j] = 0.f;
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float hv = fmaxf(fa[j] + fs[j], 0.f);
-              hv *= hv;  // relu squared
-              acc[b][0] = fmaf(fw[0][j], hv, acc[b][0]);
-              acc[b][1] = fmaf(fw[1][j], hv, acc[b][1]);
-              acc[b][2] = fmaf(fw[2][j], hv, acc[b][2]);
-            }
-          }
+      for (int g = 0; g < 3; ++g) {
+        uint2 u = kin ? *reinterpret_cast<const uint2*>(wl + (size_t)g * gh + k) : make_uint2(0, 0);
+        const float2 x01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 x23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        w3[g][0] = x01.x; w3[g][1] = x01.y; w3[g][2] = x23.x; w3[g][3] = x23.y;
+      }
+      for (int b = 0; b < B; ++b) {
+        float bs[4] = {0.f, 0.f, 0.f, 0.f};
+        if (ok && kin) {
+          const uint2 u = *reinterpret_cast<const uint2*>(
+              chunk + wbytes + (((size_t)(l - l0) * B + b) * gh + k) * 2);
+          const float2 b01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+          const float2 b23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+          bs[0] = b01.x; bs[1] = b01.y; bs[2] = b23.x; bs[3] = b23.y;
         }
-      }
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};  // i, f, r, (pad)
 #pragma unroll
-      for (int b = 0; b < MAXB; ++b) {
-#pragma unroll
-        for (int g = 0; g < 3; ++g) {
-          const float v = warp_sum(acc[b][g]);
-          if (lane == 0 && b < B) red[hw * 48 + b * 3 + g] = v;
+        for (int j = 0; j < 4; ++j) {
+          float hv = fmaxf(av[b][j] + bs[j], 0.f);
+          hv *= hv;  // relu squared
+          acc[0] = fmaf(w3[0][j], hv, acc[0]);
+          acc[1] = fmaf(w3[1][j], hv, acc[1]);
+          acc[2] = fmaf(w3[2][j], hv, acc[2]);
         }
+        const float r = transpose_reduce<4>(acc);
+        if (lane < 3) red[((size_t)warp * MAXB + b) * (kLmax * 3) + l * 3 + lane] = r;
       }
-      asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
-      if (gt < B) {
-        const int b = gt;
-        float pre[3];
-#pragma unroll
-        for (int g = 0; g < 3; ++g)
-          pre[g] = red[b * 3 + g] + red[48 + b * 3 + g] + red[96 + b * 3 + g] + red[144 + b * 3 + g];
-        const float* bg = lp.b_gates + (size_t)item * 3;
-        const float okf = ok ? 1.f : 0.f;
-        c.p.ig[((size_t)b * L + l) * H + h] = sigmoidf_(pre[0] + bg[0]) * okf;
-        c.p.fg[((size_t)b * L + l) * H + h] = sigmoidf_(pre[1] + bg[1]) * okf + (1.f - okf);
-        rg[(((size_t)b * c.p.max_len + t) * L + l) * H + h] = f2bf(sigmoidf_(pre[2] + bg[2]));
-        __threadfence();
-      }
-      asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
-      if (gt == 0) *flag = (atomicAdd(&c.p.counters[h], 1) == L - 1);
-      asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
-      if (*flag) {
-        __threadfence();
-        const int groups = hd / 8;
-        if (gt < B * groups) {
-          const int b = gt / groups;
-          const int c0 = h * hd + (gt - b * groups) * 8;
-          __nv_bfloat16* ringb = ring + (size_t)b * S * d;
-          uint4 vsrc[16];
-          float coef[16], fgv[16];
-#pragma unroll
-          for (int lv = 0; lv < 16; ++lv) {
-            if (lv < L) {
-              const long long s = t - (1ll << lv);
-              fgv[lv] = __ldcg(c.p.fg + ((size_t)b * L + lv) * H + h);
-              coef[lv] = 0.f;
-              vsrc[lv] = make_uint4(0, 0, 0, 0);
-              if (s >= 0) {
-                const float igv = __ldcg(c.p.ig + ((size_t)b * L + lv) * H + h);
-                const float rgv = bf2f(rg[(((size_t)b * c.p.max_len + s) * L + lv) * H + h]);
-                coef[lv] = igv * rgv;
-                const long long slot = ((2ll << lv) - 2) + (s & ((2ll << lv) - 1));
-                vsrc[lv] = __ldcg(reinterpret_cast<const uint4*>(ringb + (size_t)slot * d + c0));
-              }
-            }
-          }
-          float V[8];
-          const uint4 v0v = __ldcg(reinterpret_cast<const uint4*>(v0 + (size_t)b * d + c0));
-          unpack8(v0v, V);
-          *reinterpret_cast<uint4*>(ringb + (size_t)(t & 1) * d + c0) = v0v;
-#pragma unroll
-          for (int lv = 0; lv < 16; ++lv) {
-            if (lv < L) {
-              float vs[8];
-              unpack8(vsrc[lv], vs);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) V[j] = fgv[lv] * V[j] + coef[lv] * vs[j];
-              if (lv + 1 < L) {
-                const long long slot = ((2ll << (lv + 1)) - 2) + (t & ((2ll << (lv + 1)) - 1));
-                *reinterpret_cast<uint4*>(ringb + (size_t)slot * d + c0) = pack8(V);
-              }
-            }
-          }
-          *reinterpret_cast<uint4*>(y + (size_t)b * d + c0) = pack8(V);
-        }
-        if (gt == 0) c.p.counters[h] = 0;
-      }
-      asm volatile("bar.sync %0, 128;" ::"r"(1 + half) : "memory");
     }
     chunk_release(c);
   }
+  csync();
+  // sigmoid gates; transmit gate of position t into rg_hist
+  for (int i = tid; i < B * L; i += kCons) {
+    const int b = i / L, l = i - b * L;
+    float pre[3];
+#pragma unroll
+    for (int g = 0; g < 3; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) s += red[((size_t)w * MAXB + b) * (kLmax * 3) + l * 3 + g];
+      pre[g] = s + lp.b_gates[((size_t)h * L + l) * 3 + g];
+    }
+    const float okf = t - (1ll << l) >= 0 ? 1.f : 0.f;
+    const float ig = sigmoidf_(pre[0]) * okf;
+    const float fg = sigmoidf_(pre[1]) * okf + (1.f - okf);
+    const float rgt = sigmoidf_(pre[2]);
+    rg[(((size_t)b * ml + t) * L + l) * H + h] = f2bf(rgt);
+    s_f[b * kLmax + l] = fg;
+    s_c[b * kLmax + l] = ig * s_rg[b * kLmax + l];
+  }
+  csync();
+  // level recurrence (fp32 state, every level's value stored into its ring)
+  for (int i = tid; i < B * (hd / 8); i += kCons) {
+    const int b = i / (hd / 8), g = i - b * (hd / 8);
+    const int c0 = h * hd + g * 8;
+    __nv_bfloat16* ringb = ring + (size_t)b * S * d;
+    float V[8];
+    const uint4 v0 = __ldcg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(c.p.v0) +
+                                                          (size_t)b * d + c0));
+    unpack8(v0, V);
+    *reinterpret_cast<uint4*>(ringb + (size_t)(t & 1) * d + c0) = v0;  // ring 0 at t
+    for (int l = 0; l < L; ++l) {
+      float vs[8];
+      unpack8(*reinterpret_cast<const uint4*>(s_ring + ((size_t)b * kLmax + l) * 64 + g * 8), vs);
+      const float f = s_f[b * kLmax + l], cc = s_c[b * kLmax + l];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) V[j] = f * V[j] + cc * vs[j];
+      if (l + 1 < L) {
+        const long long slot = ((2ll << (l + 1)) - 2) + (t & ((2ll << (l + 1)) - 1));
+        *reinterpret_cast<uint4*>(ringb + (size_t)slot * d + c0) = pack8(V);
+      }
+    }
+    const uint4 yv = pack8(V);
+    float yr[8];
+    unpack8(yv, yr);  // y is bf16, as the reference's
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s_y[b * 64 + g * 8 + j] = yr[j];
+  }
+  csync();
+  // out-projection share: x[b, n] += sum_c W_out[n, h*hd + c] y_h[b, c] for every n,
+  // added into both residual buffers; 8 lanes per row (8 channels each), a
+  // warp covers 4 rows per pass, lane 0 issues one 4-wide reduction
+  const Seg so = get_seg(c, li, PH_B, 1);
+  const int upc = units_per_chunk(c, so);
+  const int cg = lane & 7, rsub = lane >> 3;
+  for (int cu = 0; cu < so.units; cu += upc) {
+    const int nrows = min(upc, so.units - cu) * 32;
+    const uint8_t* chunk = chunk_acquire(c);
+    for (int r0 = warp * 4; r0 < nrows; r0 += kWarps * 4) {
+      const int r = r0 + rsub;
+      float wv[8];
+      unpack8(*reinterpret_cast<const uint4*>(chunk + ((size_t)r * hd + cg * 8) * 2), wv);
+      const int n0 = cu * 32 + r0;
+      for (int b = 0; b < B; ++b) {
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sum = fmaf(wv[j], s_y[b * 64 + cg * 8 + j], sum);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        const float s1 = __shfl_sync(0xffffffffu, sum, 8);
+        const float s2 = __shfl_sync(0xffffffffu, sum, 16);
+        const float s3 = __shfl_sync(0xffffffffu, sum, 24);
+        if (lane == 0) {
+          red_add_v4(c.p.x + (size_t)b * d + n0, sum, s1, s2, s3);
+          red_add_v4(c.p.x_in + (size_t)b * d + n0, sum, s1, s2, s3);
+        }
+      }
+    }
+    chunk_release(c);
+  }
+  grid_arrive(c, li, PH_B);
 }
 
-// ------------------------------------------------------------------ attention phase
-// Items (row, head, split): each CTA attends its chunk of the window with the
-// whole block, writes a partial (max, sum, acc[hd]); the last split of a
-// (row, head) combines the partials into y (decoding.py:260-264, 427-433).
-__device__ __noinline__ void attn_phase(Ctx& c, const dh_layer_params& lp, float* sc) {
+// GEMV CTAs: split-window attention with last-arriver combine
+template <int MAXB>
+__device__ void phase_b_attn(Ctx& c, int li) {
+  const dh_layer_params& lp = layer(c, li);
   constexpr int HD = 64;
-  const int H = c.p.H, d = H * HD, B = c.p.batch, ns = c.p.nsplit;
+  const int B = c.B, H = c.H, d = c.d, ns = c.nsplit;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long t = c.t;
+  const int ml = c.p.max_len;
   const long long lo = c.p.window > 0 ? (t + 1 - c.p.window > 0 ? t + 1 - c.p.window : 0) : 0;
   const long long n = t + 1 - lo;
   const long long chunk = (n + ns - 1) / ns;
-  int i0, i1;
-  split_range(B * H * ns, c.G, c.cta, i0, i1);
-  grid_sync(c);
-  const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(c.p.q);
   const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(lp.k_cache);
   const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(lp.v_cache);
-  float* sq = c.red + 512;         // [64]
-  float* sred = c.red + 576;       // [8]
-  float* sacc = c.red + 592;       // [8][64]
-  int* flag = reinterpret_cast<int*>(c.red + 1104);
+  const int items = B * H * ns;
+  float* sq = c.misc;            // [64]
+  float* sred = sq + 64;         // [8]
+  float* sacc = sred + 8;        // [kWarps][64]
+  int* flag = reinterpret_cast<int*>(sacc + kWarps * 64);
+  float* sc = reinterpret_cast<float*>(flag + 4);  // scores [chunk]
+  // the first item's earlier positions go to shared memory before the wait
+  const int first = c.cta;
+  if (first < items) {
+    const int b = first / (H * ns), h = (first / ns) % H, split = first % ns;
+    const long long s0 = lo + split * chunk;
+    long long s1 = s0 + chunk;
+    if (s1 > t) s1 = t;  // position t is written in phase A of this step
+    const int cnt = s1 > s0 ? (int)min((long long)kKvPos, s1 - s0) : 0;
+    for (int i = tid; i < cnt * 16; i += kCons) {
+      const int pos = i >> 4, part = i & 15, kvsel = part >> 3, g = part & 7;
+      const __nv_bfloat16* src = (kvsel ? vc : kc) + ((size_t)b * ml + s0 + pos) * d + h * HD + g * 8;
+      cp_async16(c.kv + ((size_t)kvsel * kKvPos + pos) * HD + g * 8, src);
+    }
+  }
+  grid_wait(c, li, PH_A, c.NG);
+  cp_async_wait_all();
+  csync();
   const float scale = rsqrtf((float)HD);
-  for (int item = i0; item < i1; ++item) {
+  for (int item = first; item < items; item += c.NG) {
     const int b = item / (H * ns), h = (item / ns) % H, split = item % ns;
     const long long s0 = lo + split * chunk;
     long long s1 = s0 + chunk;
     if (s1 > t + 1) s1 = t + 1;
     const int cnt = s1 > s0 ? (int)(s1 - s0) : 0;
-    if (tid < HD) sq[tid] = bf2f(__ldcg(q + (size_t)b * d + h * HD + tid));
-    __syncthreads();
+    const int staged = item == first ? (int)min((long long)kKvPos, max(0ll, min(s1, t) - s0)) : 0;
+    if (tid < HD) sq[tid] = bf2f(__ldcg(static_cast<const __nv_bfloat16*>(c.p.q) + (size_t)b * d + h * HD + tid));
+    csync();
     float mloc = -INFINITY;
-#pragma unroll 2
-    for (int i = tid; i < cnt; i += kThreads) {
-      const uint4* kr = reinterpret_cast<const uint4*>(kc + ((size_t)b * c.p.max_len + s0 + i) * d + h * HD);
+    for (int i = tid; i < cnt; i += kCons) {
+      const __nv_bfloat16* kr = i < staged ? c.kv + (size_t)i * HD
+                                           : kc + ((size_t)b * ml + s0 + i) * d + h * HD;
       float s = 0.f;
 #pragma unroll
       for (int j = 0; j < HD / 8; ++j) {
         float f[8];
-        unpack8(__ldcg(kr + j), f);
+        unpack8(i < staged ? reinterpret_cast<const uint4*>(kr)[j] : __ldcg(reinterpret_cast<const uint4*>(kr) + j), f);
 #pragma unroll
         for (int e = 0; e < 8; ++e) s = fmaf(f[e], sq[j * 8 + e], s);
       }
@@ -561,35 +759,34 @@ __device__ __noinline__ void attn_phase(Ctx& c, const dh_layer_params& lp, float
     }
     mloc = warp_max(mloc);
     if (lane == 0) sred[warp] = mloc;
-    __syncthreads();
+    csync();
     float M = sred[0];
     for (int w = 1; w < kWarps; ++w) M = fmaxf(M, sred[w]);
-    __syncthreads();
+    csync();
     float lsum = 0.f;
-    for (int i = tid; i < cnt; i += kThreads) {
+    for (int i = tid; i < cnt; i += kCons) {
       const float e = expf(sc[i] - M);
       sc[i] = e;
       lsum += e;
     }
     lsum = warp_sum(lsum);
     if (lane == 0) sred[warp] = lsum;
-    __syncthreads();
+    csync();
     float Ls = 0.f;
     for (int w = 0; w < kWarps; ++w) Ls += sred[w];
-    // P V: 32 lanes x 2 channels, 8 warps over positions
     const int c2 = lane * 2;
     float a0 = 0.f, a1 = 0.f;
-#pragma unroll 8
     for (int i = warp; i < cnt; i += kWarps) {
-      const __nv_bfloat162 vv = __ldcg(reinterpret_cast<const __nv_bfloat162*>(
-          vc + ((size_t)b * c.p.max_len + s0 + i) * d + h * HD + c2));
+      const __nv_bfloat162 vv =
+          i < staged ? *reinterpret_cast<const __nv_bfloat162*>(c.kv + ((size_t)kKvPos + i) * HD + c2)
+                     : __ldcg(reinterpret_cast<const __nv_bfloat162*>(vc + ((size_t)b * ml + s0 + i) * d + h * HD + c2));
       const float2 f = __bfloat1622float2(vv);
       a0 = fmaf(sc[i], f.x, a0);
       a1 = fmaf(sc[i], f.y, a1);
     }
     sacc[warp * HD + c2] = a0;
     sacc[warp * HD + c2 + 1] = a1;
-    __syncthreads();
+    csync();
     float* mine = c.p.part + (((size_t)b * H + h) * ns + split) * (HD + 2);
     if (tid < HD) {
       float o = 0.f;
@@ -601,9 +798,9 @@ __device__ __noinline__ void attn_phase(Ctx& c, const dh_layer_params& lp, float
       mine[1] = cnt > 0 ? Ls : 0.f;
     }
     __threadfence();
-    __syncthreads();
+    csync();
     if (tid == 0) *flag = (atomicAdd(&c.p.counters[H + b * H + h], 1) == ns - 1);
-    __syncthreads();
+    csync();
     if (*flag) {
       __threadfence();
       const float* all = c.p.part + ((size_t)b * H + h) * ns * (HD + 2);
@@ -618,143 +815,226 @@ __device__ __noinline__ void attn_phase(Ctx& c, const dh_layer_params& lp, float
           den += w * __ldcg(all + s * (HD + 2) + 1);
           num += w * __ldcg(all + s * (HD + 2) + 2 + tid);
         }
-        static_cast<__nv_bfloat16*>(c.p.y)[(size_t)b * d + h * HD + tid] =
-            f2bf(den > 0.f ? num / den : 0.f);
+        static_cast<__nv_bfloat16*>(c.p.y)[(size_t)b * d + h * HD + tid] = f2bf(den > 0.f ? num / den : 0.f);
       }
       if (tid == 0) c.p.counters[H + b * H + h] = 0;
+      // this (row, head) is complete: one arrival of phase B
+      grid_arrive(c, li, PH_B);
     }
-    __syncthreads();
+    csync();
   }
+}
+
+// GEMV CTAs: attention output projection, rows owned (no atomics)
+template <int MAXB>
+__device__ void phase_o(Ctx& c, int li) {
+  const int d = c.d;
+  grid_wait(c, li, PH_B, c.B * c.H);
+  stage_copy(c, static_cast<const __nv_bfloat16*>(c.p.y), d);
+  int u0, u1;
+  split_range(d / 2, c.NG, c.cta, u0, u1);
+  const Seg s = get_seg(c, li, PH_O, 0);
+  float* x = c.p.x;
+  float* xin = c.p.x_in;
+  gemv_segment<MAXB>(c, s, d, u0, [&](int u, int b, int row, float v, float) {
+    const size_t i = (size_t)b * d + 2 * u + row;
+    const float nx = __ldcg(x + i) + v;
+    x[i] = nx;
+    xin[i] = nx;
+  });
+  grid_arrive(c, li, PH_O);
+}
+
+// GEMV CTAs: the FFN slice, down projection added into x
+template <int MAXB>
+__device__ void phase_c(Ctx& c, int li) {
+  const dh_layer_params& lp = layer(c, li);
+  const int d = c.d, B = c.B, tid = threadIdx.x;
+  if (lp.kind == 0) grid_wait(c, li, PH_B, c.H);
+  else grid_wait(c, li, PH_O, c.NG);
+  stage_norm<MAXB>(c, c.p.x_in, static_cast<const __nv_bfloat16*>(lp.norm2));
+  int j0, j1;
+  split_range(c.ff, c.NG, c.cta, j0, j1);
+  float* us = c.misc;  // [MAXB][kMaxUpc]
+  const Seg sgu = get_seg(c, li, PH_C, 0);
+  gemv_segment<MAXB>(c, sgu, d, 0, [&](int u, int b, int row, float g, float up) {
+    if (row != 0) return;
+    us[b * kMaxUpc + u] = bf2f(f2bf(g / (1.0f + expf(-g)) * up));
+  });
+  csync();
+  const Seg sd = get_seg(c, li, PH_C, 1);
+  const int upc = units_per_chunk(c, sd);
+  const int n0 = tid * 4;
+  const bool nin = n0 < d;
+  float acc[MAXB][4];
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.f;
+  for (int cu = 0; cu < sd.units; cu += upc) {
+    const int nj = min(upc, sd.units - cu);
+    const uint8_t* chunk = chunk_acquire(c);
+    if (nin) {
+      for (int j = 0; j < nj; ++j) {
+        const uint2 wv = *reinterpret_cast<const uint2*>(chunk + ((size_t)j * d + n0) * 2);
+        const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.x));
+        const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.y));
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b) {
+          if (b < B) {
+            const float uj = us[b * kMaxUpc + cu + j];
+            acc[b][0] = fmaf(uj, w01.x, acc[b][0]);
+            acc[b][1] = fmaf(uj, w01.y, acc[b][1]);
+            acc[b][2] = fmaf(uj, w23.x, acc[b][2]);
+            acc[b][3] = fmaf(uj, w23.y, acc[b][3]);
+          }
+        }
+      }
+    }
+    chunk_release(c);
+  }
+  if (nin && sd.units > 0) {
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b)
+      if (b < B) red_add_v4(c.p.x + (size_t)b * d + n0, acc[b][0], acc[b][1], acc[b][2], acc[b][3]);
+  }
+  grid_arrive(c, li, PH_C);
+}
+
+template <int MAXB>
+__device__ void phase_n(Ctx& c) {
+  const int d = c.d;
+  grid_wait(c, c.p.n_layers - 1, PH_C, c.NG);
+  stage_norm<MAXB>(c, c.p.x, static_cast<const __nv_bfloat16*>(c.p.norm_out));
+  int u0, u1;
+  split_range((c.p.vocab + 1) / 2, c.G, c.cta, u0, u1);
+  const Seg s = get_seg(c, c.p.n_layers, PH_N, 0);
+  __nv_bfloat16* lg = static_cast<__nv_bfloat16*>(c.p.logits);
+  const int V = c.p.vocab;
+  gemv_segment<MAXB>(c, s, d, u0, [&](int u, int b, int row, float v, float) {
+    lg[(size_t)b * V + 2 * u + row] = f2bf(v);
+  });
 }
 
 // ------------------------------------------------------------------ kernel
 template <int MAXB>
 __global__ void __launch_bounds__(kThreads, 1)
-    step_kernel(const __grid_constant__ dh_step_params p, int xs_elems) {
+    step_kernel(const __grid_constant__ dh_step_params p, uint32_t wait_limit) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   Ctx c{p};
   c.G = gridDim.x;
   c.cta = blockIdx.x;
-  c.nbar = 0;
+  c.B = p.batch;
+  c.d = p.d;
+  c.gh = p.d;
+  c.L = p.L;
+  c.H = p.H;
+  c.hd = p.hd;
+  c.ff = p.ff;
+  c.NG = c.G - c.H;
+  c.head = c.cta >= c.NG ? c.cta - c.NG : -1;
+  c.wait_limit = wait_limit;
+  {
+    int ns = c.NG / (c.B * c.H);
+    ns = ns < 1 ? 1 : ns;
+    c.nsplit = ns < p.nsplit ? ns : p.nsplit;
+  }
+  c.lg = 1;
+  while (c.lg < c.L && gate_chunk_bytes(c, 0, c.lg + 1) <= (uint32_t)kSlotBytes) ++c.lg;
+  c.nslots = slots_for<MAXB>();
+  c.slots = smem_raw;
+  uint8_t* q = smem_raw + (size_t)c.nslots * kSlotBytes;
+  c.xs = reinterpret_cast<__nv_bfloat16*>(q);
+  q += (size_t)MAXB * 1024 * 2;
+  c.kv = reinterpret_cast<__nv_bfloat16*>(q);
+  q += (size_t)2 * kKvPos * 64 * 2;
+  c.red = reinterpret_cast<float*>(q);
+  q += (size_t)kWarps * MAXB * kLmax * 3 * 4;
+  c.misc = reinterpret_cast<float*>(q);
+  q += (size_t)(MAXB * (4 * kLmax + 64 + kMaxUpc) + MAXB * kLmax * 32 + 2048) * 4;
+  c.full = reinterpret_cast<uint64_t*>(q);
+  c.empty = c.full + c.nslots;
+  c.abort = reinterpret_cast<volatile int*>(c.empty + c.nslots);
   c.consumed = 0;
-  c.slots = smem_raw;                                              // kSlots x kSlotBytes
-  c.xs = reinterpret_cast<__nv_bfloat16*>(smem_raw + kSlots * kSlotBytes);
-  c.red = reinterpret_cast<float*>(smem_raw + kSlots * kSlotBytes + (size_t)xs_elems * 2);
-  float* sc = c.red + 1280;                                        // attention scores
-  c.full = reinterpret_cast<uint64_t*>(c.red + 1272);              // 3 mbarriers (8-aligned)
-  c.cursor = reinterpret_cast<int*>(c.red + 1266);
-  const int nbar_total = 5 * p.n_layers + 1;
   c.t = __ldcg(p.t_buf);
-  const unsigned long long gen = __ldcg(p.barrier + 1);
-  c.base = gen * (unsigned long long)nbar_total * c.G;
-  const int B = p.batch, d = p.d;
+  c.gen = __ldcg(p.barrier);
+  if (c.t < 0 || c.t >= p.max_len) {  // no position left: nothing is written
+    if (c.cta == 0 && threadIdx.x == 0) atomicExch(p.status, DH_ERR_ARG);
+    return;
+  }
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kSlots; ++s) mbar_init(&c.full[s], 1);
+    for (int s = 0; s < c.nslots; ++s) {
+      mbar_init(&c.full[s], 1);
+      mbar_init(&c.empty[s], kWarps);
+    }
+    *c.abort = 0;
     fence_barrier_init();
-    c.cursor[0] = 0;
-    c.cursor[1] = 0;
-    c.cursor[2] = 0;
-    for (int s = 0; s < kSlots; ++s)
-      if (!issue_next(c)) break;
   }
   __syncthreads();
-  // embedding: x[b, :] = E[token[b], :] (this CTA's share of the 16-byte chunks)
-  {
-    int a, b;
-    split_range(B * d / 8, c.G, c.cta, a, b);
-    const __nv_bfloat16* emb = static_cast<const __nv_bfloat16*>(p.emb);
-    for (int i = a + threadIdx.x; i < b; i += kThreads) {
-      const int row = i / (d / 8), col = (i - row * (d / 8)) * 8;
-      long long tok = p.tokens[row];
-      if (tok < 0 || tok >= p.vocab) {
-        atomicExch(p.status, 1);
-        tok = tok < 0 ? 0 : p.vocab - 1;
+  if (threadIdx.x >= kCons) {  // producer warp
+    if (threadIdx.x == kCons) producer(c);
+    return;
+  }
+  const int nl = p.n_layers;
+  for (int li = 0; li < nl; ++li) {
+    const bool tree = p.layers[li].kind == 0;
+    if (c.head < 0) {
+      phase_a<MAXB>(c, li);
+      if (tree) {
+        phase_c<MAXB>(c, li);
+      } else {
+        phase_b_attn<MAXB>(c, li);
+        phase_o<MAXB>(c, li);
+        phase_c<MAXB>(c, li);
       }
-      float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(emb + (size_t)tok * d + col), f);
-      float4* xo = reinterpret_cast<float4*>(p.x + (size_t)row * d + col);
-      xo[0] = make_float4(f[0], f[1], f[2], f[3]);
-      xo[1] = make_float4(f[4], f[5], f[6], f[7]);
+    } else if (tree) {
+      phase_b_tree<MAXB>(c, li);
     }
   }
-  for (int li = 0; li < p.n_layers; ++li) {
-    const dh_layer_params& lp = p.layers[li];
-    const int pi = 5 * li;
-    GemvPhase g{};
-    g.K = d;
-    g.norm_w = static_cast<const __nv_bfloat16*>(lp.norm1);
-    if (lp.kind == 0) {
-      g.epi = E_MIXIN;
-      g.o0 = static_cast<__nv_bfloat16*>(p.v0);
-      g.o1 = static_cast<__nv_bfloat16*>(p.a);
-      g.o2 = static_cast<__nv_bfloat16*>(lp.b_hist);
-      gemv_phase<MAXB>(c, pi, g);
-      tree_phase<MAXB>(c, pi + 1, lp);
-    } else {
-      g.epi = E_QKV;
-      g.o0 = static_cast<__nv_bfloat16*>(p.q);
-      g.o1 = static_cast<__nv_bfloat16*>(lp.k_cache);
-      g.o2 = static_cast<__nv_bfloat16*>(lp.v_cache);
-      gemv_phase<MAXB>(c, pi, g);
-      attn_phase(c, lp, sc);
-    }
-    GemvPhase go{};
-    go.epi = E_RESID;
-    go.K = d;
-    go.N = d;
-    go.src = static_cast<const __nv_bfloat16*>(p.y);
-    go.x = p.x;
-    gemv_phase<MAXB>(c, pi + 2, go);
-    GemvPhase gf{};
-    gf.epi = E_FFNIN;
-    gf.K = d;
-    gf.norm_w = static_cast<const __nv_bfloat16*>(lp.norm2);
-    gf.o0 = static_cast<__nv_bfloat16*>(p.u);
-    gemv_phase<MAXB>(c, pi + 3, gf);
-    GemvPhase gd{};
-    gd.epi = E_RESID;
-    gd.K = p.ff;
-    gd.N = d;
-    gd.src = static_cast<const __nv_bfloat16*>(p.u);
-    gd.x = p.x;
-    gemv_phase<MAXB>(c, pi + 4, gd);
-  }
-  // every position-dependent read of this step is ordered before the next
-  // barrier; CTA 0 advances t and the barrier generation once it has passed
-  GemvPhase gl{};
-  gl.epi = E_LOGITS;
-  gl.K = d;
-  gl.N = p.vocab;
-  gl.norm_w = static_cast<const __nv_bfloat16*>(p.norm_out);
-  gl.o0 = static_cast<__nv_bfloat16*>(p.logits);
-  gemv_phase<MAXB>(c, 5 * p.n_layers, gl);
+  phase_n<MAXB>(c);
+  cp_async_wait_all();
   if (c.cta == 0 && threadIdx.x == 0) {
     p.t_buf[0] = c.t + 1;
-    atomicAdd(p.barrier + 1, 1ull);
+    atomicAdd(p.barrier, 1ull);
   }
 }
 
 template <int MAXB>
+size_t step_smem() {
+  return (size_t)slots_for<MAXB>() * kSlotBytes + (size_t)MAXB * 1024 * 2 + (size_t)2 * kKvPos * 64 * 2 +
+         (size_t)kWarps * MAXB * kLmax * 3 * 4 +
+         (size_t)(MAXB * (4 * kLmax + 64 + kMaxUpc) + MAXB * kLmax * 32 + 2048) * 4 +
+         (size_t)2 * slots_for<MAXB>() * 8 + 64;
+}
+
+template <int MAXB>
 int launch_step(const dh_step_params& p, cudaStream_t st) {
-  const int kmax = p.ff > p.d ? p.ff : p.d;
-  const int xs_elems = ((p.batch * kmax + 7) / 8) * 8;
-  const int span = (p.window > 0 && p.window < p.max_len) ? p.window : p.max_len;
-  const int chunk = (span + p.nsplit - 1) / p.nsplit;
-  const size_t smem = (size_t)kSlots * kSlotBytes + (size_t)xs_elems * 2 + (1280 + (size_t)chunk) * 4;
+  const size_t smem = step_smem<MAXB>();
   DH_REQUIRE(smem <= 227 * 1024, DH_ERR_SHAPE, "dh_decode_step: %zu bytes of shared memory", smem);
   static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_dev != dev) {
-    cudaFuncSetAttribute(step_kernel<MAXB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(step_kernel<MAXB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     configured_dev = dev;
   }
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel<MAXB>, kThreads, smem);
   DH_REQUIRE(per_sm >= 1, DH_ERR_SHAPE, "dh_decode_step: kernel does not fit on an SM");
+  const int G = sm_count();
+  DH_REQUIRE(G - p.H >= 16, DH_ERR_SHAPE, "dh_decode_step: %d SMs leave too few GEMV CTAs", G);
+  {  // the attention scores of one item live in the per-phase scratch
+    const int span = (p.window > 0 && p.window < p.max_len) ? p.window : p.max_len;
+    int ns = (G - p.H) / (p.batch * p.H);
+    ns = ns < 1 ? 1 : (ns < p.nsplit ? ns : p.nsplit);
+    const int chunk = (span + ns - 1) / ns;
+    const int misc = MAXB * (4 * kLmax + 64 + kMaxUpc) + MAXB * kLmax * 32 + 2048;
+    DH_REQUIRE(chunk + 64 + 8 + kWarps * 64 + 4 <= misc, DH_ERR_SHAPE,
+               "dh_decode_step: %d window positions per attention item exceed the scratch", chunk);
+  }
+  DH_REQUIRE((p.ff + (G - p.H) - 1) / (G - p.H) <= kMaxUpc, DH_ERR_SHAPE,
+             "dh_decode_step: FFN width %d too large for %d CTAs", p.ff, G - p.H);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sm_count());
+  cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -763,7 +1043,7 @@ int launch_step(const dh_step_params& p, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, step_kernel<MAXB>, p, xs_elems) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, step_kernel<MAXB>, p, wait_limit()) != cudaSuccess)
     return check_launch("step_kernel");
   return DH_OK;
 }
@@ -776,23 +1056,21 @@ using namespace dh;
 extern "C" int dh_decode_step(const dh_step_params* params, void* stream) {
   DH_REQUIRE(params, DH_ERR_ARG, "dh_decode_step: null params");
   const dh_step_params& p = *params;
-  DH_REQUIRE(p.layers && p.tokens && p.t_buf && p.emb && p.norm_out && p.logits && p.x && p.a &&
-                 p.v0 && p.y && p.q && p.u && p.ig && p.fg && p.counters && p.barrier && p.status,
+  DH_REQUIRE(p.layers && p.tokens && p.t_buf && p.emb && p.norm_out && p.logits && p.x && p.x_in &&
+                 p.a && p.v0 && p.y && p.q && p.part && p.counters && p.barrier && p.status,
              DH_ERR_ARG, "dh_decode_step: null pointer in params");
-  DH_REQUIRE(p.batch >= 1 && p.batch <= 16, DH_ERR_SHAPE, "dh_decode_step: batch %d not in [1,16]",
+  DH_REQUIRE(p.batch >= 1 && p.batch <= 8, DH_ERR_SHAPE, "dh_decode_step: batch %d not in [1,8]",
              p.batch);
-  DH_REQUIRE(p.hd == 64 && p.d == p.H * p.hd && p.d % 8 == 0 && p.ff % 8 == 0 && p.L >= 1 &&
-                 p.L <= 16 && p.nsplit >= 1 && p.n_layers >= 1,
-             DH_ERR_SHAPE, "dh_decode_step: unsupported shape (d=%d H=%d hd=%d ff=%d L=%d)", p.d,
-             p.H, p.hd, p.ff, p.L);
-  DH_REQUIRE(4 * p.ff <= kSlotBytes && 6 * p.d <= kSlotBytes, DH_ERR_SHAPE,
-             "dh_decode_step: a weight unit exceeds a stream slot (d=%d ff=%d)", p.d, p.ff);
-  DH_REQUIRE(p.nsplit == 1 || p.part, DH_ERR_ARG, "dh_decode_step: nsplit > 1 needs part scratch");
-  DH_REQUIRE(p.d <= 1024, DH_ERR_SHAPE, "dh_decode_step: d = %d exceeds 1024", p.d);
+  DH_REQUIRE(p.hd == 64 && p.d == p.H * p.hd && p.d % 64 == 0 && p.d <= 1024 && p.ff % 8 == 0 &&
+                 p.L >= 1 && p.L <= kLmax && p.nsplit >= 1 && p.n_layers >= 1 &&
+                 p.n_layers * 5 + 2 <= (DH_STEP_SYNC_WORDS / kSyncStride),
+             DH_ERR_SHAPE, "dh_decode_step: unsupported shape (d=%d H=%d hd=%d ff=%d L=%d layers=%d)",
+             p.d, p.H, p.hd, p.ff, p.L, p.n_layers);
+  DH_REQUIRE(4 * p.d <= kSlotBytes && 3 * p.d * 2 + p.batch * p.d * 2 <= kSlotBytes, DH_ERR_SHAPE,
+             "dh_decode_step: a weight unit exceeds a stream slot (d=%d batch=%d)", p.d, p.batch);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (p.batch == 1) return launch_step<1>(p, st);
   if (p.batch == 2) return launch_step<2>(p, st);
   if (p.batch <= 4) return launch_step<4>(p, st);
-  if (p.batch <= 8) return launch_step<8>(p, st);
-  return launch_step<16>(p, st);
+  return launch_step<8>(p, st);
 }

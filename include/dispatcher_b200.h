@@ -272,12 +272,15 @@ DH_API int dh_window_attn_prefill_tc(const void* qkv, int ld, void* out, int ldo
 /* ------------------------------------------------- persistent decode step */
 
 /* Per-layer weights and caches of the whole-step decode kernel.  Weights
- * are bf16 row-major; packed forms (built once by the host):
+ * are bf16; packed forms (built once by the host):
  *   w_in3   tree: [W_in; W1x; W1s] (3d x d); attention: [Wq; Wk; Wv]
- *   w_gates tree: (L*H, 3, gh): rows admit/forget/transmit of (level, head)
- *   b_gates tree: (L*H, 3) fp32
+ *   w_gates tree: (H, L, 3, gh): per head, per level the admit / forget /
+ *           transmit readout rows
+ *   b_gates tree: (H, L, 3) fp32
+ *   w_out   tree: (H, d, hd): head h's columns of W_out, row n = W_out[n, h*hd:];
+ *           attention: W_out (d x d) row-major
  *   w_gu    (ff, 2, d): gate row j followed by up row j
- *   w_down  (d, ff) */
+ *   w_down  (ff, d): W_down transposed (row j = column j of W_down) */
 typedef struct {
   int kind; /* 0 tree block, 1 attention block */
   const void* norm1;
@@ -295,6 +298,9 @@ typedef struct {
   void* v_cache;
 } dh_layer_params;
 
+/* uint64 words of the step kernel's hand-off counters (`barrier`) */
+#define DH_STEP_SYNC_WORDS 4096
+
 typedef struct {
   int n_layers, batch, d, H, hd, L, ff, vocab, max_len, window, nsplit;
   const int64_t* tokens;  /* (batch) next tokens */
@@ -305,18 +311,18 @@ typedef struct {
   const float* rope_sin;
   const dh_layer_params* layers; /* device array of n_layers */
   void* logits;           /* bf16 (batch, vocab) */
-  /* caller-provided scratch (device memory, zero before first use):
-   * x fp32 (batch, d); a, v0, y, q bf16 (batch, d); u bf16 (batch, ff);
-   * ig, fg fp32 (batch, L, H); part fp32 (batch, H, nsplit, hd + 2);
-   * counters int (H + batch*H); barrier uint64 [2]; status int [1] */
+  /* caller-provided device memory:
+   * x, x_in fp32 (batch, d): the residual stream and the FFN's copy of it;
+   * a, v0, y, q bf16 (batch, d); part fp32 (batch, H, nsplit, hd + 2);
+   * counters int (H + batch*H), zero; barrier uint64 [DH_STEP_SYNC_WORDS],
+   * zero before the first step (word 0 counts steps, the others are the
+   * phases' hand-off counters); status int [1] */
   float* x;
+  float* x_in;
   void* a;
   void* v0;
   void* y;
   void* q;
-  void* u;
-  float* ig;
-  float* fg;
   float* part;
   int* counters;
   unsigned long long* barrier;
@@ -324,12 +330,17 @@ typedef struct {
 } dh_step_params;
 
 /* One whole lockstep decode step (embedding, every block, logits, t += 1)
- * as ONE persistent cooperative kernel: one CTA per SM, phases separated by
- * a bounded grid barrier (a timeout sets *status = DH_ERR_TIMEOUT and the
- * kernel still runs to completion).  Replaces the captured per-token graph
- * of decoding.py:437-443 with the fused tree step of decoding.py:468-488.
- * batch <= 16, hd == 64.  `params` is a host pointer; its `layers` array
- * must already be in device memory. */
+ * as ONE persistent cooperative kernel, one CTA per SM: the last H CTAs run
+ * each head's gate readouts, level recurrence and share of the output
+ * projection, the others the projections and the FFN; each CTA streams its
+ * weight slices by bulk copies into shared memory ahead of the phase
+ * hand-offs (monotonic per-phase counters, bounded waits: a timeout sets
+ * *status = DH_ERR_TIMEOUT and the kernel still runs to completion).
+ * Replaces the captured per-token graph of decoding.py:437-443 with the
+ * fused tree step of decoding.py:457-488 (fused_step.py:26-88) and the
+ * attention step of decoding.py:411-435.  batch <= 8, hd == 64, d <= 1024.
+ * `params` is a host pointer; its `layers` array must already be in device
+ * memory. */
 DH_API int dh_decode_step(const dh_step_params* params, void* stream);
 
 #ifdef __cplusplus

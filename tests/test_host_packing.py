@@ -99,31 +99,41 @@ def test_config_validation_and_levels():
 
 
 def test_decode_step_weight_packs():
-    """Decode packs: gate/up as (ff, 2, d) row pairs, the three gate readouts
-    of a tree layer as (L*H, 3, gh) with biases (L*H, 3) fp32 — one
-    contiguous 3-row group per (level, head) for the tree step's GEMV."""
+    """Decode-step packs: gate/up as (ff, 2, d) row pairs and W_down^T; for a
+    tree layer, per head: the three gate readouts (H, L, 3, gh) with biases
+    (H, L, 3) fp32, and the head's columns of W_out (H, d, hd) — each head's
+    part one contiguous run for its head CTA's weight stream."""
     from types import SimpleNamespace
     from dispatcher_b200.step_params import pack_step_weights
     g = torch.Generator().manual_seed(3)
-    ff, d, L, H, gh = 384, 128, 8, 2, 64
+    ff, d, L, H, gh = 384, 128, 8, 2, 128
     W, b = _gate_weights(L, H, gh, seed=3)
+    w_out = torch.randn(d, d, generator=g).bfloat16()
     tree = dict(kind="tree", w_gate=torch.randn(ff, d, generator=g).bfloat16(),
                 w_up=torch.randn(ff, d, generator=g).bfloat16(),
+                w_down=torch.randn(d, ff, generator=g).bfloat16(), w_out=w_out,
                 wi=W[0], wf=W[1], wr=W[2], bi=b[0], bf=b[1], br=b[2])
     attn = dict(kind="attn", w_gate=torch.randn(ff, d, generator=g).bfloat16(),
-                w_up=torch.randn(ff, d, generator=g).bfloat16())
+                w_up=torch.randn(ff, d, generator=g).bfloat16(),
+                w_down=torch.randn(d, ff, generator=g).bfloat16())
     packed = SimpleNamespace(layers=[tree, attn])
     pack_step_weights(packed)
     for lay in (tree, attn):
         gu = lay["w_gu_pairs"]
         assert gu.shape == (ff, 2, d) and gu.is_contiguous()
         assert torch.equal(gu[:, 0], lay["w_gate"]) and torch.equal(gu[:, 1], lay["w_up"])
-    assert "w_gates3" not in attn
-    w3, b3 = tree["w_gates3"], tree["b_gates3"]
-    assert w3.shape == (L * H, 3, gh) and b3.shape == (L * H, 3) and b3.dtype == torch.float32
+        assert torch.equal(lay["w_downT"], lay["w_down"].t()) and lay["w_downT"].is_contiguous()
+    assert "w_gates_heads" not in attn
+    wh, bh = tree["w_gates_heads"], tree["b_gates_heads"]
+    assert wh.shape == (H, L, 3, gh) and bh.shape == (H, L, 3) and bh.dtype == torch.float32
     for gi in range(3):
-        assert torch.equal(w3[:, gi].reshape(L, H, gh), W[gi])
-        assert torch.equal(b3[:, gi].reshape(L, H), b[gi])
-    before = w3.data_ptr()
+        assert torch.equal(wh[:, :, gi].transpose(0, 1), W[gi])
+        assert torch.equal(bh[:, :, gi].transpose(0, 1), b[gi])
+    oh = tree["w_out_heads"]
+    hd = d // H
+    assert oh.shape == (H, d, hd) and oh.is_contiguous()
+    for h in range(H):
+        assert torch.equal(oh[h], w_out[:, h * hd:(h + 1) * hd])
+    before = wh.data_ptr()
     pack_step_weights(packed)            # built once: a second call keeps the packs
-    assert tree["w_gates3"].data_ptr() == before
+    assert tree["w_gates_heads"].data_ptr() == before
