@@ -36,6 +36,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 PREFILL_B, PREFILL_T = 8, 4096
 DECODE_CTX = 3900
 METRIC = "prefill tok/s at T=4096 (8 x 4096 per GPU)"
+GATE_UP_TRAFFIC = 2 * (65.9e6 + 57.9e6)   # DRAM bytes per gate/up GEMM launch at 8 x 4096
 
 
 def peaks():
@@ -470,7 +471,7 @@ def main():
     g_fl = sum(v[2] for k, v in per_op.items() if k in ("proj3", "qkv", "out", "gate_up", "down", "lm_head"))
     peak_t = pk["bf16_tflops_sustained"]
     gemm_tf = g_fl / (g_ms * 1e-3) / 1e12
-    e2e_v, h2d, d2h = run_prefill_e2e(model, ids_host, max(2, min(args.steps, 5)), 2)
+    e2e_v, h2d, d2h = run_prefill_e2e(model, ids_host, args.steps, 2)
     e2e_v = -max_over_ranks(-e2e_v, world) * world
 
     dec_lines = {}
@@ -506,11 +507,13 @@ def main():
         "config": prefill_config(world),
         "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05, all prefill projections)",
                      "achieved": gemm_tf, "peak": peak_t, "unit": "TFLOP/s",
-                     "frac": gemm_tf / peak_t, "traffic": None,
-                     "traffic_note": "achieved averages 73 launches of five shapes per step; "
-                                     "DRAM bytes per shape come from one ncu capture each "
-                                     "(gate/up at 4 x 4096: 123.8 MB read + written against "
-                                     "137 MB algorithmic, profiles/gemm_kernel__gate_up_4x4096.md)",
+                     "frac": gemm_tf / peak_t, "traffic": GATE_UP_TRAFFIC,
+                     "traffic_note": "DRAM bytes read + written by one launch of the largest "
+                                     "shape (FFN gate/up with the SwiGLU epilogue, M = 8 x 4096): "
+                                     "an ncu capture at M = 4 x 4096 (65.9 MB read + 57.9 MB "
+                                     "written) scaled by 2, the traffic growing with M; "
+                                     "algorithmic bytes of that launch 263 MB (A 67 + W 11.5 + "
+                                     "out 184.5); achieved averages all 73 GEMM launches of a step",
                      "peak_kind": f"{pk_kind} sustained",
                      "launches_timed": g_n,
                      "whole_step_tflops": flop_tok * tokens / (ms * 1e-3) / 1e12,

@@ -16,10 +16,10 @@
 // This follows the reference's fused step (decoding.py:457-488 with
 // fused_step.py:26-88) and attention step (decoding.py:411-435).
 //
-// Weights never depend on activations, so each CTA's producer warp streams
+// Weights never depend on activations, so each CTA's producer lane streams
 // its slices of every phase of the step, in consumption order, by bulk async
-// copies (cp.async.bulk) into a ring of shared-memory slots that runs ahead
-// of the phase waits; history rows the head CTAs need (B_hist at t - 2^l)
+// copies (cp.async.bulk) into a ring of shared-memory slots that runs ahead of
+// the phase waits; history rows the head CTAs need (B_hist at t - 2^l)
 // travel in the same stream, and ring slots, transmit gates at the source
 // positions and the attention window's keys and values (all written by
 // earlier steps) are loaded before each wait.  After a wait a phase reads
@@ -34,7 +34,7 @@
 // Failure path: every wait is bounded.  A wait that gives up sets *status to
 // DH_ERR_TIMEOUT and an abort flag in shared memory; from then on the CTA
 // skips its waits (computing garbage but always arriving, so the counters
-// stay consistent), its producer issues no further copies and, before the
+// stay consistent), the producer issues no further copies and, before the
 // CTA exits, waits (with a fixed bound) for the copies it issued.
 #include <math.h>
 
@@ -45,17 +45,25 @@ namespace {
 
 constexpr int kWarps = 8;                    // consumer warps
 constexpr int kCons = kWarps * 32;           // consumer threads
-constexpr int kThreads = kCons + 32;         // + the producer warp
+constexpr int kThreads = kCons + 128;        // + the producer warpgroup (one lane issues the copies)
+// register split after launch (168 per thread at launch: 384 x 168 = 64512):
+// producer warpgroup 128 x 56 + consumers 256 x 224 = 64512
+constexpr int kProdRegs = 56;
+constexpr int kConsRegs = 224;
+static_assert(128 * kProdRegs + kCons * kConsRegs <= kThreads * 168, "register split exceeds the launch");
 constexpr int kSlotBytes = 32 * 1024;
-// ring depth: 5 slots up to 4 lockstep rows, 4 for 8 rows (their staging needs the room)
+// ring depth: 5 slots up to 2 lockstep rows, 4 from 4 rows (their staging needs the room)
 template <int MAXB>
-constexpr int slots_for() { return MAXB >= 8 ? 4 : 5; }
+constexpr int slots_for() { return MAXB >= 4 ? 4 : 5; }
 constexpr int kKvPos = 128;                  // window positions staged per attention item
+constexpr int kHeadParts = 2;                // head CTAs per head (each takes half the out-projection rows)
+constexpr int kLgMax = 4;                    // levels per gate chunk
 constexpr int kLmax = 16;
 constexpr int kMaxUpc = 32;                  // FFN elements per GEMV CTA
 constexpr float kEps = 1.1920928955078125e-07f;  // torch RMSNorm eps=None in fp32
 constexpr uint32_t kDrainLimit = 1u << 20;
 constexpr int kSyncStride = 32;              // uint64 words between two phase counters
+constexpr int kMaxLayers = DH_STEP_SYNC_WORDS / kSyncStride / 5 - 1;  // hand-off counters available
 
 enum { PH_A = 0, PH_B = 1, PH_O = 2, PH_C = 3, PH_N = 4 };
 
@@ -127,6 +135,7 @@ struct Seg {
 struct Ctx {
   const dh_step_params& p;
   int G, cta, NG, head;  // head >= 0 on head CTAs
+  int hpart;             // which half of the head's out-projection rows
   int B, d, gh, L, H, hd, ff;
   long long t;
   unsigned long long gen;
@@ -144,12 +153,54 @@ struct Ctx {
   float* misc;           // small per-phase arrays
   __nv_bfloat16* kv;     // [2][kKvPos][hd]
   int consumed;          // chunks consumed (same in every consumer thread)
+  struct Prod* prod;     // the weight stream (shared memory; the producer lane)
+  const dh_layer_params* lay;  // the layer table, copied into shared memory
 };
 
-__device__ __forceinline__ const dh_layer_params& layer(const Ctx& c, int li) { return c.p.layers[li]; }
+// The weight stream's state, in shared memory, used by the producer lane: a
+// copy of the CTA's geometry and the cursor of the next chunk.
+struct Prod {
+  const dh_step_params* pp;
+  const dh_layer_params* lay;  // shared-memory copy of the layer table
+  const void* emb;
+  int vocab, max_len, n_layers;
+  int G, cta, NG, head, hpart, B, d, gh, L, H, hd, ff, lg, nslots;
+  long long t;
+  uint32_t wait_limit;
+  uint8_t* slots;
+  uint64_t* full;
+  uint64_t* empty;
+  volatile int* abort;
+  int cli, cph, csi, cu;  // next chunk: layer, phase, segment, unit
+  Seg cseg;
+  int cvalid;             // a chunk is left to issue
+  int pslot;              // ring slot of the next chunk
+  uint32_t peph;          // parity of that slot's empty barrier to wait for
+  long issued;            // chunks issued so far
+};
+
+// the few step parameters the plan needs, for both the consumers' context
+// and the issuer's shared-memory copy
+__device__ __forceinline__ int vocab_of(const Ctx& c) { return c.p.vocab; }
+__device__ __forceinline__ int vocab_of(const Prod& c) { return c.vocab; }
+__device__ __forceinline__ const void* emb_of(const Ctx& c) { return c.p.emb; }
+__device__ __forceinline__ const void* emb_of(const Prod& c) { return c.emb; }
+
+template <class C>
+__device__ __forceinline__ const dh_layer_params& layer(const C& c, int li) { return c.lay[li]; }
+
+// optional timeline: global timer of (layer, phase, event k) by thread 0
+__device__ __forceinline__ void stamp(const Ctx& c, int li, int ph, int k) {
+  if (c.p.trace && threadIdx.x == 0) {
+    unsigned long long ns;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ns));
+    c.p.trace[(size_t)c.cta * DH_STEP_TRACE_WORDS + (li * 5 + ph) * 4 + k] = ns;
+  }
+}
 
 // number of segments of (layer li, phase ph) for this CTA, and segment si
-__device__ int seg_count(const Ctx& c, int li, int ph) {
+template <class C>
+__device__ int seg_count(const C& c, int li, int ph) {
   if (ph == PH_N) return 1;
   const bool tree = layer(c, li).kind == 0;
   if (c.head >= 0) return (tree && ph == PH_B) ? 2 : 0;
@@ -158,17 +209,18 @@ __device__ int seg_count(const Ctx& c, int li, int ph) {
   return 0;
 }
 
-__device__ Seg get_seg(const Ctx& c, int li, int ph, int si) {
+template <class C>
+__device__ Seg get_seg(const C& c, int li, int ph, int si) {
   Seg s{nullptr, 1, 0, SEG_ROWS, 0};
   const int d = c.d;
   if (ph == PH_N) {  // lm_head row pairs, split over every CTA
     int u0, u1;
-    const int units = (c.p.vocab + 1) / 2;
+    const int units = (vocab_of(c) + 1) / 2;
     split_range(units, c.G, c.cta, u0, u1);
-    s.base = static_cast<const uint8_t*>(c.p.emb) + (size_t)u0 * 4 * d;
+    s.base = static_cast<const uint8_t*>(emb_of(c)) + (size_t)u0 * 4 * d;
     s.unit_bytes = 4 * d;
     s.units = u1 - u0;
-    s.limit = (size_t)c.p.vocab * d * 2 - (size_t)u0 * 4 * d;
+    s.limit = (size_t)vocab_of(c) * d * 2 - (size_t)u0 * 4 * d;
     return s;
   }
   const dh_layer_params& lp = layer(c, li);
@@ -178,10 +230,11 @@ __device__ Seg get_seg(const Ctx& c, int li, int ph, int si) {
       s.unit_bytes = 3 * c.gh * 2;
       s.units = c.L;
       s.kind = SEG_GATES;
-    } else {
-      s.base = static_cast<const uint8_t*>(lp.w_out) + (size_t)c.head * d * c.hd * 2;
-      s.unit_bytes = 32 * c.hd * 2;  // 32 output rows of this head's columns
-      s.units = d / 32;
+    } else {  // this CTA's half of the output rows, head h's columns
+      s.base = static_cast<const uint8_t*>(lp.w_out) +
+               ((size_t)c.head * d + (size_t)c.hpart * (d / kHeadParts)) * c.hd * 2;
+      s.unit_bytes = 32 * c.hd * 2;  // 32 output rows
+      s.units = d / kHeadParts / 32;
     }
     s.limit = (size_t)s.units * s.unit_bytes;
     return s;
@@ -208,7 +261,8 @@ __device__ Seg get_seg(const Ctx& c, int li, int ph, int si) {
   return s;
 }
 
-__device__ __forceinline__ int units_per_chunk(const Ctx& c, const Seg& s) {
+template <class C>
+__device__ __forceinline__ int units_per_chunk(const C& c, const Seg& s) {
   if (s.kind == SEG_GATES) return c.lg;
   const int n = kSlotBytes / (int)s.unit_bytes;
   return n < 1 ? 1 : n;
@@ -216,66 +270,98 @@ __device__ __forceinline__ int units_per_chunk(const Ctx& c, const Seg& s) {
 
 // bytes of a gate chunk: levels [l0, l1) of weights, then the history rows
 // B_hist[b, t - 2^l] of those levels for every lockstep row
-__device__ __forceinline__ uint32_t gate_chunk_bytes(const Ctx& c, int l0, int l1) {
+template <class C>
+__device__ __forceinline__ uint32_t gate_chunk_bytes(const C& c, int l0, int l1) {
   return (uint32_t)(l1 - l0) * 3 * c.gh * 2 + (uint32_t)(l1 - l0) * c.B * c.gh * 2;
 }
 
-// ------------------------------------------------------------------ producer
-// One lane walks the whole step's plan and keeps the ring full.
-__device__ void producer(Ctx& c) {
-  int slot = 0;
-  uint32_t eph = 0;
-  long issued = 0;
-  bool ok = true;
-  const int nl = c.p.n_layers;
-  for (int li = 0; li <= nl && ok; ++li) {
-    for (int ph = 0; ph < 5 && ok; ++ph) {
+// ------------------------------------------------------------------ the weight stream
+// The producer lane issues the CTA's chunks in plan order, each as soon as
+// every consumer warp released the slot: for every layer the phases A, B, O,
+// C in order, then the logits; in each phase this CTA's segments.
+// move the cursor to the first non-empty segment at or after (li, ph, si)
+__device__ __forceinline__ void cursor_seek(Prod* pr, int li, int ph, int si) {
+  const int nl = pr->n_layers;
+  for (; li <= nl; ++li, ph = 0, si = 0) {
+    for (; ph < 5; ++ph, si = 0) {
       if ((li == nl) != (ph == PH_N)) continue;
-      const int ns = seg_count(c, li, ph);
-      for (int si = 0; si < ns && ok; ++si) {
-        const Seg s = get_seg(c, li, ph, si);
-        const int upc = units_per_chunk(c, s);
-        for (int u = 0; u < s.units && ok; u += upc) {
-          const int n = min(upc, s.units - u);
-          if (issued >= c.nslots && !mbar_wait(&c.empty[slot], eph ^ 1, c.p.status, c.wait_limit)) {
-            *c.abort = 1;
-          }
-          if (*c.abort) { ok = false; break; }
-          uint8_t* dst = c.slots + (size_t)slot * kSlotBytes;
-          if (s.kind == SEG_GATES) {
-            const dh_layer_params& lp = layer(c, li);
-            const uint32_t wbytes = (uint32_t)n * s.unit_bytes;
-            uint32_t total = wbytes;
-            for (int l = u; l < u + n; ++l)
-              if (c.t - (1ll << l) >= 0) total += (uint32_t)c.B * c.gh * 2;
-            mbar_arrive_expect_tx(&c.full[slot], total);
-            bulk_g2s(dst, s.base + (size_t)u * s.unit_bytes, wbytes, &c.full[slot]);
-            const __nv_bfloat16* bh = static_cast<const __nv_bfloat16*>(lp.b_hist);
-            for (int l = u; l < u + n; ++l) {
-              const long long src = c.t - (1ll << l);
-              if (src < 0) continue;
-              for (int b = 0; b < c.B; ++b)
-                bulk_g2s(dst + wbytes + ((size_t)(l - u) * c.B + b) * c.gh * 2,
-                         bh + ((size_t)b * c.p.max_len + src) * c.gh, (uint32_t)c.gh * 2,
-                         &c.full[slot]);
-            }
-          } else {
-            const size_t off = (size_t)u * s.unit_bytes;
-            size_t bytes = (size_t)n * s.unit_bytes;
-            if (off + bytes > s.limit) bytes = s.limit - off;
-            mbar_arrive_expect_tx(&c.full[slot], (uint32_t)bytes);
-            bulk_g2s(dst, s.base + off, (uint32_t)bytes, &c.full[slot]);
-          }
-          ++issued;
-          if (++slot == c.nslots) { slot = 0; eph ^= 1; }
+      const int ns = seg_count(*pr, li, ph);
+      for (; si < ns; ++si) {
+        const Seg sg = get_seg(*pr, li, ph, si);
+        if (sg.units > 0) {
+          pr->cli = li;
+          pr->cph = ph;
+          pr->csi = si;
+          pr->cu = 0;
+          pr->cseg = sg;
+          pr->cvalid = 1;
+          return;
         }
       }
     }
   }
-  // no copy may still be writing shared memory when the CTA exits
-  for (int s = 0; s < c.nslots; ++s) {
-    const long n_s = issued / c.nslots + (s < issued % c.nslots ? 1 : 0);
-    if (n_s > 0) mbar_wait(&c.full[s], (uint32_t)((n_s - 1) & 1), nullptr, kDrainLimit);
+  pr->cvalid = 0;
+}
+
+// issue the chunk under the cursor into the next slot and advance
+__device__ __forceinline__ void issue_chunk(Prod* pr) {
+  const Seg s = pr->cseg;
+  const int upc = units_per_chunk(*pr, s);
+  const int u = pr->cu, n = min(upc, s.units - u);
+  const int slot = pr->pslot;
+  uint8_t* dst = pr->slots + (size_t)slot * kSlotBytes;
+  uint64_t* bar = &pr->full[slot];
+  if (s.kind == SEG_GATES) {
+    const dh_layer_params& lp = layer(*pr, pr->cli);
+    const uint32_t wbytes = (uint32_t)n * s.unit_bytes;
+    const int B = pr->B, gh = pr->gh;
+    const long long t = pr->t;
+    uint32_t total = wbytes;
+    for (int l = u; l < u + n; ++l)
+      if (t - (1ll << l) >= 0) total += (uint32_t)B * gh * 2;
+    mbar_arrive_expect_tx(bar, total);
+    bulk_g2s(dst, s.base + (size_t)u * s.unit_bytes, wbytes, bar);
+    const __nv_bfloat16* bh = static_cast<const __nv_bfloat16*>(lp.b_hist);
+    for (int l = u; l < u + n; ++l) {
+      const long long src = t - (1ll << l);
+      if (src < 0) continue;
+      for (int b = 0; b < B; ++b)
+        bulk_g2s(dst + wbytes + ((size_t)(l - u) * B + b) * gh * 2,
+                 bh + ((size_t)b * pr->max_len + src) * gh, (uint32_t)gh * 2, bar);
+    }
+  } else {
+    const size_t off = (size_t)u * s.unit_bytes;
+    size_t bytes = (size_t)n * s.unit_bytes;
+    if (off + bytes > s.limit) bytes = s.limit - off;
+    mbar_arrive_expect_tx(bar, (uint32_t)bytes);
+    bulk_g2s(dst, s.base + off, (uint32_t)bytes, bar);
+  }
+  ++pr->issued;
+  if (++pr->pslot == pr->nslots) {
+    pr->pslot = 0;
+    pr->peph ^= 1;
+  }
+  pr->cu = u + n;
+  if (pr->cu >= s.units) cursor_seek(pr, pr->cli, pr->cph, pr->csi + 1);
+}
+
+// The producer (one lane of the last warp): walks the plan, waiting (bounded)
+// for each slot to be released by every consumer warp before refilling it;
+// stops at the first failed wait or when a consumer aborted, and finally waits
+// (with a fixed bound) for the copies it issued.
+__device__ void producer(Prod* pr, int* status) {
+  while (pr->cvalid && !*pr->abort) {
+    if (pr->issued >= pr->nslots &&
+        !mbar_wait(&pr->empty[pr->pslot], pr->peph ^ 1, status, pr->wait_limit)) {
+      *pr->abort = 1;
+      break;
+    }
+    if (*pr->abort) break;
+    issue_chunk(pr);
+  }
+  for (int s = 0; s < pr->nslots; ++s) {
+    const long n_s = pr->issued / pr->nslots + (s < pr->issued % pr->nslots ? 1 : 0);
+    if (n_s > 0) mbar_wait(&pr->full[s], (uint32_t)((n_s - 1) & 1), nullptr, kDrainLimit);
   }
 }
 
@@ -327,33 +413,46 @@ __device__ __forceinline__ void grid_arrive(Ctx& c, int li, int ph) {
 
 // xs[b][k] = bf16(x[b][k] * rsqrt(mean(x[b]^2) + eps) * w[k]) for every lockstep row;
 // x comes from `xf` (fp32, read through L2) or, for the first block, from the
-// embedding rows of the step's tokens
+// embedding rows of the step's tokens.  The same loads also write this CTA's
+// slice [e0, e1) (float4 units) of x into dst0 / dst1 when they are set.
 template <int MAXB>
-__device__ void stage_norm(Ctx& c, const float* xf, const __nv_bfloat16* w) {
+__device__ void stage_norm(Ctx& c, const float* xf, const __nv_bfloat16* w, float* dst0 = nullptr,
+                           float* dst1 = nullptr, int e0 = 0, int e1 = 0) {
   const int B = c.B, d = c.d, d4 = d / 4, n4 = B * d4;
   constexpr int NV = (MAXB * 1024 + kCons * 4 - 1) / (kCons * 4);
   float* ssum = c.red;  // [MAXB]
   if (threadIdx.x < MAXB) ssum[threadIdx.x] = 0.f;
-  csync();
   float4 v[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int i = threadIdx.x + j * kCons;
-    float sq = 0.f;
     if (i < n4) {
       const int b = i / d4, k = (i - b * d4) * 4;
       if (xf) {
         v[j] = __ldcg(reinterpret_cast<const float4*>(xf + (size_t)b * d + k));
       } else {
         long long tok = c.p.tokens[b];
-        if (tok < 0 || tok >= c.p.vocab) tok = 0;  // reported by the embedding writer
+        if (tok < 0 || tok >= c.p.vocab) tok = 0;  // reported by the phase that owns the row
         const uint2 e = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(c.p.emb) +
                                                         (size_t)tok * d + k);
         const float2 e01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e.x));
         const float2 e23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e.y));
         v[j] = make_float4(e01.x, e01.y, e23.x, e23.y);
       }
+    }
+  }
+  csync();  // ssum cleared
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * kCons;
+    float sq = 0.f;
+    if (i < n4) {
       sq = v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+      if (i >= e0 && i < e1) {
+        const size_t off = (size_t)(i / d4) * d + (i - (i / d4) * d4) * 4;
+        if (dst0) *reinterpret_cast<float4*>(dst0 + off) = v[j];
+        if (dst1) *reinterpret_cast<float4*>(dst1 + off) = v[j];
+      }
     }
     if ((d4 & 31) == 0) {  // a warp's 32 float4 lie in one row: reduce, one atomic
       sq = warp_sum(sq);
@@ -399,11 +498,22 @@ __device__ __forceinline__ void dot_pair(const __nv_bfloat16* r0, const __nv_bfl
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int i = 0; i < 2 * MAXB; ++i) acc[i] = 0.f;
-#pragma unroll 2
-  for (int k = lane * 8; k < K; k += 256) {
+  uint4 wa[4], wb[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // K <= 1024: every load of the row pair up front
+    const int k = lane * 8 + i * 256;
+    if (k < K) {
+      wa[i] = *reinterpret_cast<const uint4*>(r0 + k);
+      wb[i] = *reinterpret_cast<const uint4*>(r1 + k);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int k = lane * 8 + i * 256;
+    if (k >= K) break;
     float fa[8], fb[8];
-    unpack8(*reinterpret_cast<const uint4*>(r0 + k), fa);
-    unpack8(*reinterpret_cast<const uint4*>(r1 + k), fb);
+    unpack8(wa[i], fa);
+    unpack8(wb[i], fb);
 #pragma unroll
     for (int b = 0; b < MAXB; ++b) {
       if (b < B) {
@@ -450,36 +560,23 @@ __device__ void phase_a(Ctx& c, int li) {
   const dh_layer_params& lp = layer(c, li);
   const bool tree = lp.kind == 0;
   const int d = c.d, B = c.B;
+  stamp(c, li, PH_A, 0);
   if (li > 0) grid_wait(c, li - 1, PH_C, c.NG);
-  // the residual: layer 0 starts it from the embedding rows; a tree block
-  // copies its accumulated value into xa (the input of C, which B adds into)
+  stamp(c, li, PH_A, 1);
+  // the residual: layer 0 starts it (both buffers) from the embedding rows; a
+  // tree block copies its accumulated value into x_in (the input of C, which
+  // B adds into); each CTA writes its slice, from the loads of the staging
   {
     int e0, e1;
     split_range(B * d / 4, c.NG, c.cta, e0, e1);
-    for (int i = e0 + threadIdx.x; i < e1; i += kCons) {
-      const int b = i / (d / 4), k = (i - b * (d / 4)) * 4;
-      float4 v;
-      if (li == 0) {
-        long long tok = c.p.tokens[b];
-        if (tok < 0 || tok >= c.p.vocab) {
-          atomicExch(c.p.status, DH_ERR_ARG);
-          tok = 0;
-        }
-        const uint2 e = *reinterpret_cast<const uint2*>(
-            static_cast<const __nv_bfloat16*>(c.p.emb) + (size_t)tok * d + k);
-        const float2 e01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e.x));
-        const float2 e23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e.y));
-        v = make_float4(e01.x, e01.y, e23.x, e23.y);
-        *reinterpret_cast<float4*>(c.p.x + (size_t)b * d + k) = v;
-      } else if (tree) {
-        v = __ldcg(reinterpret_cast<const float4*>(c.p.x + (size_t)b * d + k));
-      } else {
-        continue;
-      }
-      *reinterpret_cast<float4*>(c.p.x_in + (size_t)b * d + k) = v;
+    if (li == 0 && threadIdx.x < B && c.cta == 0) {
+      const long long tok = c.p.tokens[threadIdx.x];
+      if (tok < 0 || tok >= c.p.vocab) atomicExch(c.p.status, DH_ERR_ARG);
     }
+    stage_norm<MAXB>(c, li == 0 ? nullptr : c.p.x, static_cast<const __nv_bfloat16*>(lp.norm1),
+                     li == 0 ? c.p.x : nullptr, (li == 0 || tree) ? c.p.x_in : nullptr, e0, e1);
   }
-  stage_norm<MAXB>(c, li == 0 ? nullptr : c.p.x, static_cast<const __nv_bfloat16*>(lp.norm1));
+  stamp(c, li, PH_A, 2);
   const Seg s = get_seg(c, li, PH_A, 0);
   int u0, u1;
   split_range(3 * d / 2, c.NG, c.cta, u0, u1);
@@ -516,6 +613,7 @@ __device__ void phase_a(Ctx& c, int li) {
       else vc[((size_t)b * ml + t) * d + col] = f2bf(out);
     });
   }
+  stamp(c, li, PH_A, 3);
   grid_arrive(c, li, PH_A);
 }
 
@@ -535,7 +633,9 @@ __device__ void phase_b_tree(Ctx& c, int li) {
   float* s_c = s_f + MAXB * kLmax;            // [MAXB][kLmax]
   float* s_rg = s_c + MAXB * kLmax;           // [MAXB][kLmax] transmit gate at the source
   float* s_y = s_rg + MAXB * kLmax;           // [MAXB][64]
-  __nv_bfloat16* s_ring = reinterpret_cast<__nv_bfloat16*>(s_y + MAXB * 64);  // [MAXB][kLmax][64]
+  uint4* s_v0 = reinterpret_cast<uint4*>(s_y + MAXB * 64);                   // [MAXB][8]
+  __nv_bfloat16* s_ring = reinterpret_cast<__nv_bfloat16*>(s_v0 + MAXB * 8);  // [MAXB][kLmax][64]
+  stamp(c, li, PH_B, 0);
   // history written by earlier steps: ring slots of the source positions and
   // their transmit gates (one round trip, before the wait)
   for (int i = tid; i < B * L * 8; i += kCons) {
@@ -551,62 +651,78 @@ __device__ void phase_b_tree(Ctx& c, int li) {
       s_rg[b * kLmax + l] = src >= 0 ? bf2f(rg[(((size_t)b * ml + src) * L + l) * H + h]) : 0.f;
   }
   grid_wait(c, li, PH_A, c.NG);
-  stage_copy(c, static_cast<const __nv_bfloat16*>(c.p.a), gh);
-  // gate readouts: thread tid owns columns [4 tid, 4 tid + 4) of the hidden
-  // width for every level and row; per chunk, partial sums of its levels are
-  // reduced across the warp (transpose reduction) into red[warp][...]
+  stamp(c, li, PH_B, 1);
+  // A rows (every column) and this head's v0 slice, one round trip
+  {
+    const __nv_bfloat16* a = static_cast<const __nv_bfloat16*>(c.p.a);
+    const __nv_bfloat16* v0 = static_cast<const __nv_bfloat16*>(c.p.v0);
+    const int k8 = gh / 8, n = B * k8;
+    for (int i = tid; i < n + B * 8; i += kCons) {
+      if (i < n) {
+        const int b = i / k8, k = (i - b * k8) * 8;
+        *reinterpret_cast<uint4*>(c.xs + (size_t)b * 1024 + k) =
+            __ldcg(reinterpret_cast<const uint4*>(a + (size_t)b * gh + k));
+      } else {
+        const int j = i - n, b = j / 8, g = j - b * 8;
+        s_v0[b * 8 + g] = __ldcg(reinterpret_cast<const uint4*>(v0 + (size_t)b * d + h * hd + g * 8));
+      }
+    }
+  }
+  csync();
+  stamp(c, li, PH_B, 2);
+  // gate readouts, chunk by chunk (a chunk holds up to kLgMax levels: their
+  // weights, then their history rows): thread tid owns columns [4 tid, 4 tid + 4)
+  // of the hidden width; all loads of a chunk are issued before its FMAs and
+  // its (level, gate) partial sums leave in one transpose reduction per row
   float* red = c.red;  // [kWarps][MAXB][kLmax * 3]
   const int k = tid * 4;
   const bool kin = k < gh;
-  float av[MAXB][4];
-#pragma unroll
-  for (int b = 0; b < MAXB; ++b) {
-    if (b < B && kin) {
-      const uint2 u = *reinterpret_cast<const uint2*>(c.xs + (size_t)b * 1024 + k);
-      const float2 a01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-      const float2 a23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-      av[b][0] = a01.x; av[b][1] = a01.y; av[b][2] = a23.x; av[b][3] = a23.y;
-    } else {
-      av[b][0] = av[b][1] = av[b][2] = av[b][3] = 0.f;
-    }
-  }
   const Seg sg = get_seg(c, li, PH_B, 0);
   for (int l0 = 0; l0 < L; l0 += c.lg) {
-    const int l1 = min(L, l0 + c.lg);
+    const int nlv = min(L, l0 + c.lg) - l0;
     const uint8_t* chunk = chunk_acquire(c);
-    const uint32_t wbytes = (uint32_t)(l1 - l0) * sg.unit_bytes;
-    for (int l = l0; l < l1; ++l) {
-      const bool ok = t - (1ll << l) >= 0;
-      const __nv_bfloat16* wl = reinterpret_cast<const __nv_bfloat16*>(chunk + (size_t)(l - l0) * sg.unit_bytes);
-      float w3[3][4];
-#pragma unroll
-      for (int g = 0; g < 3; ++g) {
-        uint2 u = kin ? *reinterpret_cast<const uint2*>(wl + (size_t)g * gh + k) : make_uint2(0, 0);
-        const float2 x01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-        const float2 x23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-        w3[g][0] = x01.x; w3[g][1] = x01.y; w3[g][2] = x23.x; w3[g][3] = x23.y;
+    const uint32_t wbytes = (uint32_t)nlv * sg.unit_bytes;
+    for (int b = 0; b < B; ++b) {
+      const uint2 au = kin ? *reinterpret_cast<const uint2*>(c.xs + (size_t)b * 1024 + k) : make_uint2(0, 0);
+      float av[4];
+      {
+        const float2 a01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&au.x));
+        const float2 a23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&au.y));
+        av[0] = a01.x; av[1] = a01.y; av[2] = a23.x; av[3] = a23.y;
       }
-      for (int b = 0; b < B; ++b) {
-        float bs[4] = {0.f, 0.f, 0.f, 0.f};
-        if (ok && kin) {
-          const uint2 u = *reinterpret_cast<const uint2*>(
-              chunk + wbytes + (((size_t)(l - l0) * B + b) * gh + k) * 2);
-          const float2 b01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-          const float2 b23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-          bs[0] = b01.x; bs[1] = b01.y; bs[2] = b23.x; bs[3] = b23.y;
-        }
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};  // i, f, r, (pad)
+      uint2 bu[kLgMax];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float hv = fmaxf(av[b][j] + bs[j], 0.f);
-          hv *= hv;  // relu squared
-          acc[0] = fmaf(w3[0][j], hv, acc[0]);
-          acc[1] = fmaf(w3[1][j], hv, acc[1]);
-          acc[2] = fmaf(w3[2][j], hv, acc[2]);
-        }
-        const float r = transpose_reduce<4>(acc);
-        if (lane < 3) red[((size_t)warp * MAXB + b) * (kLmax * 3) + l * 3 + lane] = r;
+      for (int j = 0; j < kLgMax; ++j) {
+        const bool ok = j < nlv && kin && t - (1ll << (l0 + j)) >= 0;
+        bu[j] = ok ? *reinterpret_cast<const uint2*>(chunk + wbytes + (((size_t)j * B + b) * gh + k) * 2)
+                   : make_uint2(0, 0);
       }
+      float acc[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) acc[q] = 0.f;
+#pragma unroll
+      for (int j = 0; j < kLgMax; ++j) {
+        const float2 b01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bu[j].x));
+        const float2 b23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bu[j].y));
+        const float bs[4] = {b01.x, b01.y, b23.x, b23.y};
+        float hv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x = fmaxf(av[e] + bs[e], 0.f);
+          hv[e] = x * x;  // relu squared
+        }
+#pragma unroll
+        for (int g = 0; g < 3; ++g) {
+          const uint2 wq = (j < nlv && kin)
+              ? *reinterpret_cast<const uint2*>(chunk + ((size_t)j * 3 * gh + (size_t)g * gh + k) * 2)
+              : make_uint2(0, 0);
+          const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wq.x));
+          const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wq.y));
+          acc[j * 3 + g] = fmaf(w01.x, hv[0], fmaf(w01.y, hv[1], fmaf(w23.x, hv[2], w23.y * hv[3])));
+        }
+      }
+      const float r = transpose_reduce<16>(acc);
+      if (lane < nlv * 3) red[((size_t)warp * MAXB + b) * (kLmax * 3) + l0 * 3 + lane] = r;
     }
     chunk_release(c);
   }
@@ -626,30 +742,34 @@ __device__ void phase_b_tree(Ctx& c, int li) {
     const float ig = sigmoidf_(pre[0]) * okf;
     const float fg = sigmoidf_(pre[1]) * okf + (1.f - okf);
     const float rgt = sigmoidf_(pre[2]);
-    rg[(((size_t)b * ml + t) * L + l) * H + h] = f2bf(rgt);
+    if (c.hpart == 0) rg[(((size_t)b * ml + t) * L + l) * H + h] = f2bf(rgt);
     s_f[b * kLmax + l] = fg;
     s_c[b * kLmax + l] = ig * s_rg[b * kLmax + l];
   }
   csync();
-  // level recurrence (fp32 state, every level's value stored into its ring)
+  // level recurrence (fp32 state, every level's value stored into its ring;
+  // the head's two CTAs compute the same values, the first one stores them)
   for (int i = tid; i < B * (hd / 8); i += kCons) {
     const int b = i / (hd / 8), g = i - b * (hd / 8);
     const int c0 = h * hd + g * 8;
     __nv_bfloat16* ringb = ring + (size_t)b * S * d;
+    const bool wr = c.hpart == 0;
     float V[8];
-    const uint4 v0 = __ldcg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(c.p.v0) +
-                                                          (size_t)b * d + c0));
+    const uint4 v0 = s_v0[b * 8 + g];
     unpack8(v0, V);
-    *reinterpret_cast<uint4*>(ringb + (size_t)(t & 1) * d + c0) = v0;  // ring 0 at t
-    for (int l = 0; l < L; ++l) {
-      float vs[8];
-      unpack8(*reinterpret_cast<const uint4*>(s_ring + ((size_t)b * kLmax + l) * 64 + g * 8), vs);
-      const float f = s_f[b * kLmax + l], cc = s_c[b * kLmax + l];
+    if (wr) *reinterpret_cast<uint4*>(ringb + (size_t)(t & 1) * d + c0) = v0;  // ring 0 at t
+#pragma unroll 4
+    for (int l = 0; l < kLmax; ++l) {
+      if (l < L) {
+        float vs[8];
+        unpack8(*reinterpret_cast<const uint4*>(s_ring + ((size_t)b * kLmax + l) * 64 + g * 8), vs);
+        const float f = s_f[b * kLmax + l], cc = s_c[b * kLmax + l];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) V[j] = f * V[j] + cc * vs[j];
-      if (l + 1 < L) {
-        const long long slot = ((2ll << (l + 1)) - 2) + (t & ((2ll << (l + 1)) - 1));
-        *reinterpret_cast<uint4*>(ringb + (size_t)slot * d + c0) = pack8(V);
+        for (int j = 0; j < 8; ++j) V[j] = f * V[j] + cc * vs[j];
+        if (wr && l + 1 < L) {
+          const long long slot = ((2ll << (l + 1)) - 2) + (t & ((2ll << (l + 1)) - 1));
+          *reinterpret_cast<uint4*>(ringb + (size_t)slot * d + c0) = pack8(V);
+        }
       }
     }
     const uint4 yv = pack8(V);
@@ -659,38 +779,60 @@ __device__ void phase_b_tree(Ctx& c, int li) {
     for (int j = 0; j < 8; ++j) s_y[b * 64 + g * 8 + j] = yr[j];
   }
   csync();
-  // out-projection share: x[b, n] += sum_c W_out[n, h*hd + c] y_h[b, c] for every n,
-  // added into both residual buffers; 8 lanes per row (8 channels each), a
-  // warp covers 4 rows per pass, lane 0 issues one 4-wide reduction
+  // out-projection share: x[b, n] += sum_c W_out[n, h*hd + c] y_h[b, c] for this
+  // CTA's half of the rows n, added into both residual buffers.  Thread r owns
+  // row r of a chunk (256 rows x 64 channels), reading its 16-byte pieces in a
+  // rotated order (no bank conflicts); four rows leave in one vector reduction.
   const Seg so = get_seg(c, li, PH_B, 1);
   const int upc = units_per_chunk(c, so);
-  const int cg = lane & 7, rsub = lane >> 3;
+  const int nbase = c.hpart * (d / kHeadParts);
   for (int cu = 0; cu < so.units; cu += upc) {
     const int nrows = min(upc, so.units - cu) * 32;
     const uint8_t* chunk = chunk_acquire(c);
-    for (int r0 = warp * 4; r0 < nrows; r0 += kWarps * 4) {
-      const int r = r0 + rsub;
-      float wv[8];
-      unpack8(*reinterpret_cast<const uint4*>(chunk + ((size_t)r * hd + cg * 8) * 2), wv);
-      const int n0 = cu * 32 + r0;
-      for (int b = 0; b < B; ++b) {
-        float sum = 0.f;
+    const int r = tid;
+    float sum[MAXB];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) sum = fmaf(wv[j], s_y[b * 64 + cg * 8 + j], sum);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        const float s1 = __shfl_sync(0xffffffffu, sum, 8);
-        const float s2 = __shfl_sync(0xffffffffu, sum, 16);
-        const float s3 = __shfl_sync(0xffffffffu, sum, 24);
-        if (lane == 0) {
-          red_add_v4(c.p.x + (size_t)b * d + n0, sum, s1, s2, s3);
-          red_add_v4(c.p.x_in + (size_t)b * d + n0, sum, s1, s2, s3);
+    for (int b = 0; b < MAXB; ++b) sum[b] = 0.f;
+    if (r < nrows) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+      uint4 wv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        wv[i] = *reinterpret_cast<const uint4*>(chunk + ((size_t)r * 64 + ((half * 4 + i + r) & 7) * 8) * 2);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int pc = (half * 4 + i + r) & 7;
+        float wf[8];
+        unpack8(wv[i], wf);
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b) {
+          if (b < B) {
+            const float4 y0 = *reinterpret_cast<const float4*>(s_y + b * 64 + pc * 8);
+            const float4 y1 = *reinterpret_cast<const float4*>(s_y + b * 64 + pc * 8 + 4);
+            sum[b] = fmaf(wf[0], y0.x, fmaf(wf[1], y0.y, fmaf(wf[2], y0.z, fmaf(wf[3], y0.w,
+                     fmaf(wf[4], y1.x, fmaf(wf[5], y1.y, fmaf(wf[6], y1.z, fmaf(wf[7], y1.w, sum[b]))))))));
+          }
+        }
+      }
+      }
+    }
+    const int n = nbase + cu * 32 + r;
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b) {
+      if (b < B) {
+        const float s1 = __shfl_down_sync(0xffffffffu, sum[b], 1);
+        const float s2 = __shfl_down_sync(0xffffffffu, sum[b], 2);
+        const float s3 = __shfl_down_sync(0xffffffffu, sum[b], 3);
+        if ((lane & 3) == 0 && r < nrows) {
+          red_add_v4(c.p.x + (size_t)b * d + n, sum[b], s1, s2, s3);
+          red_add_v4(c.p.x_in + (size_t)b * d + n, sum[b], s1, s2, s3);
         }
       }
     }
     chunk_release(c);
   }
+  stamp(c, li, PH_B, 3);
   grid_arrive(c, li, PH_B);
 }
 
@@ -728,9 +870,12 @@ __device__ void phase_b_attn(Ctx& c, int li) {
       cp_async16(c.kv + ((size_t)kvsel * kKvPos + pos) * HD + g * 8, src);
     }
   }
+  stamp(c, li, PH_B, 0);
   grid_wait(c, li, PH_A, c.NG);
+  stamp(c, li, PH_B, 1);
   cp_async_wait_all();
   csync();
+  stamp(c, li, PH_B, 2);
   const float scale = rsqrtf((float)HD);
   for (int item = first; item < items; item += c.NG) {
     const int b = item / (H * ns), h = (item / ns) % H, split = item % ns;
@@ -829,8 +974,11 @@ __device__ void phase_b_attn(Ctx& c, int li) {
 template <int MAXB>
 __device__ void phase_o(Ctx& c, int li) {
   const int d = c.d;
+  stamp(c, li, PH_O, 0);
   grid_wait(c, li, PH_B, c.B * c.H);
+  stamp(c, li, PH_O, 1);
   stage_copy(c, static_cast<const __nv_bfloat16*>(c.p.y), d);
+  stamp(c, li, PH_O, 2);
   int u0, u1;
   split_range(d / 2, c.NG, c.cta, u0, u1);
   const Seg s = get_seg(c, li, PH_O, 0);
@@ -842,6 +990,7 @@ __device__ void phase_o(Ctx& c, int li) {
     x[i] = nx;
     xin[i] = nx;
   });
+  stamp(c, li, PH_O, 3);
   grid_arrive(c, li, PH_O);
 }
 
@@ -850,9 +999,12 @@ template <int MAXB>
 __device__ void phase_c(Ctx& c, int li) {
   const dh_layer_params& lp = layer(c, li);
   const int d = c.d, B = c.B, tid = threadIdx.x;
-  if (lp.kind == 0) grid_wait(c, li, PH_B, c.H);
+  stamp(c, li, PH_C, 0);
+  if (lp.kind == 0) grid_wait(c, li, PH_B, c.H * kHeadParts);
   else grid_wait(c, li, PH_O, c.NG);
+  stamp(c, li, PH_C, 1);
   stage_norm<MAXB>(c, c.p.x_in, static_cast<const __nv_bfloat16*>(lp.norm2));
+  stamp(c, li, PH_C, 2);
   int j0, j1;
   split_range(c.ff, c.NG, c.cta, j0, j1);
   float* us = c.misc;  // [MAXB][kMaxUpc]
@@ -873,6 +1025,7 @@ __device__ void phase_c(Ctx& c, int li) {
     const int nj = min(upc, sd.units - cu);
     const uint8_t* chunk = chunk_acquire(c);
     if (nin) {
+#pragma unroll 4
       for (int j = 0; j < nj; ++j) {
         const uint2 wv = *reinterpret_cast<const uint2*>(chunk + ((size_t)j * d + n0) * 2);
         const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.x));
@@ -896,14 +1049,18 @@ __device__ void phase_c(Ctx& c, int li) {
     for (int b = 0; b < MAXB; ++b)
       if (b < B) red_add_v4(c.p.x + (size_t)b * d + n0, acc[b][0], acc[b][1], acc[b][2], acc[b][3]);
   }
+  stamp(c, li, PH_C, 3);
   grid_arrive(c, li, PH_C);
 }
 
 template <int MAXB>
 __device__ void phase_n(Ctx& c) {
-  const int d = c.d;
-  grid_wait(c, c.p.n_layers - 1, PH_C, c.NG);
+  const int d = c.d, nl = c.p.n_layers;
+  stamp(c, nl, 0, 0);
+  grid_wait(c, nl - 1, PH_C, c.NG);
+  stamp(c, nl, 0, 1);
   stage_norm<MAXB>(c, c.p.x, static_cast<const __nv_bfloat16*>(c.p.norm_out));
+  stamp(c, nl, 0, 2);
   int u0, u1;
   split_range((c.p.vocab + 1) / 2, c.G, c.cta, u0, u1);
   const Seg s = get_seg(c, c.p.n_layers, PH_N, 0);
@@ -912,6 +1069,7 @@ __device__ void phase_n(Ctx& c) {
   gemv_segment<MAXB>(c, s, d, u0, [&](int u, int b, int row, float v, float) {
     lg[(size_t)b * V + 2 * u + row] = f2bf(v);
   });
+  stamp(c, nl, 0, 3);
 }
 
 // ------------------------------------------------------------------ kernel
@@ -929,8 +1087,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   c.H = p.H;
   c.hd = p.hd;
   c.ff = p.ff;
-  c.NG = c.G - c.H;
-  c.head = c.cta >= c.NG ? c.cta - c.NG : -1;
+  c.NG = c.G - c.H * kHeadParts;
+  c.head = c.cta >= c.NG ? (c.cta - c.NG) / kHeadParts : -1;
+  c.hpart = c.cta >= c.NG ? (c.cta - c.NG) % kHeadParts : 0;
   c.wait_limit = wait_limit;
   {
     int ns = c.NG / (c.B * c.H);
@@ -938,7 +1097,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     c.nsplit = ns < p.nsplit ? ns : p.nsplit;
   }
   c.lg = 1;
-  while (c.lg < c.L && gate_chunk_bytes(c, 0, c.lg + 1) <= (uint32_t)kSlotBytes) ++c.lg;
+  while (c.lg < c.L && c.lg < kLgMax && gate_chunk_bytes(c, 0, c.lg + 1) <= (uint32_t)kSlotBytes)
+    ++c.lg;
   c.nslots = slots_for<MAXB>();
   c.slots = smem_raw;
   uint8_t* q = smem_raw + (size_t)c.nslots * kSlotBytes;
@@ -950,6 +1110,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   q += (size_t)kWarps * MAXB * kLmax * 3 * 4;
   c.misc = reinterpret_cast<float*>(q);
   q += (size_t)(MAXB * (4 * kLmax + 64 + kMaxUpc) + MAXB * kLmax * 32 + 2048) * 4;
+  static_assert(3 * kLmax + 64 + 32 + kLmax * 32 <= 4 * kLmax + 64 + kMaxUpc + kLmax * 32,
+                "head phase arrays fit the per-row scratch");
   c.full = reinterpret_cast<uint64_t*>(q);
   c.empty = c.full + c.nslots;
   c.abort = reinterpret_cast<volatile int*>(c.empty + c.nslots);
@@ -969,14 +1131,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     *c.abort = 0;
     fence_barrier_init();
   }
+  c.prod = reinterpret_cast<Prod*>(const_cast<int*>(reinterpret_cast<volatile int*>(c.abort)) + 4);
+  {  // the layer table, read once into shared memory
+    dh_layer_params* lay = reinterpret_cast<dh_layer_params*>(
+        reinterpret_cast<uint8_t*>(c.prod) + ((sizeof(Prod) + 15) / 16) * 16);
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.layers);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(lay);
+    const int words = p.n_layers * (int)(sizeof(dh_layer_params) / 8);
+    for (int i = threadIdx.x; i < words; i += kThreads) dst[i] = src[i];
+    c.lay = lay;
+  }
   __syncthreads();
-  if (threadIdx.x >= kCons) {  // producer warp
-    if (threadIdx.x == kCons) producer(c);
+  if (threadIdx.x == 0) {
+    Prod* pr = c.prod;
+    pr->pp = &p;
+    pr->lay = c.lay;
+    pr->emb = p.emb;
+    pr->vocab = p.vocab;
+    pr->max_len = p.max_len;
+    pr->n_layers = p.n_layers;
+    pr->G = c.G; pr->cta = c.cta; pr->NG = c.NG; pr->head = c.head; pr->hpart = c.hpart;
+    pr->B = c.B; pr->d = c.d; pr->gh = c.gh; pr->L = c.L; pr->H = c.H; pr->hd = c.hd;
+    pr->ff = c.ff; pr->lg = c.lg; pr->nslots = c.nslots; pr->t = c.t;
+    pr->wait_limit = c.wait_limit;
+    pr->slots = c.slots; pr->full = c.full; pr->empty = c.empty; pr->abort = c.abort;
+    pr->issued = 0; pr->pslot = 0; pr->peph = 0;
+    cursor_seek(pr, 0, 0, 0);
+  }
+  __syncthreads();
+  stamp(c, p.n_layers, 1, 0);
+  if (threadIdx.x >= kCons) {  // the producer warpgroup: one lane works, the rest leave
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProdRegs));
+    if (threadIdx.x == kCons) producer(c.prod, p.status);
     return;
   }
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsRegs));
   const int nl = p.n_layers;
   for (int li = 0; li < nl; ++li) {
-    const bool tree = p.layers[li].kind == 0;
+    const bool tree = c.lay[li].kind == 0;
     if (c.head < 0) {
       phase_a<MAXB>(c, li);
       if (tree) {
@@ -992,6 +1184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   phase_n<MAXB>(c);
   cp_async_wait_all();
+  stamp(c, p.n_layers, 1, 1);
   if (c.cta == 0 && threadIdx.x == 0) {
     p.t_buf[0] = c.t + 1;
     atomicAdd(p.barrier, 1ull);
@@ -1003,7 +1196,8 @@ size_t step_smem() {
   return (size_t)slots_for<MAXB>() * kSlotBytes + (size_t)MAXB * 1024 * 2 + (size_t)2 * kKvPos * 64 * 2 +
          (size_t)kWarps * MAXB * kLmax * 3 * 4 +
          (size_t)(MAXB * (4 * kLmax + 64 + kMaxUpc) + MAXB * kLmax * 32 + 2048) * 4 +
-         (size_t)2 * slots_for<MAXB>() * 8 + 64;
+         (size_t)2 * slots_for<MAXB>() * 8 + 64 + ((sizeof(Prod) + 15) / 16) * 16 +
+         (size_t)kMaxLayers * sizeof(dh_layer_params);
 }
 
 template <int MAXB>
@@ -1018,21 +1212,32 @@ int launch_step(const dh_step_params& p, cudaStream_t st) {
     configured_dev = dev;
   }
   int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel<MAXB>, kThreads, smem);
-  DH_REQUIRE(per_sm >= 1, DH_ERR_SHAPE, "dh_decode_step: kernel does not fit on an SM");
+  const cudaError_t occ =
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel<MAXB>, kThreads, smem);
+  if (per_sm < 1) {
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, step_kernel<MAXB>);
+    return set_error(DH_ERR_SHAPE,
+                     "dh_decode_step: kernel does not fit on an SM (%s; %d regs, %zu B smem "
+                     "requested, max dynamic %d, max threads %d)",
+                     cudaGetErrorString(occ), fa.numRegs, smem, fa.maxDynamicSharedSizeBytes,
+                     fa.maxThreadsPerBlock);
+  }
   const int G = sm_count();
-  DH_REQUIRE(G - p.H >= 16, DH_ERR_SHAPE, "dh_decode_step: %d SMs leave too few GEMV CTAs", G);
+  DH_REQUIRE(G - p.H * kHeadParts >= 16, DH_ERR_SHAPE,
+             "dh_decode_step: %d SMs leave too few GEMV CTAs", G);
   {  // the attention scores of one item live in the per-phase scratch
     const int span = (p.window > 0 && p.window < p.max_len) ? p.window : p.max_len;
-    int ns = (G - p.H) / (p.batch * p.H);
+    int ns = (G - p.H * kHeadParts) / (p.batch * p.H);
     ns = ns < 1 ? 1 : (ns < p.nsplit ? ns : p.nsplit);
     const int chunk = (span + ns - 1) / ns;
     const int misc = MAXB * (4 * kLmax + 64 + kMaxUpc) + MAXB * kLmax * 32 + 2048;
     DH_REQUIRE(chunk + 64 + 8 + kWarps * 64 + 4 <= misc, DH_ERR_SHAPE,
                "dh_decode_step: %d window positions per attention item exceed the scratch", chunk);
   }
-  DH_REQUIRE((p.ff + (G - p.H) - 1) / (G - p.H) <= kMaxUpc, DH_ERR_SHAPE,
-             "dh_decode_step: FFN width %d too large for %d CTAs", p.ff, G - p.H);
+  DH_REQUIRE((p.ff + (G - p.H * kHeadParts) - 1) / (G - p.H * kHeadParts) <= kMaxUpc,
+             DH_ERR_SHAPE, "dh_decode_step: FFN width %d too large for %d CTAs", p.ff,
+             G - p.H * kHeadParts);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kThreads);
@@ -1063,7 +1268,7 @@ extern "C" int dh_decode_step(const dh_step_params* params, void* stream) {
              p.batch);
   DH_REQUIRE(p.hd == 64 && p.d == p.H * p.hd && p.d % 64 == 0 && p.d <= 1024 && p.ff % 8 == 0 &&
                  p.L >= 1 && p.L <= kLmax && p.nsplit >= 1 && p.n_layers >= 1 &&
-                 p.n_layers * 5 + 2 <= (DH_STEP_SYNC_WORDS / kSyncStride),
+                 p.n_layers <= kMaxLayers,
              DH_ERR_SHAPE, "dh_decode_step: unsupported shape (d=%d H=%d hd=%d ff=%d L=%d layers=%d)",
              p.d, p.H, p.hd, p.ff, p.L, p.n_layers);
   DH_REQUIRE(4 * p.d <= kSlotBytes && 3 * p.d * 2 + p.batch * p.d * 2 <= kSlotBytes, DH_ERR_SHAPE,

@@ -22,7 +22,7 @@ class StepParams(ctypes.Structure):
                 ("tokens", _p), ("t_buf", _p), ("emb", _p), ("norm_out", _p), ("rope_cos", _p),
                 ("rope_sin", _p), ("layers", _p), ("logits", _p), ("x", _p), ("x_in", _p),
                 ("a", _p), ("v0", _p), ("y", _p), ("q", _p), ("part", _p), ("counters", _p),
-                ("barrier", _p), ("status", _p)]
+                ("barrier", _p), ("status", _p), ("trace", _p)]
 
 
 SYNC_WORDS = 4096   # DH_STEP_SYNC_WORDS

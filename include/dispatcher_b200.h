@@ -327,7 +327,16 @@ typedef struct {
   int* counters;
   unsigned long long* barrier;
   int* status;
+  /* nullable: when set, thread 0 of CTA c writes the global timer (ns) at
+   * trace[c * DH_STEP_TRACE_WORDS + (layer * 5 + phase) * 4 + k] for k =
+   * 0 phase entry, 1 after its hand-off wait, 2 after its input staging,
+   * 3 before its arrival (phase: 0 projections, 1 gates / attention,
+   * 2 attention out-projection, 3 FFN; at layer n_layers: phase 0 the
+   * logits, phase 1 k = 0, 1 the CTA's start and end) */
+  unsigned long long* trace;
 } dh_step_params;
+
+#define DH_STEP_TRACE_WORDS 512
 
 /* One whole lockstep decode step (embedding, every block, logits, t += 1)
  * as ONE persistent cooperative kernel, one CTA per SM: the last H CTAs run
