@@ -1,29 +1,44 @@
 // Whole decode step as ONE persistent cooperative kernel (one CTA per SM).
 //
-// Roles.  The last H CTAs are "head" CTAs (one per attention head of the
+// Roles.  The last 2H CTAs are "head" CTAs (two per attention head of the
 // mixer); the others are "GEMV" CTAs.  A tree block is three dependent
 // phases:
 //   A  (GEMV CTAs)  h = RMSNorm(x); [v0 | A | B_hist[t]] = W3 h
 //   B  (head CTAs)  head h: the gate readouts of all levels
-//                   (relu^2(A + B_hist[t - 2^l]) . W_l), the level recurrence
-//                   over the ring buffers, and the head's share of the output
-//                   projection, added into the residual with vector atomics
+//                   (W_l . relu^2(A + B_hist[t - 2^l])), the level recurrence
+//                   over the ring buffers, and half of the head's share of the
+//                   output projection, added into the residual
 //   C  (GEMV CTAs)  h2 = RMSNorm(x); u = silu(Wg h2) * (Wu h2) for this CTA's
-//                   slice of the FFN width; x += Wd[:, slice] u (vector atomics)
+//                   slice of the FFN width; x += Wd[:, slice] u
 // An attention block is A (q, k, v with RoPE, cache write), B (window
 // attention split over the GEMV CTAs, last-arriver combine), O (output
 // projection, rows owned) and C.  The step ends with the logits on all CTAs.
 // This follows the reference's fused step (decoding.py:457-488 with
 // fused_step.py:26-88) and attention step (decoding.py:411-435).
 //
-// Weights never depend on activations, so each CTA's producer lane streams
-// its slices of every phase of the step, in consumption order, by bulk async
-// copies (cp.async.bulk) into a ring of shared-memory slots that runs ahead of
-// the phase waits; history rows the head CTAs need (B_hist at t - 2^l)
-// travel in the same stream, and ring slots, transmit gates at the source
-// positions and the attention window's keys and values (all written by
-// earlier steps) are loaded before each wait.  After a wait a phase reads
-// only the small activation vector and computes from shared memory.
+// Arithmetic.  Every weight contraction runs on the tensor cores as
+// mma.sync.m16n8k16 (bf16 operands from shared memory through ldmatrix, fp32
+// accumulators): a CUDA-core dot product needs ~17 instructions per 16 bytes
+// of bf16 weights (load, eight conversions, eight FMAs), which caps a whole
+// step at ~550 us on 148 SMs, while one mma consumes 512 bytes of weights.
+// The N = 8 columns of an mma hold the lockstep rows.  tcgen05.mma is not used
+// here: a CTA owns only a few 16-row tiles of each matrix and a tcgen05
+// instruction costs ~120-130 cycles whatever its N, so a 1024-wide row block
+// would take >= 64 instructions (~4 us) per phase.  K is split over the 8
+// consumer warps; their partial tiles meet in shared memory.  Weights are
+// stored in HBM with the 16-byte chunks of every row XOR-permuted by
+// (row & 7) (packed once by the host), so a linear bulk copy lands them in a
+// layout whose ldmatrix reads are free of bank conflicts.
+//
+// Streaming.  Weights never depend on activations, so each CTA's producer
+// lane streams its slices of every phase of the step, in consumption order,
+// by bulk async copies (cp.async.bulk) into a ring of shared-memory slots
+// that runs ahead of the phase waits; history rows the head CTAs need
+// (B_hist at t - 2^l) travel in the same stream, and ring slots, transmit
+// gates at the source positions and the attention window's keys and values
+// (all written by earlier steps) are loaded before each wait.  After a wait
+// a phase reads only the small activation vector and computes from shared
+// memory.
 //
 // Hand-off: a phase's CTAs add 1 to its own monotonically increasing 64-bit
 // counter with release semantics after their writes; waiters spin on it with
@@ -52,14 +67,14 @@ constexpr int kProdRegs = 56;
 constexpr int kConsRegs = 224;
 static_assert(128 * kProdRegs + kCons * kConsRegs <= kThreads * 168, "register split exceeds the launch");
 constexpr int kSlotBytes = 32 * 1024;
-// ring depth: 5 slots up to 2 lockstep rows, 4 from 4 rows (their staging needs the room)
-template <int MAXB>
-constexpr int slots_for() { return MAXB >= 4 ? 4 : 5; }
+constexpr int kSlots = 5;
+constexpr int kMaxB = 2;                     // lockstep rows of this kernel
 constexpr int kKvPos = 128;                  // window positions staged per attention item
 constexpr int kHeadParts = 2;                // head CTAs per head (each takes half the out-projection rows)
-constexpr int kLgMax = 4;                    // levels per gate chunk
 constexpr int kLmax = 16;
 constexpr int kMaxUpc = 32;                  // FFN elements per GEMV CTA
+constexpr int kMaxD = 1024;
+constexpr int kMisc = 4096;                  // floats of per-phase scratch
 constexpr float kEps = 1.1920928955078125e-07f;  // torch RMSNorm eps=None in fp32
 constexpr uint32_t kDrainLimit = 1u << 20;
 constexpr int kSyncStride = 32;              // uint64 words between two phase counters
@@ -82,10 +97,11 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 __device__ __forceinline__ void red_release_u64(unsigned long long* p) {
   asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(p) : "memory");
 }
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
-               "f"(d)
-               : "memory");
+__device__ __forceinline__ void red_add_f32(float* p, float a) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory");
+}
+__device__ __forceinline__ void red_add_v2(float* p, float a, float b) {
+  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
 }
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -99,37 +115,45 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// After this, lane l holds the warp-wide sum of v[l % NV] (NV a power of two <= 32).
-template <int NV>
-__device__ __forceinline__ float transpose_reduce(float (&v)[NV]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int n = NV; n > 1; n >>= 1) {
-    const int o = n >> 1;
-    const bool upper = (lane & o) != 0;
-#pragma unroll
-    for (int i = 0; i < n / 2; ++i) {
-      const float send = upper ? v[i] : v[i + n / 2];
-      const float keep = upper ? v[i + n / 2] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-    }
-  }
-  float r = v[0];
-#pragma unroll
-  for (int o = NV; o < 32; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
-  return r;
+// tensor-core fragments (m16n8k16, bf16 in, fp32 accumulate)
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t (&r)[2], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+// byte offset of 16-byte chunk `ch` of row `r` in a swizzled tile of rows of `rb` bytes
+__device__ __forceinline__ uint32_t swz(int r, int ch, int rb) {
+  return (uint32_t)(r * rb + ((ch ^ (r & 7)) << 4));
 }
 
 // ------------------------------------------------------------------ the plan
-// A segment is a run of equal units of one weight matrix (or of history rows)
-// that this CTA streams for one phase; chunks are whole units, <= one slot.
-enum { SEG_ROWS = 0, SEG_GATES = 1 };
+// A segment is a run of equal units of one matrix (or of history rows) that
+// this CTA streams for one phase; a chunk is up to one slot of whole units.
+enum { SEG_ROWS = 0, SEG_BHIST = 1 };
 struct Seg {
   const uint8_t* base;
-  uint32_t unit_bytes;  // SEG_GATES: bytes of one level's weights (3 gh bf16)
+  uint32_t unit_bytes;
   int units;
   int kind;
-  size_t limit;         // bytes readable from base (the last unit may be short)
+  size_t limit;   // bytes readable from base (the last unit may be short)
+  int per_chunk;  // units per chunk
 };
 
 struct Ctx {
@@ -141,18 +165,18 @@ struct Ctx {
   unsigned long long gen;
   uint32_t wait_limit;
   int nsplit;            // attention splits per (row, head)
-  int lg;                // levels per gate chunk
   int nslots;            // ring slots
   // shared memory
   uint8_t* slots;
   uint64_t* full;
   uint64_t* empty;
   volatile int* abort;
-  __nv_bfloat16* xs;     // staged activation rows [MAXB][1024]
-  float* red;            // reductions
+  __nv_bfloat16* xs;     // staged activation rows [kMaxB][kMaxD], chunk-swizzled
+  __nv_bfloat16* zrow;   // a row of zeros (kMaxD)
+  float* red;            // partial tiles / reductions
   float* misc;           // small per-phase arrays
   __nv_bfloat16* kv;     // [2][kKvPos][hd]
-  int consumed;          // chunks consumed (same in every consumer thread)
+  int acq, rel;          // chunks acquired / released (same in every consumer thread)
   struct Prod* prod;     // the weight stream (shared memory; the producer lane)
   const dh_layer_params* lay;  // the layer table, copied into shared memory
 };
@@ -160,11 +184,10 @@ struct Ctx {
 // The weight stream's state, in shared memory, used by the producer lane: a
 // copy of the CTA's geometry and the cursor of the next chunk.
 struct Prod {
-  const dh_step_params* pp;
-  const dh_layer_params* lay;  // shared-memory copy of the layer table
-  const void* emb;
+  const dh_layer_params* lay;
+  const void* lm_head;
   int vocab, max_len, n_layers;
-  int G, cta, NG, head, hpart, B, d, gh, L, H, hd, ff, lg, nslots;
+  int G, cta, NG, head, hpart, B, d, gh, L, H, hd, ff, nslots;
   long long t;
   uint32_t wait_limit;
   uint8_t* slots;
@@ -179,12 +202,12 @@ struct Prod {
   long issued;            // chunks issued so far
 };
 
-// the few step parameters the plan needs, for both the consumers' context
-// and the issuer's shared-memory copy
+// the few step parameters the plan needs, for the consumers' context and for
+// the issuer's shared-memory copy
 __device__ __forceinline__ int vocab_of(const Ctx& c) { return c.p.vocab; }
 __device__ __forceinline__ int vocab_of(const Prod& c) { return c.vocab; }
-__device__ __forceinline__ const void* emb_of(const Ctx& c) { return c.p.emb; }
-__device__ __forceinline__ const void* emb_of(const Prod& c) { return c.emb; }
+__device__ __forceinline__ const void* lm_head_of(const Ctx& c) { return c.p.lm_head; }
+__device__ __forceinline__ const void* lm_head_of(const Prod& c) { return c.lm_head; }
 
 template <class C>
 __device__ __forceinline__ const dh_layer_params& layer(const C& c, int li) { return c.lay[li]; }
@@ -198,12 +221,17 @@ __device__ __forceinline__ void stamp(const Ctx& c, int li, int ph, int k) {
   }
 }
 
+// bytes between two history rows in a B_hist chunk: one 16-byte chunk more
+// than a row, so the rows of an ldmatrix read fall in different banks
+template <class C>
+__device__ __forceinline__ int bh_stride(const C& c) { return c.gh * 2 + 16; }
+
 // number of segments of (layer li, phase ph) for this CTA, and segment si
 template <class C>
 __device__ int seg_count(const C& c, int li, int ph) {
   if (ph == PH_N) return 1;
   const bool tree = layer(c, li).kind == 0;
-  if (c.head >= 0) return (tree && ph == PH_B) ? 2 : 0;
+  if (c.head >= 0) return (tree && ph == PH_B) ? 3 : 0;
   if (ph == PH_A || ph == PH_O) return (ph == PH_O && tree) ? 0 : 1;
   if (ph == PH_C) return 2;
   return 0;
@@ -211,74 +239,74 @@ __device__ int seg_count(const C& c, int li, int ph) {
 
 template <class C>
 __device__ Seg get_seg(const C& c, int li, int ph, int si) {
-  Seg s{nullptr, 1, 0, SEG_ROWS, 0};
+  Seg s{nullptr, 1, 0, SEG_ROWS, 0, 1};  // one tile per chunk unless stated
   const int d = c.d;
-  if (ph == PH_N) {  // lm_head row pairs, split over every CTA
+  if (ph == PH_N) {  // 16-row tiles of the (swizzled) lm_head, split over every CTA
+    const int V = vocab_of(c);
     int u0, u1;
-    const int units = (vocab_of(c) + 1) / 2;
-    split_range(units, c.G, c.cta, u0, u1);
-    s.base = static_cast<const uint8_t*>(emb_of(c)) + (size_t)u0 * 4 * d;
-    s.unit_bytes = 4 * d;
+    split_range((V + 15) / 16, c.G, c.cta, u0, u1);
+    s.base = static_cast<const uint8_t*>(lm_head_of(c)) + (size_t)u0 * 32 * d;
+    s.unit_bytes = 32 * d;
     s.units = u1 - u0;
-    s.limit = (size_t)vocab_of(c) * d * 2 - (size_t)u0 * 4 * d;
+    s.limit = (size_t)V * d * 2 - (size_t)u0 * 32 * d;
     return s;
   }
   const dh_layer_params& lp = layer(c, li);
-  if (c.head >= 0) {  // tree block B: gates (+ history rows), then the out-projection block
+  if (c.head >= 0) {  // tree block B: history rows, gate readout tiles, out-projection rows
     if (si == 0) {
-      s.base = static_cast<const uint8_t*>(lp.w_gates) + (size_t)c.head * c.L * 3 * c.gh * 2;
-      s.unit_bytes = 3 * c.gh * 2;
-      s.units = c.L;
-      s.kind = SEG_GATES;
+      s.base = static_cast<const uint8_t*>(lp.b_hist);
+      s.unit_bytes = (uint32_t)(c.L * bh_stride(c));  // one lockstep row's L history rows
+      s.units = c.B;
+      s.kind = SEG_BHIST;
+    } else if (si == 1) {  // three 16-row tiles: admit, forget, transmit rows of every level
+      s.base = static_cast<const uint8_t*>(lp.w_gates) + (size_t)c.head * 3 * 16 * c.gh * 2;
+      s.unit_bytes = 16 * c.gh * 2;
+      s.units = 3;
     } else {  // this CTA's half of the output rows, head h's columns
       s.base = static_cast<const uint8_t*>(lp.w_out) +
                ((size_t)c.head * d + (size_t)c.hpart * (d / kHeadParts)) * c.hd * 2;
-      s.unit_bytes = 32 * c.hd * 2;  // 32 output rows
-      s.units = d / kHeadParts / 32;
+      s.unit_bytes = 16 * c.hd * 2;  // one 16-row tile
+      s.units = d / kHeadParts / 16;
+      s.per_chunk = kSlotBytes / (16 * c.hd * 2);
     }
     s.limit = (size_t)s.units * s.unit_bytes;
     return s;
   }
   const int gi = c.cta;
   int u0, u1;
-  if (ph == PH_A || ph == PH_O) {  // row pairs of W3 / Wqkv / W_out
-    const int units = ph == PH_A ? 3 * d / 2 : d / 2;
+  if (ph == PH_A || ph == PH_O) {  // 16-row tiles of W3 / Wqkv / W_out
+    const int units = ph == PH_A ? 3 * d / 16 : d / 16;
     split_range(units, c.NG, gi, u0, u1);
-    s.base = static_cast<const uint8_t*>(ph == PH_A ? lp.w_in3 : lp.w_out) + (size_t)u0 * 4 * d;
-    s.unit_bytes = 4 * d;
-  } else {  // PH_C: (gate, up) row pairs, then rows of Wd^T, for the same FFN slice
-    split_range(c.ff, c.NG, gi, u0, u1);
+    s.base = static_cast<const uint8_t*>(ph == PH_A ? lp.w_in3 : lp.w_out) + (size_t)u0 * 32 * d;
+    s.unit_bytes = 32 * d;
+    s.units = u1 - u0;
+    s.limit = (size_t)s.units * s.unit_bytes;
+  } else {  // PH_C: 16-row tiles of (gate, up) row pairs (8 FFN columns each), then Wd^T rows
+    split_range(c.ff / 8, c.NG, gi, u0, u1);
     if (si == 0) {
-      s.base = static_cast<const uint8_t*>(lp.w_gu) + (size_t)u0 * 4 * d;
-      s.unit_bytes = 4 * d;
-    } else {
-      s.base = static_cast<const uint8_t*>(lp.w_down) + (size_t)u0 * 2 * d;
-      s.unit_bytes = 2 * d;
+      s.base = static_cast<const uint8_t*>(lp.w_gu) + (size_t)u0 * 32 * d;
+      s.unit_bytes = 32 * d;
+      s.units = u1 - u0;
+      s.limit = (size_t)s.units * s.unit_bytes;
+    } else {  // 16-row tiles of Wd^T over the same 8 (u1 - u0) FFN columns
+      const int jn = 8 * (u1 - u0);
+      s.base = static_cast<const uint8_t*>(lp.w_down) + (size_t)u0 * 8 * 2 * d;
+      s.unit_bytes = 32 * d;
+      s.units = (jn + 15) / 16;
+      s.limit = (size_t)jn * 2 * d;
     }
   }
-  s.units = u1 - u0;
-  s.limit = (size_t)s.units * s.unit_bytes;
   return s;
 }
 
 template <class C>
-__device__ __forceinline__ int units_per_chunk(const C& c, const Seg& s) {
-  if (s.kind == SEG_GATES) return c.lg;
-  const int n = kSlotBytes / (int)s.unit_bytes;
-  return n < 1 ? 1 : n;
-}
-
-// bytes of a gate chunk: levels [l0, l1) of weights, then the history rows
-// B_hist[b, t - 2^l] of those levels for every lockstep row
-template <class C>
-__device__ __forceinline__ uint32_t gate_chunk_bytes(const C& c, int l0, int l1) {
-  return (uint32_t)(l1 - l0) * 3 * c.gh * 2 + (uint32_t)(l1 - l0) * c.B * c.gh * 2;
-}
+__device__ __forceinline__ int units_per_chunk(const C&, const Seg& s) { return s.per_chunk; }
 
 // ------------------------------------------------------------------ the weight stream
 // The producer lane issues the CTA's chunks in plan order, each as soon as
 // every consumer warp released the slot: for every layer the phases A, B, O,
 // C in order, then the logits; in each phase this CTA's segments.
+
 // move the cursor to the first non-empty segment at or after (li, ph, si)
 __device__ __forceinline__ void cursor_seek(Prod* pr, int li, int ph, int si) {
   const int nl = pr->n_layers;
@@ -311,23 +339,19 @@ __device__ __forceinline__ void issue_chunk(Prod* pr) {
   const int slot = pr->pslot;
   uint8_t* dst = pr->slots + (size_t)slot * kSlotBytes;
   uint64_t* bar = &pr->full[slot];
-  if (s.kind == SEG_GATES) {
-    const dh_layer_params& lp = layer(*pr, pr->cli);
-    const uint32_t wbytes = (uint32_t)n * s.unit_bytes;
-    const int B = pr->B, gh = pr->gh;
+  if (s.kind == SEG_BHIST) {  // lockstep row u: its history rows of every level
+    const int gh = pr->gh, L = pr->L, stride = bh_stride(*pr);
     const long long t = pr->t;
-    uint32_t total = wbytes;
-    for (int l = u; l < u + n; ++l)
-      if (t - (1ll << l) >= 0) total += (uint32_t)B * gh * 2;
+    uint32_t total = 0;
+    for (int l = 0; l < L; ++l)
+      if (t - (1ll << l) >= 0) total += (uint32_t)gh * 2;
     mbar_arrive_expect_tx(bar, total);
-    bulk_g2s(dst, s.base + (size_t)u * s.unit_bytes, wbytes, bar);
-    const __nv_bfloat16* bh = static_cast<const __nv_bfloat16*>(lp.b_hist);
-    for (int l = u; l < u + n; ++l) {
+    const __nv_bfloat16* bh = reinterpret_cast<const __nv_bfloat16*>(s.base);
+    for (int l = 0; l < L; ++l) {
       const long long src = t - (1ll << l);
       if (src < 0) continue;
-      for (int b = 0; b < B; ++b)
-        bulk_g2s(dst + wbytes + ((size_t)(l - u) * B + b) * gh * 2,
-                 bh + ((size_t)b * pr->max_len + src) * gh, (uint32_t)gh * 2, bar);
+      bulk_g2s(dst + (size_t)l * stride, bh + ((size_t)u * pr->max_len + src) * gh, (uint32_t)gh * 2,
+               bar);
     }
   } else {
     const size_t off = (size_t)u * s.unit_bytes;
@@ -345,10 +369,10 @@ __device__ __forceinline__ void issue_chunk(Prod* pr) {
   if (pr->cu >= s.units) cursor_seek(pr, pr->cli, pr->cph, pr->csi + 1);
 }
 
-// The producer (one lane of the last warp): walks the plan, waiting (bounded)
-// for each slot to be released by every consumer warp before refilling it;
-// stops at the first failed wait or when a consumer aborted, and finally waits
-// (with a fixed bound) for the copies it issued.
+// The producer (one lane of the producer warpgroup): walks the plan, waiting
+// (bounded) for each slot to be released by every consumer warp before
+// refilling it; stops at the first failed wait or when a consumer aborted,
+// and finally waits (with a fixed bound) for the copies it issued.
 __device__ void producer(Prod* pr, int* status) {
   while (pr->cvalid && !*pr->abort) {
     if (pr->issued >= pr->nslots &&
@@ -366,10 +390,12 @@ __device__ void producer(Prod* pr, int* status) {
 }
 
 // ------------------------------------------------------------------ consumer helpers
+// Chunks are acquired and released in stream order; a phase may hold several.
 __device__ __forceinline__ const uint8_t* chunk_acquire(Ctx& c) {
-  const int slot = c.consumed % c.nslots;
+  const int k = c.acq++;
+  const int slot = k % c.nslots;
   if (!*c.abort) {
-    if (!mbar_wait(&c.full[slot], (uint32_t)((c.consumed / c.nslots) & 1), c.p.status, c.wait_limit))
+    if (!mbar_wait(&c.full[slot], (uint32_t)((k / c.nslots) & 1), c.p.status, c.wait_limit))
       *c.abort = 1;
   }
   return c.slots + (size_t)slot * kSlotBytes;
@@ -377,8 +403,8 @@ __device__ __forceinline__ const uint8_t* chunk_acquire(Ctx& c) {
 
 __device__ __forceinline__ void chunk_release(Ctx& c) {
   __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(&c.empty[c.consumed % c.nslots]);
-  c.consumed += 1;
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&c.empty[c.rel % c.nslots]);
+  c.rel += 1;
 }
 
 __device__ __forceinline__ unsigned long long* phase_ctr(const Ctx& c, int li, int ph) {
@@ -411,17 +437,38 @@ __device__ __forceinline__ void grid_arrive(Ctx& c, int li, int ph) {
   if (threadIdx.x == 0) red_release_u64(phase_ctr(c, li, ph));
 }
 
+// xs row b, element k (a row is kMaxD wide, its 16-byte chunks XOR-permuted by b)
+__device__ __forceinline__ __nv_bfloat16* xs_at(const Ctx& c, int b, int k) {
+  return c.xs + (size_t)b * kMaxD + (((k >> 3) ^ (b & 7)) << 3) + (k & 7);
+}
+
 // xs[b][k] = bf16(x[b][k] * rsqrt(mean(x[b]^2) + eps) * w[k]) for every lockstep row;
 // x comes from `xf` (fp32, read through L2) or, for the first block, from the
 // embedding rows of the step's tokens.  The same loads also write this CTA's
 // slice [e0, e1) (float4 units) of x into dst0 / dst1 when they are set.
-template <int MAXB>
-__device__ void stage_norm(Ctx& c, const float* xf, const __nv_bfloat16* w, float* dst0 = nullptr,
+// The norm weights this thread multiplies by, w[k..k+3] of each of its float4
+// units (constant: loaded before the phase's wait).
+constexpr int kNV = (kMaxB * kMaxD + kCons * 4 - 1) / (kCons * 4);
+struct NormW {
+  uint2 w[kNV];
+};
+__device__ __forceinline__ NormW load_normw(const Ctx& c, const __nv_bfloat16* w) {
+  NormW nw;
+  const int d4 = c.d / 4, n4 = c.B * d4;
+#pragma unroll
+  for (int j = 0; j < kNV; ++j) {
+    const int i = threadIdx.x + j * kCons;
+    nw.w[j] = i < n4 ? *reinterpret_cast<const uint2*>(w + (i - (i / d4) * d4) * 4) : make_uint2(0, 0);
+  }
+  return nw;
+}
+
+__device__ void stage_norm(Ctx& c, const float* xf, const NormW& nw, float* dst0 = nullptr,
                            float* dst1 = nullptr, int e0 = 0, int e1 = 0) {
   const int B = c.B, d = c.d, d4 = d / 4, n4 = B * d4;
-  constexpr int NV = (MAXB * 1024 + kCons * 4 - 1) / (kCons * 4);
-  float* ssum = c.red;  // [MAXB]
-  if (threadIdx.x < MAXB) ssum[threadIdx.x] = 0.f;
+  constexpr int NV = kNV;
+  float* ssum = c.misc + kMisc - kMaxB;  // [kMaxB]
+  if (threadIdx.x < kMaxB) ssum[threadIdx.x] = 0.f;
   float4 v[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
@@ -432,7 +479,7 @@ __device__ void stage_norm(Ctx& c, const float* xf, const __nv_bfloat16* w, floa
         v[j] = __ldcg(reinterpret_cast<const float4*>(xf + (size_t)b * d + k));
       } else {
         long long tok = c.p.tokens[b];
-        if (tok < 0 || tok >= c.p.vocab) tok = 0;  // reported by the phase that owns the row
+        if (tok < 0 || tok >= c.p.vocab) tok = 0;  // reported by phase A of the first block
         const uint2 e = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(c.p.emb) +
                                                         (size_t)tok * d + k);
         const float2 e01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&e.x));
@@ -468,99 +515,95 @@ __device__ void stage_norm(Ctx& c, const float* xf, const __nv_bfloat16* w, floa
     if (i < n4) {
       const int b = i / d4, k = (i - b * d4) * 4;
       const float r = rsqrtf(ssum[b] / (float)d + kEps);
-      const uint2 wv = *reinterpret_cast<const uint2*>(w + k);
+      const uint2 wv = nw.w[j];
       const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.x));
       const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.y));
       uint2 pk;
       pk.x = pack2(v[j].x * r * w01.x, v[j].y * r * w01.y);
       pk.y = pack2(v[j].z * r * w23.x, v[j].w * r * w23.y);
-      *reinterpret_cast<uint2*>(c.xs + (size_t)b * 1024 + k) = pk;
+      *reinterpret_cast<uint2*>(xs_at(c, b, k)) = pk;
     }
   }
   csync();
 }
 
-// xs[b][0:K] = src[b][0:K] (bf16 produced by another CTA)
+// xs rows = src[b][0:K] (bf16 produced by another CTA)
 __device__ void stage_copy(Ctx& c, const __nv_bfloat16* src, int K) {
   const int k8 = K / 8, n = c.B * k8;
   for (int i = threadIdx.x; i < n; i += kCons) {
     const int b = i / k8, k = (i - b * k8) * 8;
-    *reinterpret_cast<uint4*>(c.xs + (size_t)b * 1024 + k) =
+    *reinterpret_cast<uint4*>(xs_at(c, b, k)) =
         __ldcg(reinterpret_cast<const uint4*>(src + (size_t)b * K + k));
   }
   csync();
 }
 
-// acc[0..MAXB) += row r0 . xs[b], acc[MAXB..2MAXB) += row r1 . xs[b]  (this lane's k slice)
-template <int MAXB>
-__device__ __forceinline__ void dot_pair(const __nv_bfloat16* r0, const __nv_bfloat16* r1, int K,
-                                         const __nv_bfloat16* xs, int B, float (&acc)[2 * MAXB]) {
-  const int lane = threadIdx.x & 31;
+// B fragments of the staged rows for this warp's K range: k-step i covers
+// columns [(warp * ksw + i) * 16, +16); columns n of the mma are the lockstep
+// rows (rows >= B read zeros)
+__device__ __forceinline__ void load_xfrags(const Ctx& c, int ksw, uint32_t (&bx)[8][2]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = lane & 7, half = (lane >> 3) & 1;
 #pragma unroll
-  for (int i = 0; i < 2 * MAXB; ++i) acc[i] = 0.f;
-  uint4 wa[4], wb[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {  // K <= 1024: every load of the row pair up front
-    const int k = lane * 8 + i * 256;
-    if (k < K) {
-      wa[i] = *reinterpret_cast<const uint4*>(r0 + k);
-      wb[i] = *reinterpret_cast<const uint4*>(r1 + k);
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int k = lane * 8 + i * 256;
-    if (k >= K) break;
-    float fa[8], fb[8];
-    unpack8(wa[i], fa);
-    unpack8(wb[i], fb);
-#pragma unroll
-    for (int b = 0; b < MAXB; ++b) {
-      if (b < B) {
-        float fx[8];
-        unpack8(*reinterpret_cast<const uint4*>(xs + (size_t)b * 1024 + k), fx);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          acc[b] = fmaf(fa[j], fx[j], acc[b]);
-          acc[MAXB + b] = fmaf(fb[j], fx[j], acc[MAXB + b]);
-        }
-      }
+  for (int i = 0; i < 8; ++i) {
+    if (i < ksw) {
+      const int ch = (warp * ksw + i) * 2 + half;
+      const __nv_bfloat16* row = n < c.B ? c.xs + (size_t)n * kMaxD + ((ch ^ (n & 7)) << 3)
+                                         : c.zrow + (ch << 3);
+      ldsm_x2(bx[i], smem_u32(row));
     }
   }
 }
 
-// Consume segment `s` (row pairs of a K-wide matrix) against xs; `store(u, b,
-// row, v, other, has1)` receives unit u's row `row` for lockstep row b.
-template <int MAXB, class Store>
-__device__ void gemv_segment(Ctx& c, const Seg& s, int K, int unit0, Store store) {
+// One segment of 16-row tiles (one tile per chunk) against the staged rows:
+// each warp contracts its K range, the partial tiles meet in shared memory,
+// and threads (row pair p, lockstep row b) run epi(tile, p, b, v_even, v_odd).
+template <class Epi>
+__device__ void gemv_tiles(Ctx& c, const Seg& s, const uint32_t (&bx)[8][2], int ksw, Epi epi) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int upc = units_per_chunk(c, s);
-  for (int cu = 0; cu < s.units; cu += upc) {
-    const int n = min(upc, s.units - cu);
+  const int g = lane >> 2, t4 = lane & 3;
+  const int rb = c.d * 2;  // bytes of a weight row
+  const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, ahalf = lane >> 4;
+  for (int u = 0; u < s.units; ++u) {
     const uint8_t* chunk = chunk_acquire(c);
-    for (int u = warp; u < n; u += kWarps) {
-      const size_t off = (size_t)(cu + u) * s.unit_bytes;
-      const __nv_bfloat16* r0 = reinterpret_cast<const __nv_bfloat16*>(chunk + (size_t)u * s.unit_bytes);
-      const bool has1 = off + s.unit_bytes <= s.limit;
-      const __nv_bfloat16* r1 = has1 ? r0 + K : r0;
-      float acc[2 * MAXB];
-      dot_pair<MAXB>(r0, r1, K, c.xs, c.B, acc);
-      const float r = transpose_reduce<2 * MAXB>(acc);
-      const float other = __shfl_xor_sync(0xffffffffu, r, MAXB);
-      const int b = lane % MAXB, row = (lane / MAXB) & 1;
-      if (lane < 2 * MAXB && b < c.B && (row == 0 || has1)) store(unit0 + cu + u, b, row, r, other);
+    const uint32_t base = smem_u32(chunk);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i < ksw) {
+        uint32_t a[4];
+        ldsm_x4(a, base + swz(arow, (warp * ksw + i) * 2 + ahalf, rb));
+        mma16816(acc, a, bx[i]);
+      }
     }
+    float* pb = c.red + ((size_t)(u & 1) * kWarps + warp) * 16 * 8;  // [16 rows][8 columns]
+    pb[g * 8 + 2 * t4] = acc[0];
+    pb[g * 8 + 2 * t4 + 1] = acc[1];
+    pb[(g + 8) * 8 + 2 * t4] = acc[2];
+    pb[(g + 8) * 8 + 2 * t4 + 1] = acc[3];
     chunk_release(c);
+    csync();
+    if (threadIdx.x < 8 * c.B) {
+      const int p = threadIdx.x / c.B, b = threadIdx.x - p * c.B;
+      const float* q = c.red + (size_t)(u & 1) * kWarps * 16 * 8;
+      float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        v0 += q[(w * 16 + 2 * p) * 8 + b];
+        v1 += q[(w * 16 + 2 * p + 1) * 8 + b];
+      }
+      epi(u, p, b, v0, v1);
+    }
   }
 }
 
 // ------------------------------------------------------------------ phases
-template <int MAXB>
 __device__ void phase_a(Ctx& c, int li) {
   const dh_layer_params& lp = layer(c, li);
   const bool tree = lp.kind == 0;
   const int d = c.d, B = c.B;
   stamp(c, li, PH_A, 0);
+  const NormW nw = load_normw(c, static_cast<const __nv_bfloat16*>(lp.norm1));
   if (li > 0) grid_wait(c, li - 1, PH_C, c.NG);
   stamp(c, li, PH_A, 1);
   // the residual: layer 0 starts it (both buffers) from the embedding rows; a
@@ -573,44 +616,51 @@ __device__ void phase_a(Ctx& c, int li) {
       const long long tok = c.p.tokens[threadIdx.x];
       if (tok < 0 || tok >= c.p.vocab) atomicExch(c.p.status, DH_ERR_ARG);
     }
-    stage_norm<MAXB>(c, li == 0 ? nullptr : c.p.x, static_cast<const __nv_bfloat16*>(lp.norm1),
-                     li == 0 ? c.p.x : nullptr, (li == 0 || tree) ? c.p.x_in : nullptr, e0, e1);
+    stage_norm(c, li == 0 ? nullptr : c.p.x, nw, li == 0 ? c.p.x : nullptr,
+               (li == 0 || tree) ? c.p.x_in : nullptr, e0, e1);
   }
   stamp(c, li, PH_A, 2);
+  const int ksw = d / 128;
+  uint32_t bx[8][2];
+  load_xfrags(c, ksw, bx);
   const Seg s = get_seg(c, li, PH_A, 0);
   int u0, u1;
-  split_range(3 * d / 2, c.NG, c.cta, u0, u1);
+  split_range(3 * d / 16, c.NG, c.cta, u0, u1);
   const long long t = c.t;
+  const int ml = c.p.max_len;
   if (tree) {
     __nv_bfloat16* v0 = static_cast<__nv_bfloat16*>(c.p.v0);
     __nv_bfloat16* a = static_cast<__nv_bfloat16*>(c.p.a);
     __nv_bfloat16* bh = static_cast<__nv_bfloat16*>(lp.b_hist);
-    const int ml = c.p.max_len;
-    gemv_segment<MAXB>(c, s, d, u0, [&](int u, int b, int row, float v, float) {
-      const int n = 2 * u + row, seg = n / d, col = n - seg * d;
-      if (seg == 0) v0[(size_t)b * d + col] = f2bf(v);
-      else if (seg == 1) a[(size_t)b * d + col] = f2bf(v);
-      else bh[((size_t)b * ml + t) * d + col] = f2bf(v);
+    gemv_tiles(c, s, bx, ksw, [&](int u, int p, int b, float ve, float vo) {
+      const int n = (u0 + u) * 16 + 2 * p, seg = n / d, col = n - seg * d;
+      const uint32_t pk = pack2(ve, vo);
+      __nv_bfloat16* dst = seg == 0 ? v0 + (size_t)b * d + col
+                         : seg == 1 ? a + (size_t)b * d + col
+                                    : bh + ((size_t)b * ml + t) * d + col;
+      *reinterpret_cast<uint32_t*>(dst) = pk;
     });
   } else {
     __nv_bfloat16* q = static_cast<__nv_bfloat16*>(c.p.q);
     __nv_bfloat16* kc = static_cast<__nv_bfloat16*>(lp.k_cache);
     __nv_bfloat16* vc = static_cast<__nv_bfloat16*>(lp.v_cache);
-    const int ml = c.p.max_len, hd = c.hd;
+    const int hd = c.hd;
     const float* cosT = c.p.rope_cos;
     const float* sinT = c.p.rope_sin;
-    gemv_segment<MAXB>(c, s, d, u0, [&](int u, int b, int row, float v, float other) {
-      const int n = 2 * u + row, seg = n / d, col = n - seg * d;
-      float out = v;
+    gemv_tiles(c, s, bx, ksw, [&](int u, int p, int b, float x1, float x2) {
+      const int n = (u0 + u) * 16 + 2 * p, seg = n / d, col = n - seg * d;
+      float o1 = x1, o2 = x2;
       if (seg < 2) {  // rotate the pair (2j, 2j+1) of q and k at position t
         const int j = (col % hd) >> 1;
         const float cs = cosT[t * (hd / 2) + j], sn = sinT[t * (hd / 2) + j];
-        const float x1 = row == 0 ? v : other, x2 = row == 0 ? other : v;
-        out = row == 0 ? (x1 * cs - x2 * sn) : (x1 * sn + x2 * cs);
+        o1 = x1 * cs - x2 * sn;
+        o2 = x1 * sn + x2 * cs;
       }
-      if (seg == 0) q[(size_t)b * d + col] = f2bf(out);
-      else if (seg == 1) kc[((size_t)b * ml + t) * d + col] = f2bf(out);
-      else vc[((size_t)b * ml + t) * d + col] = f2bf(out);
+      const uint32_t pk = pack2(o1, o2);
+      __nv_bfloat16* dst = seg == 0 ? q + (size_t)b * d + col
+                         : seg == 1 ? kc + ((size_t)b * ml + t) * d + col
+                                    : vc + ((size_t)b * ml + t) * d + col;
+      *reinterpret_cast<uint32_t*>(dst) = pk;
     });
   }
   stamp(c, li, PH_A, 3);
@@ -618,23 +668,25 @@ __device__ void phase_a(Ctx& c, int li) {
 }
 
 // head CTA: gates of every level, level recurrence, out-projection share
-template <int MAXB>
 __device__ void phase_b_tree(Ctx& c, int li) {
   const dh_layer_params& lp = layer(c, li);
   const int B = c.B, L = c.L, H = c.H, hd = c.hd, gh = c.gh, d = c.d, h = c.head;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g4 = lane >> 2, t4 = lane & 3;
   const long long t = c.t;
   const int ml = c.p.max_len;
   const int S = (1 << (L + 1)) - 2;
   __nv_bfloat16* ring = static_cast<__nv_bfloat16*>(lp.v_ring);
   __nv_bfloat16* rg = static_cast<__nv_bfloat16*>(lp.rg_hist);
   // small arrays in c.misc
-  float* s_f = c.misc;                        // [MAXB][kLmax]
-  float* s_c = s_f + MAXB * kLmax;            // [MAXB][kLmax]
-  float* s_rg = s_c + MAXB * kLmax;           // [MAXB][kLmax] transmit gate at the source
-  float* s_y = s_rg + MAXB * kLmax;           // [MAXB][64]
-  uint4* s_v0 = reinterpret_cast<uint4*>(s_y + MAXB * 64);                   // [MAXB][8]
-  __nv_bfloat16* s_ring = reinterpret_cast<__nv_bfloat16*>(s_v0 + MAXB * 8);  // [MAXB][kLmax][64]
+  float* s_f = c.misc;                        // [kMaxB][kLmax]
+  float* s_c = s_f + kMaxB * kLmax;           // [kMaxB][kLmax]
+  float* s_rg = s_c + kMaxB * kLmax;          // [kMaxB][kLmax] transmit gate at the source
+  uint4* s_v0 = reinterpret_cast<uint4*>(s_rg + kMaxB * kLmax);              // [kMaxB][8]
+  __nv_bfloat16* s_y = reinterpret_cast<__nv_bfloat16*>(s_v0 + kMaxB * 8);   // [kMaxB][64]
+  __nv_bfloat16* s_ring = s_y + kMaxB * 64;                                  // [kMaxB][kLmax][64]
+  float* red = reinterpret_cast<float*>(s_ring + kMaxB * kLmax * 64);       // [kWarps][kMaxB][48]
+  float* s_bias = red + kWarps * kMaxB * 48;                                 // [kLmax][3]
   stamp(c, li, PH_B, 0);
   // history written by earlier steps: ring slots of the source positions and
   // their transmit gates (one round trip, before the wait)
@@ -650,6 +702,7 @@ __device__ void phase_b_tree(Ctx& c, int li) {
     if (g == 0)
       s_rg[b * kLmax + l] = src >= 0 ? bf2f(rg[(((size_t)b * ml + src) * L + l) * H + h]) : 0.f;
   }
+  for (int i = tid; i < L * 3; i += kCons) s_bias[i] = lp.b_gates[(size_t)h * L * 3 + i];
   grid_wait(c, li, PH_A, c.NG);
   stamp(c, li, PH_B, 1);
   // A rows (every column) and this head's v0 slice, one round trip
@@ -660,7 +713,7 @@ __device__ void phase_b_tree(Ctx& c, int li) {
     for (int i = tid; i < n + B * 8; i += kCons) {
       if (i < n) {
         const int b = i / k8, k = (i - b * k8) * 8;
-        *reinterpret_cast<uint4*>(c.xs + (size_t)b * 1024 + k) =
+        *reinterpret_cast<uint4*>(xs_at(c, b, k)) =
             __ldcg(reinterpret_cast<const uint4*>(a + (size_t)b * gh + k));
       } else {
         const int j = i - n, b = j / 8, g = j - b * 8;
@@ -670,62 +723,75 @@ __device__ void phase_b_tree(Ctx& c, int li) {
   }
   csync();
   stamp(c, li, PH_B, 2);
-  // gate readouts, chunk by chunk (a chunk holds up to kLgMax levels: their
-  // weights, then their history rows): thread tid owns columns [4 tid, 4 tid + 4)
-  // of the hidden width; all loads of a chunk are issued before its FMAs and
-  // its (level, gate) partial sums leave in one transpose reduction per row
-  float* red = c.red;  // [kWarps][MAXB][kLmax * 3]
-  const int k = tid * 4;
-  const bool kin = k < gh;
-  const Seg sg = get_seg(c, li, PH_B, 0);
-  for (int l0 = 0; l0 < L; l0 += c.lg) {
-    const int nlv = min(L, l0 + c.lg) - l0;
-    const uint8_t* chunk = chunk_acquire(c);
-    const uint32_t wbytes = (uint32_t)nlv * sg.unit_bytes;
+  // gate readouts on the tensor cores: D = W x hv with W the three 16-row
+  // tiles (admit / forget / transmit rows of levels 0..15) and hv the 16
+  // columns relu^2(A + B_hist[t - 2^l]) (bf16), built in registers from
+  // ldmatrix fragments of the history rows; the readout of level l is the
+  // diagonal element (l, l).  K is split over the warps.
+  const uint8_t* bhc[kMaxB];
+  for (int b = 0; b < B; ++b) bhc[b] = chunk_acquire(c);
+  const uint8_t* wg[3];
+  for (int g = 0; g < 3; ++g) wg[g] = chunk_acquire(c);
+  const int ksw = gh / 128;
+  const int bstride = bh_stride(c);
+  {
+    const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, ahalf = lane >> 4;
+    const int brow = lane & 7, bhalf = (lane >> 3) & 1;
+    const __nv_bfloat162 z2 = __floats2bfloat162_rn(0.f, 0.f);
     for (int b = 0; b < B; ++b) {
-      const uint2 au = kin ? *reinterpret_cast<const uint2*>(c.xs + (size_t)b * 1024 + k) : make_uint2(0, 0);
-      float av[4];
-      {
-        const float2 a01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&au.x));
-        const float2 a23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&au.y));
-        av[0] = a01.x; av[1] = a01.y; av[2] = a23.x; av[3] = a23.y;
-      }
-      uint2 bu[kLgMax];
+      float acc[3][2][4];
 #pragma unroll
-      for (int j = 0; j < kLgMax; ++j) {
-        const bool ok = j < nlv && kin && t - (1ll << (l0 + j)) >= 0;
-        bu[j] = ok ? *reinterpret_cast<const uint2*>(chunk + wbytes + (((size_t)j * B + b) * gh + k) * 2)
-                   : make_uint2(0, 0);
-      }
-      float acc[16];
+      for (int g = 0; g < 3; ++g)
 #pragma unroll
-      for (int q = 0; q < 16; ++q) acc[q] = 0.f;
+        for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int j = 0; j < kLgMax; ++j) {
-        const float2 b01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bu[j].x));
-        const float2 b23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bu[j].y));
-        const float bs[4] = {b01.x, b01.y, b23.x, b23.y};
-        float hv[4];
+          for (int e = 0; e < 4; ++e) acc[g][nt][e] = 0.f;
+#pragma unroll 1
+      for (int i = 0; i < ksw; ++i) {
+        {
+          const int ch = (warp * ksw + i) * 2;  // first 16-byte chunk of this k-step
+          // A values at this thread's fragment columns (k = 8 ch + 2 t4, +8)
+          const __nv_bfloat162 a_lo = *reinterpret_cast<const __nv_bfloat162*>(xs_at(c, b, ch * 8 + 2 * t4));
+          const __nv_bfloat162 a_hi = *reinterpret_cast<const __nv_bfloat162*>(xs_at(c, b, ch * 8 + 8 + 2 * t4));
+          uint32_t aw[3][4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float x = fmaxf(av[e] + bs[e], 0.f);
-          hv[e] = x * x;  // relu squared
+          for (int g = 0; g < 3; ++g) ldsm_x4(aw[g], smem_u32(wg[g]) + swz(arow, ch + ahalf, gh * 2));
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            // history row of level l = 8 nt + (lane & 7); levels without a
+            // source (or beyond L) read the zero row
+            const int l = nt * 8 + brow;
+            const bool ok = l < L && t - (1ll << l) >= 0;
+            const uint8_t* rowp = ok ? bhc[b] + (size_t)l * bstride
+                                     : reinterpret_cast<const uint8_t*>(c.zrow);
+            uint32_t bf[2];
+            ldsm_x2(bf, smem_u32(rowp + (ch + bhalf) * 16));
+            __nv_bfloat162 h0 = __hmax2(__hadd2(a_lo, *reinterpret_cast<__nv_bfloat162*>(&bf[0])), z2);
+            __nv_bfloat162 h1 = __hmax2(__hadd2(a_hi, *reinterpret_cast<__nv_bfloat162*>(&bf[1])), z2);
+            h0 = __hmul2(h0, h0);  // relu squared, rounded to bf16 as the reference's fused gates
+            h1 = __hmul2(h1, h1);
+            uint32_t hv[2] = {*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1)};
+#pragma unroll
+            for (int g = 0; g < 3; ++g) mma16816(acc[g][nt], aw[g], hv);
+          }
         }
+      }
+      // diagonal: level l = g4 sits in acc[..][0][0] when g4 == 2 t4 and in
+      // acc[..][0][1] when g4 == 2 t4 + 1; level 8 + g4 likewise in [1][2] / [1][3]
+      float* rb = red + ((size_t)warp * kMaxB + b) * 48;
 #pragma unroll
-        for (int g = 0; g < 3; ++g) {
-          const uint2 wq = (j < nlv && kin)
-              ? *reinterpret_cast<const uint2*>(chunk + ((size_t)j * 3 * gh + (size_t)g * gh + k) * 2)
-              : make_uint2(0, 0);
-          const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wq.x));
-          const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wq.y));
-          acc[j * 3 + g] = fmaf(w01.x, hv[0], fmaf(w01.y, hv[1], fmaf(w23.x, hv[2], w23.y * hv[3])));
+      for (int g = 0; g < 3; ++g) {
+        if (g4 == 2 * t4) {
+          rb[g * 16 + g4] = acc[g][0][0];
+          rb[g * 16 + g4 + 8] = acc[g][1][2];
+        } else if (g4 == 2 * t4 + 1) {
+          rb[g * 16 + g4] = acc[g][0][1];
+          rb[g * 16 + g4 + 8] = acc[g][1][3];
         }
       }
-      const float r = transpose_reduce<16>(acc);
-      if (lane < nlv * 3) red[((size_t)warp * MAXB + b) * (kLmax * 3) + l0 * 3 + lane] = r;
     }
-    chunk_release(c);
   }
+  for (int b = 0; b < B + 3; ++b) chunk_release(c);
   csync();
   // sigmoid gates; transmit gate of position t into rg_hist
   for (int i = tid; i < B * L; i += kCons) {
@@ -735,8 +801,8 @@ __device__ void phase_b_tree(Ctx& c, int li) {
     for (int g = 0; g < 3; ++g) {
       float s = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) s += red[((size_t)w * MAXB + b) * (kLmax * 3) + l * 3 + g];
-      pre[g] = s + lp.b_gates[((size_t)h * L + l) * 3 + g];
+      for (int w = 0; w < kWarps; ++w) s += red[((size_t)w * kMaxB + b) * 48 + g * 16 + l];
+      pre[g] = s + s_bias[l * 3 + g];
     }
     const float okf = t - (1ll << l) >= 0 ? 1.f : 0.f;
     const float ig = sigmoidf_(pre[0]) * okf;
@@ -758,7 +824,7 @@ __device__ void phase_b_tree(Ctx& c, int li) {
     const uint4 v0 = s_v0[b * 8 + g];
     unpack8(v0, V);
     if (wr) *reinterpret_cast<uint4*>(ringb + (size_t)(t & 1) * d + c0) = v0;  // ring 0 at t
-#pragma unroll 4
+#pragma unroll 1
     for (int l = 0; l < kLmax; ++l) {
       if (l < L) {
         float vs[8];
@@ -772,62 +838,47 @@ __device__ void phase_b_tree(Ctx& c, int li) {
         }
       }
     }
-    const uint4 yv = pack8(V);
-    float yr[8];
-    unpack8(yv, yr);  // y is bf16, as the reference's
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s_y[b * 64 + g * 8 + j] = yr[j];
+    *reinterpret_cast<uint4*>(s_y + b * 64 + g * 8) = pack8(V);  // y is bf16, as the reference's
   }
   csync();
-  // out-projection share: x[b, n] += sum_c W_out[n, h*hd + c] y_h[b, c] for this
-  // CTA's half of the rows n, added into both residual buffers.  Thread r owns
-  // row r of a chunk (256 rows x 64 channels), reading its 16-byte pieces in a
-  // rotated order (no bank conflicts); four rows leave in one vector reduction.
-  const Seg so = get_seg(c, li, PH_B, 1);
+  // out-projection share on the tensor cores: x[b, n] += sum_c W_out[n, h*hd + c] y_h[b, c]
+  // for this CTA's half of the rows n, added into both residual buffers.
+  // A = 16-row tiles of the (swizzled) head block, B = y rows (hd = 64: 4 k-steps).
+  uint32_t by[4][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int n = lane & 7, half = (lane >> 3) & 1;
+    const __nv_bfloat16* row = n < B ? s_y + n * 64 + (2 * i + half) * 8 : c.zrow + (2 * i + half) * 8;
+    ldsm_x2(by[i], smem_u32(row));
+  }
+  const Seg so = get_seg(c, li, PH_B, 2);
   const int upc = units_per_chunk(c, so);
   const int nbase = c.hpart * (d / kHeadParts);
+  const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, ahalf = lane >> 4;
   for (int cu = 0; cu < so.units; cu += upc) {
-    const int nrows = min(upc, so.units - cu) * 32;
+    const int ntile = min(upc, so.units - cu);
     const uint8_t* chunk = chunk_acquire(c);
-    const int r = tid;
-    float sum[MAXB];
-#pragma unroll
-    for (int b = 0; b < MAXB; ++b) sum[b] = 0.f;
-    if (r < nrows) {
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-      uint4 wv[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        wv[i] = *reinterpret_cast<const uint4*>(chunk + ((size_t)r * 64 + ((half * 4 + i + r) & 7) * 8) * 2);
+    for (int mt = warp; mt < ntile; mt += kWarps) {
+      const uint32_t tb = smem_u32(chunk) + (uint32_t)mt * 16 * hd * 2;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int pc = (half * 4 + i + r) & 7;
-        float wf[8];
-        unpack8(wv[i], wf);
-#pragma unroll
-        for (int b = 0; b < MAXB; ++b) {
-          if (b < B) {
-            const float4 y0 = *reinterpret_cast<const float4*>(s_y + b * 64 + pc * 8);
-            const float4 y1 = *reinterpret_cast<const float4*>(s_y + b * 64 + pc * 8 + 4);
-            sum[b] = fmaf(wf[0], y0.x, fmaf(wf[1], y0.y, fmaf(wf[2], y0.z, fmaf(wf[3], y0.w,
-                     fmaf(wf[4], y1.x, fmaf(wf[5], y1.y, fmaf(wf[6], y1.z, fmaf(wf[7], y1.w, sum[b]))))))));
-          }
-        }
+        uint32_t a[4];
+        ldsm_x4(a, tb + swz(arow, 2 * i + ahalf, hd * 2));
+        mma16816(acc, a, by[i]);
       }
+      const int n0 = nbase + (cu + mt) * 16 + g4;
+      if (2 * t4 < B) {
+        red_add_f32(c.p.x + (size_t)(2 * t4) * d + n0, acc[0]);
+        red_add_f32(c.p.x_in + (size_t)(2 * t4) * d + n0, acc[0]);
+        red_add_f32(c.p.x + (size_t)(2 * t4) * d + n0 + 8, acc[2]);
+        red_add_f32(c.p.x_in + (size_t)(2 * t4) * d + n0 + 8, acc[2]);
       }
-    }
-    const int n = nbase + cu * 32 + r;
-#pragma unroll
-    for (int b = 0; b < MAXB; ++b) {
-      if (b < B) {
-        const float s1 = __shfl_down_sync(0xffffffffu, sum[b], 1);
-        const float s2 = __shfl_down_sync(0xffffffffu, sum[b], 2);
-        const float s3 = __shfl_down_sync(0xffffffffu, sum[b], 3);
-        if ((lane & 3) == 0 && r < nrows) {
-          red_add_v4(c.p.x + (size_t)b * d + n, sum[b], s1, s2, s3);
-          red_add_v4(c.p.x_in + (size_t)b * d + n, sum[b], s1, s2, s3);
-        }
+      if (2 * t4 + 1 < B) {
+        red_add_f32(c.p.x + (size_t)(2 * t4 + 1) * d + n0, acc[1]);
+        red_add_f32(c.p.x_in + (size_t)(2 * t4 + 1) * d + n0, acc[1]);
+        red_add_f32(c.p.x + (size_t)(2 * t4 + 1) * d + n0 + 8, acc[3]);
+        red_add_f32(c.p.x_in + (size_t)(2 * t4 + 1) * d + n0 + 8, acc[3]);
       }
     }
     chunk_release(c);
@@ -837,7 +888,6 @@ __device__ void phase_b_tree(Ctx& c, int li) {
 }
 
 // GEMV CTAs: split-window attention with last-arriver combine
-template <int MAXB>
 __device__ void phase_b_attn(Ctx& c, int li) {
   const dh_layer_params& lp = layer(c, li);
   constexpr int HD = 64;
@@ -971,7 +1021,6 @@ __device__ void phase_b_attn(Ctx& c, int li) {
 }
 
 // GEMV CTAs: attention output projection, rows owned (no atomics)
-template <int MAXB>
 __device__ void phase_o(Ctx& c, int li) {
   const int d = c.d;
   stamp(c, li, PH_O, 0);
@@ -979,101 +1028,117 @@ __device__ void phase_o(Ctx& c, int li) {
   stamp(c, li, PH_O, 1);
   stage_copy(c, static_cast<const __nv_bfloat16*>(c.p.y), d);
   stamp(c, li, PH_O, 2);
+  const int ksw = d / 128;
+  uint32_t bx[8][2];
+  load_xfrags(c, ksw, bx);
   int u0, u1;
-  split_range(d / 2, c.NG, c.cta, u0, u1);
+  split_range(d / 16, c.NG, c.cta, u0, u1);
   const Seg s = get_seg(c, li, PH_O, 0);
   float* x = c.p.x;
   float* xin = c.p.x_in;
-  gemv_segment<MAXB>(c, s, d, u0, [&](int u, int b, int row, float v, float) {
-    const size_t i = (size_t)b * d + 2 * u + row;
-    const float nx = __ldcg(x + i) + v;
-    x[i] = nx;
-    xin[i] = nx;
+  gemv_tiles(c, s, bx, ksw, [&](int u, int p, int b, float ve, float vo) {
+    const size_t i = (size_t)b * d + (u0 + u) * 16 + 2 * p;
+    const float2 old = __ldcg(reinterpret_cast<const float2*>(x + i));
+    const float2 nx = make_float2(old.x + ve, old.y + vo);
+    *reinterpret_cast<float2*>(x + i) = nx;
+    *reinterpret_cast<float2*>(xin + i) = nx;
   });
   stamp(c, li, PH_O, 3);
   grid_arrive(c, li, PH_O);
 }
 
 // GEMV CTAs: the FFN slice, down projection added into x
-template <int MAXB>
 __device__ void phase_c(Ctx& c, int li) {
   const dh_layer_params& lp = layer(c, li);
-  const int d = c.d, B = c.B, tid = threadIdx.x;
+  const int d = c.d, B = c.B, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g4 = lane >> 2, t4 = lane & 3;
   stamp(c, li, PH_C, 0);
+  const NormW nw = load_normw(c, static_cast<const __nv_bfloat16*>(lp.norm2));
   if (lp.kind == 0) grid_wait(c, li, PH_B, c.H * kHeadParts);
   else grid_wait(c, li, PH_O, c.NG);
   stamp(c, li, PH_C, 1);
-  stage_norm<MAXB>(c, c.p.x_in, static_cast<const __nv_bfloat16*>(lp.norm2));
+  stage_norm(c, c.p.x_in, nw);
   stamp(c, li, PH_C, 2);
-  int j0, j1;
-  split_range(c.ff, c.NG, c.cta, j0, j1);
-  float* us = c.misc;  // [MAXB][kMaxUpc]
+  const int ksw = d / 128;
+  uint32_t bx[8][2];
+  load_xfrags(c, ksw, bx);
+  int t0, t1;
+  split_range(c.ff / 8, c.NG, c.cta, t0, t1);
+  const int jn = 8 * (t1 - t0);  // FFN columns of this CTA
+  float* us = c.misc;            // [kMaxB][kMaxUpc] (u rounded to bf16)
   const Seg sgu = get_seg(c, li, PH_C, 0);
-  gemv_segment<MAXB>(c, sgu, d, 0, [&](int u, int b, int row, float g, float up) {
-    if (row != 0) return;
-    us[b * kMaxUpc + u] = bf2f(f2bf(g / (1.0f + expf(-g)) * up));
+  gemv_tiles(c, sgu, bx, ksw, [&](int u, int p, int b, float gate, float up) {
+    us[b * kMaxUpc + u * 8 + p] = bf2f(f2bf(gate / (1.0f + expf(-gate)) * up));
   });
   csync();
+  // down projection on the tensor cores: D[b, n] = sum_j u[b, j] Wd[n, j0 + j]
+  // with A = u (rows = lockstep rows) and B = 16-row tiles of Wd^T (one per
+  // chunk, read transposed by ldmatrix); warp w takes n-tiles w, w + 8, ...
   const Seg sd = get_seg(c, li, PH_C, 1);
-  const int upc = units_per_chunk(c, sd);
-  const int n0 = tid * 4;
-  const bool nin = n0 < d;
-  float acc[MAXB][4];
+  float acc[16][4];
 #pragma unroll
-  for (int b = 0; b < MAXB; ++b) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.f;
-  for (int cu = 0; cu < sd.units; cu += upc) {
-    const int nj = min(upc, sd.units - cu);
+  for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  const int ntiles = d / 8;  // 8-column tiles of n
+  for (int kt = 0; kt < sd.units; ++kt) {
     const uint8_t* chunk = chunk_acquire(c);
-    if (nin) {
-#pragma unroll 4
-      for (int j = 0; j < nj; ++j) {
-        const uint2 wv = *reinterpret_cast<const uint2*>(chunk + ((size_t)j * d + n0) * 2);
-        const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.x));
-        const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.y));
+    const int kvalid = min(16, jn - kt * 16);
+    uint32_t au[4] = {0u, 0u, 0u, 0u};
+    if (g4 < B) {
+      const int k0 = kt * 16 + 2 * t4;
+      const float* ur = us + g4 * kMaxUpc;
+      au[0] = k0 < jn ? pack2(ur[k0], ur[k0 + 1]) : 0u;
+      au[2] = k0 + 8 < jn ? pack2(ur[k0 + 8], ur[k0 + 9]) : 0u;
+    }
+    const uint32_t base = smem_u32(chunk);
+    const int krow = (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
-        for (int b = 0; b < MAXB; ++b) {
-          if (b < B) {
-            const float uj = us[b * kMaxUpc + cu + j];
-            acc[b][0] = fmaf(uj, w01.x, acc[b][0]);
-            acc[b][1] = fmaf(uj, w01.y, acc[b][1]);
-            acc[b][2] = fmaf(uj, w23.x, acc[b][2]);
-            acc[b][3] = fmaf(uj, w23.y, acc[b][3]);
-          }
-        }
+    for (int i = 0; i < 16; ++i) {
+      const int nt = warp + kWarps * i;
+      if (nt < ntiles) {
+        uint32_t bw[2];
+        ldsm_x2_t(bw, base + swz(krow, nt, d * 2));
+        if (kvalid <= 8) bw[1] = 0u;  // rows past this CTA's columns hold stale data
+        mma16816(acc[i], au, bw);     // only rows b < B (acc[.][0..1]) are kept
       }
     }
     chunk_release(c);
   }
-  if (nin && sd.units > 0) {
+  if (g4 < B && sd.units > 0) {
 #pragma unroll
-    for (int b = 0; b < MAXB; ++b)
-      if (b < B) red_add_v4(c.p.x + (size_t)b * d + n0, acc[b][0], acc[b][1], acc[b][2], acc[b][3]);
+    for (int i = 0; i < 16; ++i) {
+      const int nt = warp + kWarps * i;
+      if (nt < ntiles) red_add_v2(c.p.x + (size_t)g4 * d + nt * 8 + 2 * t4, acc[i][0], acc[i][1]);
+    }
   }
   stamp(c, li, PH_C, 3);
   grid_arrive(c, li, PH_C);
 }
 
-template <int MAXB>
 __device__ void phase_n(Ctx& c) {
   const int d = c.d, nl = c.p.n_layers;
   stamp(c, nl, 0, 0);
+  const NormW nw = load_normw(c, static_cast<const __nv_bfloat16*>(c.p.norm_out));
   grid_wait(c, nl - 1, PH_C, c.NG);
   stamp(c, nl, 0, 1);
-  stage_norm<MAXB>(c, c.p.x, static_cast<const __nv_bfloat16*>(c.p.norm_out));
+  stage_norm(c, c.p.x, nw);
   stamp(c, nl, 0, 2);
+  const int ksw = d / 128;
+  uint32_t bx[8][2];
+  load_xfrags(c, ksw, bx);
   int u0, u1;
-  split_range((c.p.vocab + 1) / 2, c.G, c.cta, u0, u1);
-  const Seg s = get_seg(c, c.p.n_layers, PH_N, 0);
-  __nv_bfloat16* lg = static_cast<__nv_bfloat16*>(c.p.logits);
   const int V = c.p.vocab;
-  gemv_segment<MAXB>(c, s, d, u0, [&](int u, int b, int row, float v, float) {
-    lg[(size_t)b * V + 2 * u + row] = f2bf(v);
+  split_range((V + 15) / 16, c.G, c.cta, u0, u1);
+  const Seg s = get_seg(c, nl, PH_N, 0);
+  __nv_bfloat16* lg = static_cast<__nv_bfloat16*>(c.p.logits);
+  gemv_tiles(c, s, bx, ksw, [&](int u, int p, int b, float ve, float vo) {
+    const int n = (u0 + u) * 16 + 2 * p;
+    if (n < V) lg[(size_t)b * V + n] = f2bf(ve);
+    if (n + 1 < V) lg[(size_t)b * V + n + 1] = f2bf(vo);
   });
   stamp(c, nl, 0, 3);
 }
 
 // ------------------------------------------------------------------ kernel
-template <int MAXB>
 __global__ void __launch_bounds__(kThreads, 1)
     step_kernel(const __grid_constant__ dh_step_params p, uint32_t wait_limit) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -1096,33 +1161,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     ns = ns < 1 ? 1 : ns;
     c.nsplit = ns < p.nsplit ? ns : p.nsplit;
   }
-  c.lg = 1;
-  while (c.lg < c.L && c.lg < kLgMax && gate_chunk_bytes(c, 0, c.lg + 1) <= (uint32_t)kSlotBytes)
-    ++c.lg;
-  c.nslots = slots_for<MAXB>();
+  // ring slots, then the attention staging buffer, which head CTAs (never
+  // in an attention phase) use as one more ring slot
+  static_assert(2 * kKvPos * 64 * 2 == kSlotBytes, "the staging buffer doubles as a slot");
+  c.nslots = c.head >= 0 ? kSlots + 1 : kSlots;
   c.slots = smem_raw;
-  uint8_t* q = smem_raw + (size_t)c.nslots * kSlotBytes;
+  c.kv = reinterpret_cast<__nv_bfloat16*>(smem_raw + (size_t)kSlots * kSlotBytes);
+  uint8_t* q = smem_raw + (size_t)(kSlots + 1) * kSlotBytes;
   c.xs = reinterpret_cast<__nv_bfloat16*>(q);
-  q += (size_t)MAXB * 1024 * 2;
-  c.kv = reinterpret_cast<__nv_bfloat16*>(q);
-  q += (size_t)2 * kKvPos * 64 * 2;
+  q += (size_t)kMaxB * kMaxD * 2;
+  c.zrow = reinterpret_cast<__nv_bfloat16*>(q);
+  q += (size_t)kMaxD * 2;
   c.red = reinterpret_cast<float*>(q);
-  q += (size_t)kWarps * MAXB * kLmax * 3 * 4;
+  q += (size_t)2 * kWarps * 16 * 8 * 4;
   c.misc = reinterpret_cast<float*>(q);
-  q += (size_t)(MAXB * (4 * kLmax + 64 + kMaxUpc) + MAXB * kLmax * 32 + 2048) * 4;
-  static_assert(3 * kLmax + 64 + 32 + kLmax * 32 <= 4 * kLmax + 64 + kMaxUpc + kLmax * 32,
-                "head phase arrays fit the per-row scratch");
+  q += (size_t)kMisc * 4;
   c.full = reinterpret_cast<uint64_t*>(q);
-  c.empty = c.full + c.nslots;
-  c.abort = reinterpret_cast<volatile int*>(c.empty + c.nslots);
-  c.consumed = 0;
+  c.empty = c.full + kSlots + 1;
+  c.abort = reinterpret_cast<volatile int*>(c.empty + kSlots + 1);
+  c.prod = reinterpret_cast<Prod*>(const_cast<int*>(reinterpret_cast<volatile int*>(c.abort)) + 4);
+  c.acq = 0;
+  c.rel = 0;
   c.t = __ldcg(p.t_buf);
   c.gen = __ldcg(p.barrier);
   if (c.t < 0 || c.t >= p.max_len) {  // no position left: nothing is written
     if (c.cta == 0 && threadIdx.x == 0) atomicExch(p.status, DH_ERR_ARG);
     return;
   }
-
+  {  // the layer table, read once into shared memory; the zero row
+    dh_layer_params* lay = reinterpret_cast<dh_layer_params*>(
+        reinterpret_cast<uint8_t*>(c.prod) + ((sizeof(Prod) + 15) / 16) * 16);
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.layers);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(lay);
+    const int words = p.n_layers * (int)(sizeof(dh_layer_params) / 8);
+    for (int i = threadIdx.x; i < words; i += kThreads) dst[i] = src[i];
+    for (int i = threadIdx.x; i < kMaxD / 8; i += kThreads)
+      reinterpret_cast<uint4*>(c.zrow)[i] = make_uint4(0, 0, 0, 0);
+    c.lay = lay;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < c.nslots; ++s) {
       mbar_init(&c.full[s], 1);
@@ -1131,28 +1207,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     *c.abort = 0;
     fence_barrier_init();
   }
-  c.prod = reinterpret_cast<Prod*>(const_cast<int*>(reinterpret_cast<volatile int*>(c.abort)) + 4);
-  {  // the layer table, read once into shared memory
-    dh_layer_params* lay = reinterpret_cast<dh_layer_params*>(
-        reinterpret_cast<uint8_t*>(c.prod) + ((sizeof(Prod) + 15) / 16) * 16);
-    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.layers);
-    unsigned long long* dst = reinterpret_cast<unsigned long long*>(lay);
-    const int words = p.n_layers * (int)(sizeof(dh_layer_params) / 8);
-    for (int i = threadIdx.x; i < words; i += kThreads) dst[i] = src[i];
-    c.lay = lay;
-  }
   __syncthreads();
   if (threadIdx.x == 0) {
     Prod* pr = c.prod;
-    pr->pp = &p;
     pr->lay = c.lay;
-    pr->emb = p.emb;
+    pr->lm_head = p.lm_head;
     pr->vocab = p.vocab;
     pr->max_len = p.max_len;
     pr->n_layers = p.n_layers;
     pr->G = c.G; pr->cta = c.cta; pr->NG = c.NG; pr->head = c.head; pr->hpart = c.hpart;
     pr->B = c.B; pr->d = c.d; pr->gh = c.gh; pr->L = c.L; pr->H = c.H; pr->hd = c.hd;
-    pr->ff = c.ff; pr->lg = c.lg; pr->nslots = c.nslots; pr->t = c.t;
+    pr->ff = c.ff; pr->nslots = c.nslots; pr->t = c.t;
     pr->wait_limit = c.wait_limit;
     pr->slots = c.slots; pr->full = c.full; pr->empty = c.empty; pr->abort = c.abort;
     pr->issued = 0; pr->pslot = 0; pr->peph = 0;
@@ -1170,19 +1235,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int li = 0; li < nl; ++li) {
     const bool tree = c.lay[li].kind == 0;
     if (c.head < 0) {
-      phase_a<MAXB>(c, li);
+      phase_a(c, li);
       if (tree) {
-        phase_c<MAXB>(c, li);
+        phase_c(c, li);
       } else {
-        phase_b_attn<MAXB>(c, li);
-        phase_o<MAXB>(c, li);
-        phase_c<MAXB>(c, li);
+        phase_b_attn(c, li);
+        phase_o(c, li);
+        phase_c(c, li);
       }
     } else if (tree) {
-      phase_b_tree<MAXB>(c, li);
+      phase_b_tree(c, li);
     }
   }
-  phase_n<MAXB>(c);
+  phase_n(c);
   cp_async_wait_all();
   stamp(c, p.n_layers, 1, 1);
   if (c.cta == 0 && threadIdx.x == 0) {
@@ -1191,32 +1256,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int MAXB>
 size_t step_smem() {
-  return (size_t)slots_for<MAXB>() * kSlotBytes + (size_t)MAXB * 1024 * 2 + (size_t)2 * kKvPos * 64 * 2 +
-         (size_t)kWarps * MAXB * kLmax * 3 * 4 +
-         (size_t)(MAXB * (4 * kLmax + 64 + kMaxUpc) + MAXB * kLmax * 32 + 2048) * 4 +
-         (size_t)2 * slots_for<MAXB>() * 8 + 64 + ((sizeof(Prod) + 15) / 16) * 16 +
-         (size_t)kMaxLayers * sizeof(dh_layer_params);
+  return (size_t)(kSlots + 1) * kSlotBytes + (size_t)kMaxB * kMaxD * 2 + (size_t)kMaxD * 2 +
+         (size_t)2 * kWarps * 16 * 8 * 4 + (size_t)kMisc * 4 + (size_t)2 * (kSlots + 1) * 8 + 16 +
+         ((sizeof(Prod) + 15) / 16) * 16 + (size_t)kMaxLayers * sizeof(dh_layer_params);
 }
 
-template <int MAXB>
 int launch_step(const dh_step_params& p, cudaStream_t st) {
-  const size_t smem = step_smem<MAXB>();
+  const size_t smem = step_smem();
   DH_REQUIRE(smem <= 227 * 1024, DH_ERR_SHAPE, "dh_decode_step: %zu bytes of shared memory", smem);
   static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_dev != dev) {
-    cudaFuncSetAttribute(step_kernel<MAXB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     configured_dev = dev;
   }
   int per_sm = 0;
   const cudaError_t occ =
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel<MAXB>, kThreads, smem);
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel, kThreads, smem);
   if (per_sm < 1) {
     cudaFuncAttributes fa{};
-    cudaFuncGetAttributes(&fa, step_kernel<MAXB>);
+    cudaFuncGetAttributes(&fa, step_kernel);
     return set_error(DH_ERR_SHAPE,
                      "dh_decode_step: kernel does not fit on an SM (%s; %d regs, %zu B smem "
                      "requested, max dynamic %d, max threads %d)",
@@ -1224,20 +1285,18 @@ int launch_step(const dh_step_params& p, cudaStream_t st) {
                      fa.maxThreadsPerBlock);
   }
   const int G = sm_count();
-  DH_REQUIRE(G - p.H * kHeadParts >= 16, DH_ERR_SHAPE,
-             "dh_decode_step: %d SMs leave too few GEMV CTAs", G);
+  const int NG = G - p.H * kHeadParts;
+  DH_REQUIRE(NG >= 16, DH_ERR_SHAPE, "dh_decode_step: %d SMs leave too few GEMV CTAs", G);
+  DH_REQUIRE(8 * ((p.ff / 8 + NG - 1) / NG) <= kMaxUpc, DH_ERR_SHAPE,
+             "dh_decode_step: FFN width %d too large for %d CTAs", p.ff, NG);
   {  // the attention scores of one item live in the per-phase scratch
     const int span = (p.window > 0 && p.window < p.max_len) ? p.window : p.max_len;
-    int ns = (G - p.H * kHeadParts) / (p.batch * p.H);
+    int ns = NG / (p.batch * p.H);
     ns = ns < 1 ? 1 : (ns < p.nsplit ? ns : p.nsplit);
     const int chunk = (span + ns - 1) / ns;
-    const int misc = MAXB * (4 * kLmax + 64 + kMaxUpc) + MAXB * kLmax * 32 + 2048;
-    DH_REQUIRE(chunk + 64 + 8 + kWarps * 64 + 4 <= misc, DH_ERR_SHAPE,
+    DH_REQUIRE(chunk + 64 + 8 + kWarps * 64 + 4 <= kMisc - kMaxB, DH_ERR_SHAPE,
                "dh_decode_step: %d window positions per attention item exceed the scratch", chunk);
   }
-  DH_REQUIRE((p.ff + (G - p.H * kHeadParts) - 1) / (G - p.H * kHeadParts) <= kMaxUpc,
-             DH_ERR_SHAPE, "dh_decode_step: FFN width %d too large for %d CTAs", p.ff,
-             G - p.H * kHeadParts);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kThreads);
@@ -1248,7 +1307,7 @@ int launch_step(const dh_step_params& p, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, step_kernel<MAXB>, p, wait_limit()) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, step_kernel, p, wait_limit()) != cudaSuccess)
     return check_launch("step_kernel");
   return DH_OK;
 }
@@ -1261,21 +1320,16 @@ using namespace dh;
 extern "C" int dh_decode_step(const dh_step_params* params, void* stream) {
   DH_REQUIRE(params, DH_ERR_ARG, "dh_decode_step: null params");
   const dh_step_params& p = *params;
-  DH_REQUIRE(p.layers && p.tokens && p.t_buf && p.emb && p.norm_out && p.logits && p.x && p.x_in &&
-                 p.a && p.v0 && p.y && p.q && p.part && p.counters && p.barrier && p.status,
+  DH_REQUIRE(p.layers && p.tokens && p.t_buf && p.emb && p.lm_head && p.norm_out && p.logits &&
+                 p.x && p.x_in && p.a && p.v0 && p.y && p.q && p.part && p.counters && p.barrier &&
+                 p.status,
              DH_ERR_ARG, "dh_decode_step: null pointer in params");
-  DH_REQUIRE(p.batch >= 1 && p.batch <= 8, DH_ERR_SHAPE, "dh_decode_step: batch %d not in [1,8]",
-             p.batch);
-  DH_REQUIRE(p.hd == 64 && p.d == p.H * p.hd && p.d % 64 == 0 && p.d <= 1024 && p.ff % 8 == 0 &&
-                 p.L >= 1 && p.L <= kLmax && p.nsplit >= 1 && p.n_layers >= 1 &&
-                 p.n_layers <= kMaxLayers,
+  DH_REQUIRE(p.batch >= 1 && p.batch <= kMaxB, DH_ERR_SHAPE,
+             "dh_decode_step: batch %d not in [1,%d]", p.batch, kMaxB);
+  DH_REQUIRE(p.hd == 64 && p.d == p.H * p.hd && p.d % 128 == 0 && p.d <= kMaxD && p.ff % 16 == 0 &&
+                 p.L >= 1 && p.L <= kLmax && p.L * (2 * p.d + 16) <= kSlotBytes && p.nsplit >= 1 &&
+                 p.n_layers >= 1 && p.n_layers <= kMaxLayers,
              DH_ERR_SHAPE, "dh_decode_step: unsupported shape (d=%d H=%d hd=%d ff=%d L=%d layers=%d)",
              p.d, p.H, p.hd, p.ff, p.L, p.n_layers);
-  DH_REQUIRE(4 * p.d <= kSlotBytes && 3 * p.d * 2 + p.batch * p.d * 2 <= kSlotBytes, DH_ERR_SHAPE,
-             "dh_decode_step: a weight unit exceeds a stream slot (d=%d batch=%d)", p.d, p.batch);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (p.batch == 1) return launch_step<1>(p, st);
-  if (p.batch == 2) return launch_step<2>(p, st);
-  if (p.batch <= 4) return launch_step<4>(p, st);
-  return launch_step<8>(p, st);
+  return launch_step(p, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -88,7 +88,7 @@ class FusedGraphedHybridDecoder:
     def __init__(self, model, max_len=None, dtype=None, step_kernel="graph",
                  multi_document=False):
         """step_kernel: "graph" (per-op kernels captured in one CUDA graph) or
-        "persistent" (one cooperative kernel per step, batch <= 8).
+        "persistent" (one cooperative kernel per step, batch <= 2).
 
         multi_document: accept prompts (and generated tokens) that contain the
         document separator of a doc_reset model.  The decoder then keeps each
@@ -171,10 +171,11 @@ class FusedGraphedHybridDecoder:
         from .step_params import SYNC_WORDS
         self.barrier = torch.zeros(SYNC_WORDS, device=dev, dtype=torch.int64)
         self.graph = None
-        # one persistent kernel per step for lockstep batches of up to 8 rows
+        # one persistent kernel per step for lockstep batches of up to 2 rows
         # (dh_decode_step); larger batches run the per-op kernels in 16-row chunks
-        self.persistent = (self.step_kernel == "persistent" and batch <= 8 and d <= 1024
-                           and d % 64 == 0 and hd == 64 and cfg.levels <= 16)
+        self.persistent = (self.step_kernel == "persistent" and batch <= 2 and d <= 1024
+                           and d % 128 == 0 and hd == 64
+                           and cfg.levels * (2 * d + 16) <= 32768)
         if not self.persistent:
             # the fused FFN reads the down projection by rows of its transpose
             for lay in self.w.layers:

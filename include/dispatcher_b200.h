@@ -272,14 +272,17 @@ DH_API int dh_window_attn_prefill_tc(const void* qkv, int ld, void* out, int ldo
 /* ------------------------------------------------- persistent decode step */
 
 /* Per-layer weights and caches of the whole-step decode kernel.  Weights
- * are bf16; packed forms (built once by the host):
+ * are bf16 in packed forms built once by the host; every matrix below is
+ * stored row-major with the 16-byte chunks of row r XOR-permuted by (r & 7)
+ * (chunk c of row r at position c ^ (r & 7)), r counted from the first row
+ * of the matrix (of each 16-row tile for w_gates and w_out of a tree block):
  *   w_in3   tree: [W_in; W1x; W1s] (3d x d); attention: [Wq; Wk; Wv]
- *   w_gates tree: (H, L, 3, gh): per head, per level the admit / forget /
- *           transmit readout rows
- *   b_gates tree: (H, L, 3) fp32
+ *   w_gates tree: (H, 3, 16, gh): per head, three 16-row tiles (admit,
+ *           forget, transmit), row l = that readout of level l, rows >= L zero
+ *   b_gates tree: (H, L, 3) fp32 (not permuted)
  *   w_out   tree: (H, d, hd): head h's columns of W_out, row n = W_out[n, h*hd:];
- *           attention: W_out (d x d) row-major
- *   w_gu    (ff, 2, d): gate row j followed by up row j
+ *           attention: W_out (d x d)
+ *   w_gu    (2 ff, d): gate row j at 2j, up row j at 2j + 1
  *   w_down  (ff, d): W_down transposed (row j = column j of W_down) */
 typedef struct {
   int kind; /* 0 tree block, 1 attention block */
@@ -305,7 +308,8 @@ typedef struct {
   int n_layers, batch, d, H, hd, L, ff, vocab, max_len, window, nsplit;
   const int64_t* tokens;  /* (batch) next tokens */
   int64_t* t_buf;         /* position, advanced by the kernel */
-  const void* emb;        /* (vocab, d), also the tied lm_head */
+  const void* emb;        /* (vocab, d): the embedding rows */
+  const void* lm_head;    /* (vocab, d): the (tied) output head, rows permuted as above */
   const void* norm_out;
   const float* rope_cos;  /* (max_len, hd/2) fp32 */
   const float* rope_sin;
@@ -339,15 +343,17 @@ typedef struct {
 #define DH_STEP_TRACE_WORDS 512
 
 /* One whole lockstep decode step (embedding, every block, logits, t += 1)
- * as ONE persistent cooperative kernel, one CTA per SM: the last H CTAs run
- * each head's gate readouts, level recurrence and share of the output
- * projection, the others the projections and the FFN; each CTA streams its
+ * as ONE persistent cooperative kernel, one CTA per SM: the last 2H CTAs
+ * run each head's gate readouts, level recurrence and share of the output
+ * projection, the others the projections and the FFN, every contraction on
+ * the tensor cores (mma.sync m16n8k16); each CTA streams its
  * weight slices by bulk copies into shared memory ahead of the phase
  * hand-offs (monotonic per-phase counters, bounded waits: a timeout sets
  * *status = DH_ERR_TIMEOUT and the kernel still runs to completion).
  * Replaces the captured per-token graph of decoding.py:437-443 with the
  * fused tree step of decoding.py:457-488 (fused_step.py:26-88) and the
- * attention step of decoding.py:411-435.  batch <= 8, hd == 64, d <= 1024.
+ * attention step of decoding.py:411-435.  batch <= 2, hd == 64, d a multiple
+ * of 128 up to 1024, L * (2 d + 16) <= 32768.
  * `params` is a host pointer; its `layers` array must already be in device
  * memory. */
 DH_API int dh_decode_step(const dh_step_params* params, void* stream);

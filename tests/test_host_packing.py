@@ -98,42 +98,70 @@ def test_config_validation_and_levels():
     assert DispatcherConfig(attn_window=0).attn_slots() == set()
 
 
+def _unswizzle(w, period=None):
+    R, K = w.shape
+    r = torch.arange(R)
+    if period is not None:
+        r = r % period
+    pos = torch.arange(K // 8)[None, :] ^ (r[:, None] & 7)
+    return torch.gather(w.view(R, K // 8, 8), 1, pos[:, :, None].expand(R, K // 8, 8)).view(R, K)
+
+
+def test_swizzle_rows_permutes_chunks():
+    """Chunk c of row r lands at c ^ (r & 7), counted per tile with `period`."""
+    from dispatcher_b200.step_params import swizzle_rows
+    w = torch.arange(40 * 128, dtype=torch.float32).reshape(40, 128).bfloat16()
+    sw = swizzle_rows(w)
+    assert torch.equal(sw[0], w[0])
+    assert torch.equal(sw[3].view(16, 8)[5 ^ 3], w[3].view(16, 8)[5])
+    assert torch.equal(_unswizzle(sw), w)
+    swp = swizzle_rows(w, period=16)
+    assert torch.equal(_unswizzle(swp, 16), w)
+    assert torch.equal(swp[16], w[16]) and torch.equal(swp[19].view(16, 8)[2 ^ 3], w[19].view(16, 8)[2])
+
+
 def test_decode_step_weight_packs():
-    """Decode-step packs: gate/up as (ff, 2, d) row pairs and W_down^T; for a
-    tree layer, per head: the three gate readouts (H, L, 3, gh) with biases
-    (H, L, 3) fp32, and the head's columns of W_out (H, d, hd) — each head's
-    part one contiguous run for its head CTA's weight stream."""
+    """Decode-step packs (all rows chunk-permuted): W3 / Wqkv, W_out, gate/up
+    as (2 ff, d) row pairs, W_down^T; for a tree layer the gate readouts as
+    three 16-row tiles per head (row l = level l, zero rows past L), their
+    biases (H, L, 3) fp32 and each head's columns of W_out (H, d, hd); and a
+    permuted copy of the tied output head."""
     from types import SimpleNamespace
     from dispatcher_b200.step_params import pack_step_weights
     g = torch.Generator().manual_seed(3)
     ff, d, L, H, gh = 384, 128, 8, 2, 128
     W, b = _gate_weights(L, H, gh, seed=3)
     w_out = torch.randn(d, d, generator=g).bfloat16()
-    tree = dict(kind="tree", w_gate=torch.randn(ff, d, generator=g).bfloat16(),
-                w_up=torch.randn(ff, d, generator=g).bfloat16(),
-                w_down=torch.randn(d, ff, generator=g).bfloat16(), w_out=w_out,
-                wi=W[0], wf=W[1], wr=W[2], bi=b[0], bf=b[1], br=b[2])
-    attn = dict(kind="attn", w_gate=torch.randn(ff, d, generator=g).bfloat16(),
-                w_up=torch.randn(ff, d, generator=g).bfloat16(),
-                w_down=torch.randn(d, ff, generator=g).bfloat16())
-    packed = SimpleNamespace(layers=[tree, attn])
+    mk = lambda *s: torch.randn(*s, generator=g).bfloat16()  # noqa: E731
+    tree = dict(kind="tree", w3=mk(3 * d, d), w_gate=mk(ff, d), w_up=mk(ff, d),
+                w_down=mk(d, ff), w_out=w_out, wi=W[0], wf=W[1], wr=W[2],
+                bi=b[0], bf=b[1], br=b[2])
+    attn = dict(kind="attn", wqkv=mk(3 * d, d), w_gate=mk(ff, d), w_up=mk(ff, d),
+                w_down=mk(d, ff), w_out=mk(d, d))
+    emb = mk(515, d)
+    packed = SimpleNamespace(layers=[tree, attn], lm_head=emb)
     pack_step_weights(packed)
+    assert torch.equal(_unswizzle(packed.lm_head_sw[:512]), emb[:512])
     for lay in (tree, attn):
-        gu = lay["w_gu_pairs"]
-        assert gu.shape == (ff, 2, d) and gu.is_contiguous()
+        gu = _unswizzle(lay["sw_gu"]).view(ff, 2, d)
         assert torch.equal(gu[:, 0], lay["w_gate"]) and torch.equal(gu[:, 1], lay["w_up"])
-        assert torch.equal(lay["w_downT"], lay["w_down"].t()) and lay["w_downT"].is_contiguous()
-    assert "w_gates_heads" not in attn
-    wh, bh = tree["w_gates_heads"], tree["b_gates_heads"]
-    assert wh.shape == (H, L, 3, gh) and bh.shape == (H, L, 3) and bh.dtype == torch.float32
+        assert torch.equal(_unswizzle(lay["sw_downT"]), lay["w_down"].t())
+        src = lay["w3"] if lay["kind"] == "tree" else lay["wqkv"]
+        assert torch.equal(_unswizzle(lay["sw_in3"]), src)
+    assert torch.equal(_unswizzle(attn["sw_out"]), attn["w_out"])
+    assert "sw_gates" not in attn
+    tiles = _unswizzle(tree["sw_gates"], 16).view(H, 3, 16, gh)
     for gi in range(3):
-        assert torch.equal(wh[:, :, gi].transpose(0, 1), W[gi])
+        assert torch.equal(tiles[:, gi, :L].transpose(0, 1), W[gi])
+    assert not tiles[:, :, L:].any()
+    bh = tree["b_gates_heads"]
+    assert bh.shape == (H, L, 3) and bh.dtype == torch.float32
+    for gi in range(3):
         assert torch.equal(bh[:, :, gi].transpose(0, 1), b[gi])
-    oh = tree["w_out_heads"]
     hd = d // H
-    assert oh.shape == (H, d, hd) and oh.is_contiguous()
+    heads = _unswizzle(tree["sw_out"], d).view(H, d, hd)
     for h in range(H):
-        assert torch.equal(oh[h], w_out[:, h * hd:(h + 1) * hd])
-    before = wh.data_ptr()
+        assert torch.equal(heads[h], w_out[:, h * hd:(h + 1) * hd])
+    before = tree["sw_gates"].data_ptr()
     pack_step_weights(packed)            # built once: a second call keeps the packs
-    assert tree["w_gates_heads"].data_ptr() == before
+    assert tree["sw_gates"].data_ptr() == before
