@@ -362,6 +362,214 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvIn in, Epi ep
   }
 }
 
+// ---------------------------------------------------------------- tensor-core GEMV
+// For 3..16 lockstep rows the FMA loops above cost 2*B FMAs per weight pair;
+// here the rows are the N side of mma.sync.m16n8k16 (bf16 in, fp32 out) and
+// a weight element costs 1/(8*16) of an instruction.  A CTA takes 16-row
+// tiles of the weight matrix (8 epilogue units: row pairs), its 8 warps
+// split K, and each warp holds 4 chunks of 32 columns per pass in registers.
+//
+// Fragments come straight from global memory with 16-byte loads: lane
+// (g, t4) reads columns [32c + 8 t4, +8) of tile rows g and g + 8.  The mma
+// sums over its 16 "logical" k of a k-step; which physical columns they are
+// does not matter as long as the activation fragment uses the same ones, so
+// k-step s of chunk c takes physical columns 32c + 8 t4 + 4s + {0,1} as
+// logical k {2 t4, 2 t4 + 1} and 32c + 8 t4 + 4s + {2,3} as {2 t4 + 8, 2 t4 + 9}
+// in both operands.  The activations sit in shared memory with the same
+// column order and rows padded by 64 bytes (conflict-free 16-byte reads).
+constexpr int kTcWarps = 8;
+constexpr int kTcChunks = 4;                          // 32-column chunks per warp and pass
+constexpr int kTcPassCols = kTcWarps * kTcChunks * 32;  // 1024 columns per pass
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__host__ __device__ constexpr size_t tc_smem_bytes(int nt, int K) {
+  return (size_t)nt * 8 * (K + 32) * 2 + (size_t)kTcWarps * 16 * 16 * 4 + 16 * 17 * 4;
+}
+
+template <int NT, class Epi>
+__global__ void __launch_bounds__(kTcWarps * 32, 2) gemv_tc_kernel(GemvIn in, Epi epi) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int K = in.K, batch = in.batch, KP = K + 32;
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);            // [NT*8][KP]
+  float* red = reinterpret_cast<float*>(smem_raw + (size_t)NT * 8 * KP * 2);  // [warp][16][16]
+  float* tile_out = red + kTcWarps * 16 * 16;                                // [16][17]
+  __shared__ float s_rstd[16];
+  pdl_trigger();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int nunits = epi.units();
+  const int ntiles = (nunits + 7) / 8;
+  const int nchunks = K / 32;
+  const int npass = (K + kTcPassCols - 1) / kTcPassCols;
+  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int nitems = my_tiles * npass;
+
+  // weight rows of tile rows g and g + 8 (units past the end read the last
+  // unit's rows; their results are dropped)
+  auto tile_rows = [&](int tile, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) {
+    const __nv_bfloat16 *a, *b;
+    epi.rows(min(tile * 8 + (g >> 1), nunits - 1), a, b);
+    r0 = (g & 1) ? b : a;
+    epi.rows(min(tile * 8 + 4 + (g >> 1), nunits - 1), a, b);
+    r1 = (g & 1) ? b : a;
+  };
+  auto load_item = [&](int item, uint4 (&w)[2 * kTcChunks]) {
+    const int tile = blockIdx.x + (item / npass) * gridDim.x, pass = item % npass;
+    const __nv_bfloat16 *r0, *r1;
+    tile_rows(tile, r0, r1);
+#pragma unroll
+    for (int i = 0; i < kTcChunks; ++i) {
+      const int c = pass * (kTcWarps * kTcChunks) + warp * kTcChunks + i;
+      if (c < nchunks) {
+        w[2 * i] = ld_stream16(r0 + c * 32 + 8 * t4);
+        w[2 * i + 1] = ld_stream16(r1 + c * 32 + 8 * t4);
+      }
+    }
+  };
+
+  // the first item's weights do not depend on the previous kernel
+  uint4 cur[2 * kTcChunks], nxt[2 * kTcChunks];
+  if (nitems > 0) load_item(0, cur);
+  if (lane == 0) {  // later tiles of this CTA: into L2 while the predecessor drains
+    for (int tile = blockIdx.x + gridDim.x * (1 + warp); tile < ntiles; tile += gridDim.x * kTcWarps)
+      for (int r = 0; r < 16; r += 2) {
+        const __nv_bfloat16 *a, *b;
+        epi.rows(min(tile * 8 + r / 2, nunits - 1), a, b);
+        prefetch_l2(a, (uint32_t)K * 2);
+        if (b != a) prefetch_l2(b, (uint32_t)K * 2);
+      }
+  }
+  pdl_wait();
+
+  // activations (RMS-normalised when norm_w is set) as bf16 rows of xs
+  if (in.x_f32) {
+    const float* x = static_cast<const float*>(in.x);
+    if (in.norm_w) {
+      for (int b = warp; b < batch; b += kTcWarps) {
+        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)b * K);
+        float ss = 0.f;
+        for (int i = lane; i < K / 4; i += 32) {
+          const float4 v = xr[i];
+          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) s_rstd[b] = rsqrtf(ss / (float)K + kNormEps);
+      }
+      __syncthreads();
+    }
+    const int k4 = K / 4;
+    for (int i = tid; i < batch * k4; i += blockDim.x) {
+      const int b = i / k4, k = (i - b * k4) * 4;
+      float4 v = reinterpret_cast<const float4*>(x + (size_t)b * K)[k / 4];
+      if (in.norm_w) {
+        const float r = s_rstd[b];
+        const uint2 wv = *reinterpret_cast<const uint2*>(in.norm_w + k);
+        const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.x));
+        const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.y));
+        v.x = v.x * r * w01.x;
+        v.y = v.y * r * w01.y;
+        v.z = v.z * r * w23.x;
+        v.w = v.w * r * w23.y;
+      }
+      uint2 pk;
+      pk.x = pack2(v.x, v.y);
+      pk.y = pack2(v.z, v.w);
+      *reinterpret_cast<uint2*>(xs + (size_t)b * KP + k) = pk;
+    }
+  } else {
+    const int k8 = K / 8;
+    const uint4* x = static_cast<const uint4*>(in.x);
+    for (int i = tid; i < batch * k8; i += blockDim.x) {
+      const int b = i / k8, k = (i - b * k8) * 8;
+      *reinterpret_cast<uint4*>(xs + (size_t)b * KP + k) = x[i];
+    }
+  }
+  __syncthreads();
+
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  for (int item = 0; item < nitems; ++item) {
+    if (item + 1 < nitems) load_item(item + 1, nxt);
+    const int tile = blockIdx.x + (item / npass) * gridDim.x, pass = item % npass;
+#pragma unroll
+    for (int i = 0; i < kTcChunks; ++i) {
+      const int c = pass * (kTcWarps * kTcChunks) + warp * kTcChunks + i;
+      if (c < nchunks) {
+        uint4 xv[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          xv[nt] = *reinterpret_cast<const uint4*>(xs + (size_t)(nt * 8 + g) * KP + c * 32 + 8 * t4);
+        const uint4 wa = cur[2 * i], wb = cur[2 * i + 1];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_bf16_16816(acc[nt], wa.x, wb.x, wa.y, wb.y, xv[nt].x, xv[nt].y);
+          mma_bf16_16816(acc[nt], wa.z, wb.z, wa.w, wb.w, xv[nt].z, xv[nt].w);
+        }
+      }
+    }
+    if (pass == npass - 1) {
+      // partial tiles of the 8 warps meet in shared memory
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float* pr = red + (size_t)warp * 256;
+        *reinterpret_cast<float2*>(pr + g * 16 + nt * 8 + 2 * t4) = make_float2(acc[nt][0], acc[nt][1]);
+        *reinterpret_cast<float2*>(pr + (g + 8) * 16 + nt * 8 + 2 * t4) =
+            make_float2(acc[nt][2], acc[nt][3]);
+        acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+      }
+      __syncthreads();
+      {
+        const int r = tid >> 4, col = tid & 15;
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kTcWarps; ++w) s += red[w * 256 + r * 16 + col];
+        tile_out[r * 17 + col] = s;
+      }
+      __syncthreads();
+      {
+        const int j = tid >> 5, row = (tid >> 4) & 1, b = tid & 15;
+        const int u = tile * 8 + j;
+        if (u < nunits && b < batch) {
+          const __nv_bfloat16 *a, *bb;
+          const bool has1 = epi.rows(u, a, bb);
+          epi.store(u, b, row, tile_out[(2 * j + row) * 17 + b], tile_out[(2 * j + 1 - row) * 17 + b],
+                    has1);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2 * kTcChunks; ++i) cur[i] = nxt[i];
+  }
+}
+
+template <int NT, class Epi>
+int launch_gemv_tc(const GemvIn& in, const Epi& epi, int nunits, cudaStream_t st) {
+  const size_t smem = tc_smem_bytes(NT, in.K);
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaFuncSetAttribute(gemv_tc_kernel<NT, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)tc_smem_bytes(2, 5632));
+    configured_dev = dev;
+  }
+  const int ntiles = (nunits + 7) / 8;
+  const int per_sm = smem <= 110 * 1024 ? 2 : 1;
+  const int grid = std::min(ntiles, sm_count() * per_sm);
+  return launch_pdl(gemv_tc_kernel<NT, Epi>, dim3(grid), dim3(kTcWarps * 32), smem, st, in, epi)
+             ? set_error(DH_ERR_CUDA, "gemv_tc_kernel launch: %s", cudaGetErrorString(cudaGetLastError()))
+             : DH_OK;
+}
+
 template <int MAXB, class Epi>
 int launch_gemv_b(const GemvIn& in, const Epi& epi, int nunits, cudaStream_t st) {
   const size_t smem = (size_t)MAXB * in.K * sizeof(__nv_bfloat16);
@@ -393,6 +601,10 @@ int launch_gemv(GemvIn in, const Epi& epi, int nunits, cudaStream_t st) {
     return set_error(DH_ERR_SHAPE, "gemv: batch*K too large for shared memory");
   if (in.batch == 1) return launch_gemv_b<1>(in, epi, nunits, st);
   if (in.batch == 2) return launch_gemv_b<2>(in, epi, nunits, st);
+  if (in.K % 32 == 0 && aligned16(in.x)) {  // tensor cores from three rows on
+    if (in.batch <= 8) return launch_gemv_tc<1>(in, epi, nunits, st);
+    return launch_gemv_tc<2>(in, epi, nunits, st);
+  }
   if (in.batch <= 4) return launch_gemv_b<4>(in, epi, nunits, st);
   if (in.batch <= 8) return launch_gemv_b<8>(in, epi, nunits, st);
   return launch_gemv_b<16>(in, epi, nunits, st);
@@ -568,6 +780,175 @@ __global__ void __launch_bounds__(128) tree_step_kernel(TreeStepParams p) {
     *reinterpret_cast<uint4*>(p.y + (size_t)b * d + c0) = pack8(V);
   }
   if (tid == 0) p.counters[h] = 0;
+}
+
+// ---------------------------------------------------------------- tree step, 3..16 rows
+// Gate readouts on the tensor cores.  For one level l the readouts of every
+// head and gate form one GEMM: D (NP x B) = W_l (NP x gh) . hv_l (gh x B),
+// with W_l the packed rows g*H + h (NP = 3H padded to 16) and hv_l[k, b] =
+// relu(A[b, k] + B_hist[b, t - 2^l, k])^2 in bf16 (zero history where the
+// source position is missing or in another document).  hv_l is formed once
+// per level and column, for all heads.  Grid (L, gh / 256): each CTA adds
+// its 256-column share into the fp32 pre-activations with atomics; the
+// recurrence kernel that follows reads them and leaves zeros behind.
+struct TreeGatesTcParams {
+  const __nv_bfloat16 *a, *bh, *w;
+  const int64_t* t_buf;
+  const int* doc;  // nullable
+  float* pre;      // (batch, L, NP) fp32, zero on entry
+  int batch, max_len, L, NP, gh;
+};
+
+template <int MT>
+__global__ void __launch_bounds__(256) tree_gates_tc_kernel(TreeGatesTcParams p) {
+  __shared__ float red[kTcWarps][MT * 16][17];
+  __shared__ bool s_ok[16];
+  pdl_trigger();
+  const int l = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int gh = p.gh, NP = p.NP;
+  const long long t = *p.t_buf;  // advanced only by the last kernel of a step
+  const long long src = t - (1ll << l);
+  // this warp's 32 columns (warps past gh contribute zeros)
+  const bool live = (blockIdx.y * kTcWarps + warp) * 32 < gh;
+  const int k0 = live ? (blockIdx.y * kTcWarps + warp) * 32 + 8 * t4 : 0;
+  // gate weights: independent of the earlier kernels of the step
+  uint4 wa[MT], wb[MT];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    const size_t r = (size_t)l * NP + mt * 16 + g;
+    wa[mt] = live ? ld_stream16(p.w + r * gh + k0) : make_uint4(0, 0, 0, 0);
+    wb[mt] = live ? ld_stream16(p.w + (r + 8) * gh + k0) : make_uint4(0, 0, 0, 0);
+  }
+  pdl_wait();
+  if (tid < 16) {
+    bool ok = src >= 0 && tid < p.batch;
+    if (ok && p.doc) ok = p.doc[(size_t)tid * p.max_len + src] == p.doc[(size_t)tid * p.max_len + t];
+    s_ok[tid] = ok;
+  }
+  __syncthreads();
+  // hv fragments of lockstep rows n = g and g + 8 for this lane's 8 columns
+  uint32_t hv[2][4];
+  const __nv_bfloat162 z2 = __floats2bfloat162_rn(0.f, 0.f);
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int n = nt * 8 + g;
+    uint4 av = make_uint4(0, 0, 0, 0), bv = make_uint4(0, 0, 0, 0);
+    if (live && n < p.batch) {
+      av = *reinterpret_cast<const uint4*>(p.a + (size_t)n * gh + k0);
+      if (s_ok[n]) bv = *reinterpret_cast<const uint4*>(p.bh + ((size_t)n * p.max_len + src) * gh + k0);
+    }
+    const uint32_t* ap = &av.x;
+    const uint32_t* bp = &bv.x;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __hmax2(__hadd2(*reinterpret_cast<const __nv_bfloat162*>(ap + i),
+                                         *reinterpret_cast<const __nv_bfloat162*>(bp + i)),
+                                 z2);
+      h = __hmul2(h, h);  // relu squared, rounded to bf16
+      hv[nt][i] = n < p.batch ? *reinterpret_cast<uint32_t*>(&h) : 0u;
+    }
+  }
+  float acc[MT][2][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.f;
+      mma_bf16_16816(acc[mt][nt], wa[mt].x, wb[mt].x, wa[mt].y, wb[mt].y, hv[nt][0], hv[nt][1]);
+      mma_bf16_16816(acc[mt][nt], wa[mt].z, wb[mt].z, wa[mt].w, wb[mt].w, hv[nt][2], hv[nt][3]);
+    }
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      red[warp][mt * 16 + g][nt * 8 + 2 * t4] = acc[mt][nt][0];
+      red[warp][mt * 16 + g][nt * 8 + 2 * t4 + 1] = acc[mt][nt][1];
+      red[warp][mt * 16 + g + 8][nt * 8 + 2 * t4] = acc[mt][nt][2];
+      red[warp][mt * 16 + g + 8][nt * 8 + 2 * t4 + 1] = acc[mt][nt][3];
+    }
+  __syncthreads();
+  for (int i = tid; i < MT * 16 * 16; i += blockDim.x) {
+    const int m = i >> 4, n = i & 15;
+    if (n < p.batch) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < kTcWarps; ++w) s += red[w][m][n];
+      atomicAdd(p.pre + ((size_t)n * p.L + l) * NP + m, s);
+    }
+  }
+}
+
+// Level recurrence of one (head, row): one thread per channel, every level's
+// history value fetched up front (ring slots of earlier positions, written by
+// earlier steps), then the short serial chain (fused_step.py:62-88 semantics,
+// fp32 state, each level's value stored into its ring slot at t).
+struct TreeRecurParams {
+  float* pre;  // (batch, L, NP): read and cleared
+  const float *bi, *bf, *br;
+  const int64_t* t_buf;
+  const int* doc;  // nullable
+  __nv_bfloat16* rg;
+  const __nv_bfloat16* v0;
+  __nv_bfloat16* ring;
+  __nv_bfloat16* y;
+  int batch, max_len, L, H, hd, NP, S;
+};
+
+__global__ void __launch_bounds__(64) tree_recur_kernel(TreeRecurParams p) {
+  constexpr int LMAX = 16;
+  __shared__ float s_f[LMAX], s_c[LMAX];
+  pdl_trigger();
+  const int h = blockIdx.x, b = blockIdx.y, c = threadIdx.x;
+  const int L = p.L, H = p.H, hd = p.hd, d = H * hd;
+  const long long t = *p.t_buf;
+  __nv_bfloat16* ringb = p.ring + (size_t)b * p.S * d + h * hd + c;
+  float vs[LMAX];
+#pragma unroll
+  for (int l = 0; l < LMAX; ++l) {
+    const long long s = t - (1ll << l);
+    vs[l] = 0.f;
+    if (l < L && s >= 0 && c < hd)
+      vs[l] = bf2f(ringb[(size_t)(((2ll << l) - 2) + (s & ((2ll << l) - 1))) * d]);
+  }
+  float rg_src = 0.f;
+  if (c < L) {
+    const long long s = t - (1ll << c);
+    if (s >= 0) rg_src = bf2f(p.rg[(((size_t)b * p.max_len + s) * L + c) * H + h]);
+  }
+  pdl_wait();
+  if (c < L) {
+    const int l = c;
+    const long long s = t - (1ll << l);
+    bool ok = s >= 0;
+    if (ok && p.doc) ok = p.doc[(size_t)b * p.max_len + s] == p.doc[(size_t)b * p.max_len + t];
+    float* pr = p.pre + ((size_t)b * L + l) * p.NP;
+    const float pi = pr[h], pf = pr[H + h], prr = pr[2 * H + h];
+    pr[h] = 0.f;
+    pr[H + h] = 0.f;
+    pr[2 * H + h] = 0.f;
+    const float okf = ok ? 1.f : 0.f;
+    const int lh = l * H + h;
+    const float ig = sigmoidf_(pi + p.bi[lh]) * okf;
+    const float fg = sigmoidf_(pf + p.bf[lh]) * okf + (1.f - okf);
+    const float rgt = sigmoidf_(prr + p.br[lh]);
+    p.rg[(((size_t)b * p.max_len + t) * L + l) * H + h] = f2bf(rgt);
+    s_f[l] = fg;
+    s_c[l] = ig * rg_src;
+  }
+  __syncthreads();
+  if (c >= hd) return;
+  const __nv_bfloat16 v0 = p.v0[(size_t)b * d + h * hd + c];
+  float V = bf2f(v0);
+  ringb[(size_t)(t & 1) * d] = v0;  // ring 0 at t
+#pragma unroll
+  for (int l = 0; l < LMAX; ++l) {
+    if (l < L) {
+      V = s_f[l] * V + s_c[l] * vs[l];
+      if (l + 1 < L) ringb[(size_t)(((2ll << (l + 1)) - 2) + (t & ((2ll << (l + 1)) - 1))) * d] = f2bf(V);
+    }
+  }
+  p.y[(size_t)b * d + h * hd + c] = f2bf(V);
 }
 
 // ---------------------------------------------------------------- attention
@@ -1007,6 +1388,43 @@ extern "C" int dh_decode_tree_step(const void* a_in, const void* b_hist, const v
                     : nb <= 4 ? launch_pdl(tree_step_kernel<4>, grid, dim3(128), 0, STREAM(stream), p)
                               : launch_pdl(tree_step_kernel<16>, grid, dim3(128), 0, STREAM(stream), p);
     if (bad) return check_launch("tree_step_kernel");
+  }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_tree_step_tc(const void* a_in, const void* b_hist, const void* w_gates,
+                                      int np, const float* bi, const float* bf, const float* br,
+                                      const int64_t* t_buf, float* pre, void* rg_hist,
+                                      const void* v0, void* v_ring, void* y, const int* doc_hist,
+                                      int batch, int max_len, int L, int H, int hd, int gh,
+                                      void* stream) {
+  DH_REQUIRE(a_in && b_hist && w_gates && bi && bf && br && t_buf && pre && rg_hist && v0 &&
+                 v_ring && y,
+             DH_ERR_ARG, "dh_decode_tree_step_tc: null pointer");
+  DH_REQUIRE(L >= 1 && L <= 16 && H >= 1 && np % 16 == 0 && np >= 3 * H && np <= 48 &&
+                 hd >= 1 && hd <= 64 && gh % 32 == 0 && batch >= 1,
+             DH_ERR_SHAPE, "dh_decode_tree_step_tc: unsupported sizes (L=%d H=%d np=%d hd=%d gh=%d)",
+             L, H, np, hd, gh);
+  DH_REQUIRE(aligned16(a_in) && aligned16(b_hist) && aligned16(w_gates), DH_ERR_ARG,
+             "dh_decode_tree_step_tc: a, B_hist and the gate weights must be 16-byte aligned");
+  const int d = H * hd, S = (1 << (L + 1)) - 2;
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    const int* doc = doc_hist ? doc_hist + (size_t)b0 * max_len : nullptr;
+    float* pr = pre + (size_t)b0 * L * np;
+    TreeGatesTcParams gp{BF(a_in) + (size_t)b0 * gh, BF(b_hist) + (size_t)b0 * max_len * gh,
+                         BF(w_gates), t_buf, doc, pr, nb, max_len, L, np, gh};
+    const dim3 gg(L, (gh + 255) / 256);
+    const int bad = np <= 16   ? launch_pdl(tree_gates_tc_kernel<1>, gg, dim3(256), 0, STREAM(stream), gp)
+                    : np <= 32 ? launch_pdl(tree_gates_tc_kernel<2>, gg, dim3(256), 0, STREAM(stream), gp)
+                               : launch_pdl(tree_gates_tc_kernel<3>, gg, dim3(256), 0, STREAM(stream), gp);
+    if (bad) return check_launch("tree_gates_tc_kernel");
+    TreeRecurParams rp{pr, bi, bf, br, t_buf, doc,
+                       BFM(rg_hist) + (size_t)b0 * max_len * L * H,
+                       BF(v0) + (size_t)b0 * d, BFM(v_ring) + (size_t)b0 * S * d,
+                       BFM(y) + (size_t)b0 * d, nb, max_len, L, H, hd, np, S};
+    if (launch_pdl(tree_recur_kernel, dim3(H, nb), dim3(64), 0, STREAM(stream), rp))
+      return check_launch("tree_recur_kernel");
   }
   return DH_OK;
 }

@@ -567,15 +567,22 @@ __device__ void gemv_tiles(Ctx& c, const Seg& s, const uint32_t (&bx)[8][2], int
   for (int u = 0; u < s.units; ++u) {
     const uint8_t* chunk = chunk_acquire(c);
     const uint32_t base = smem_u32(chunk);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    // four independent accumulator chains: the k-steps do not wait on one
+    // another's mma latency
+    float ac[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ac[j][0] = ac[j][1] = ac[j][2] = ac[j][3] = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (i < ksw) {
         uint32_t a[4];
         ldsm_x4(a, base + swz(arow, (warp * ksw + i) * 2 + ahalf, rb));
-        mma16816(acc, a, bx[i]);
+        mma16816(ac[i & 3], a, bx[i]);
       }
     }
+    float acc[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[e] = (ac[0][e] + ac[1][e]) + (ac[2][e] + ac[3][e]);
     float* pb = c.red + ((size_t)(u & 1) * kWarps + warp) * 16 * 8;  // [16 rows][8 columns]
     pb[g * 8 + 2 * t4] = acc[0];
     pb[g * 8 + 2 * t4 + 1] = acc[1];
@@ -739,16 +746,23 @@ __device__ void phase_b_tree(Ctx& c, int li) {
     const int brow = lane & 7, bhalf = (lane >> 3) & 1;
     const __nv_bfloat162 z2 = __floats2bfloat162_rn(0.f, 0.f);
     for (int b = 0; b < B; ++b) {
-      float acc[3][2][4];
+      // two accumulator sets (even / odd k-steps) halve the mma chains
+      float acc2[2][3][2][4];
 #pragma unroll
-      for (int g = 0; g < 3; ++g)
+      for (int s2 = 0; s2 < 2; ++s2)
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
+        for (int g = 0; g < 3; ++g)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) acc[g][nt][e] = 0.f;
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc2[s2][g][nt][e] = 0.f;
 #pragma unroll 1
-      for (int i = 0; i < ksw; ++i) {
-        {
+      for (int i0 = 0; i0 < ksw; i0 += 2) {
+#pragma unroll
+        for (int s2 = 0; s2 < 2; ++s2) {
+          const int i = i0 + s2;
+          if (i >= ksw) break;
+          float (&acc)[3][2][4] = acc2[s2];
           const int ch = (warp * ksw + i) * 2;  // first 16-byte chunk of this k-step
           // A values at this thread's fragment columns (k = 8 ch + 2 t4, +8)
           const __nv_bfloat162 a_lo = *reinterpret_cast<const __nv_bfloat162*>(xs_at(c, b, ch * 8 + 2 * t4));
@@ -776,6 +790,13 @@ __device__ void phase_b_tree(Ctx& c, int li) {
           }
         }
       }
+      float acc[3][2][4];
+#pragma unroll
+      for (int g = 0; g < 3; ++g)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[g][nt][e] = acc2[0][g][nt][e] + acc2[1][g][nt][e];
       // diagonal: level l = g4 sits in acc[..][0][0] when g4 == 2 t4 and in
       // acc[..][0][1] when g4 == 2 t4 + 1; level 8 + g4 likewise in [1][2] / [1][3]
       float* rb = red + ((size_t)warp * kMaxB + b) * 48;

@@ -176,11 +176,27 @@ class FusedGraphedHybridDecoder:
         self.persistent = (self.step_kernel == "persistent" and batch <= 2 and d <= 1024
                            and d % 128 == 0 and hd == 64
                            and cfg.levels * (2 * d + 16) <= 32768)
-        if not self.persistent:
-            # the fused FFN reads the down projection by rows of its transpose
+        # up to 2 rows: one fused FFN launch, which reads the down projection
+        # by rows of its transpose; from 3 rows on the gate/up and the down
+        # projection run as two tensor-core GEMVs (u through HBM, 16 KB a row)
+        self.ffn_fused = batch <= 2
+        if not self.persistent and self.ffn_fused:
             for lay in self.w.layers:
                 if "w_downT" not in lay:
                     lay["w_downT"] = lay["w_down"].t().contiguous()
+        # tree blocks of 3..16 rows: tensor-core gate readouts over the packed
+        # gate rows (all heads of a level at once), pre-activations in fp32
+        self.tree_tc = (not self.persistent and batch > 2 and 3 * H <= 48 and d % 32 == 0
+                        and hd <= 64)
+        self.pre = None
+        if self.tree_tc:
+            from .ops import pack_gate_weights
+            np_ = ((3 * H + 15) // 16) * 16
+            self.pre = torch.zeros(batch, L, np_, device=dev, dtype=f32)
+            for lay in self.w.layers:
+                if lay["kind"] == "tree" and "w_gates_np" not in lay:
+                    lay["w_gates_np"], _, lay["gates_np"] = pack_gate_weights(
+                        lay["wi"], lay["wf"], lay["wr"], lay["bi"], lay["bf"], lay["br"])
         self._step_params = None
         if self.persistent:
             from .step_params import build_step_params
@@ -211,11 +227,18 @@ class FusedGraphedHybridDecoder:
             if lay["kind"] == "tree":
                 call("dh_decode_mixer_in", P(self.x), P(lay["norm1"]), P(lay["w3"]), P(self.v0),
                      P(self.a), P(cache.B_hist), P(self.t_buf), self.max_len, B, d, s)
-                call("dh_decode_tree_step", P(self.a), P(cache.B_hist), P(lay["wi"]),
-                     P(lay["wf"]), P(lay["wr"]), P(lay["bi"]), P(lay["bf"]), P(lay["br"]),
-                     P(self.t_buf), P(self.ig), P(self.fg), P(cache.rg_hist), P(self.v0),
-                     P(cache.V_ring), P(self.y), P(tree_ctr), P(self.doc_hist), B,
-                     self.max_len, L, H, hd, d, s)
+                if self.tree_tc:
+                    call("dh_decode_tree_step_tc", P(self.a), P(cache.B_hist),
+                         P(lay["w_gates_np"]), lay["gates_np"], P(lay["bi"]), P(lay["bf"]),
+                         P(lay["br"]), P(self.t_buf), P(self.pre), P(cache.rg_hist),
+                         P(self.v0), P(cache.V_ring), P(self.y), P(self.doc_hist), B,
+                         self.max_len, L, H, hd, d, s)
+                else:
+                    call("dh_decode_tree_step", P(self.a), P(cache.B_hist), P(lay["wi"]),
+                         P(lay["wf"]), P(lay["wr"]), P(lay["bi"]), P(lay["bf"]), P(lay["br"]),
+                         P(self.t_buf), P(self.ig), P(self.fg), P(cache.rg_hist), P(self.v0),
+                         P(cache.V_ring), P(self.y), P(tree_ctr), P(self.doc_hist), B,
+                         self.max_len, L, H, hd, d, s)
             else:
                 call("dh_decode_attn_in", P(self.x), P(lay["norm1"]), P(lay["wqkv"]),
                      P(cache.rope_cos), P(cache.rope_sin), P(self.q), P(cache.k), P(cache.v),
@@ -227,8 +250,14 @@ class FusedGraphedHybridDecoder:
             # then the whole FFN with its residual in one launch
             call("dh_decode_linear_residual", P(self.y), P(lay["w_out"]), P(self.x),
                  P(self.x_copy), B, d, d, s)
-            call("dh_decode_ffn", P(self.x_copy), P(lay["norm2"]), P(lay["w_gate"]),
-                 P(lay["w_up"]), P(lay["w_downT"]), P(self.x), B, d, ff, s)
+            if self.ffn_fused:
+                call("dh_decode_ffn", P(self.x_copy), P(lay["norm2"]), P(lay["w_gate"]),
+                     P(lay["w_up"]), P(lay["w_downT"]), P(self.x), B, d, ff, s)
+            else:
+                call("dh_decode_ffn_in", P(self.x_copy), P(lay["norm2"]), P(lay["w_gate"]),
+                     P(lay["w_up"]), P(self.u), B, d, ff, s)
+                call("dh_decode_linear_residual", P(self.u), P(lay["w_down"]), P(self.x),
+                     None, B, ff, d, s)
         call("dh_decode_logits", P(self.x), P(W.norm_out), P(W.lm_head), P(self.logits_out),
              B, d, V, s)
         call("dh_decode_advance", P(self.t_buf), s)

@@ -90,6 +90,23 @@ DH_API int dh_decode_tree_step(const void* a_in, const void* b_hist, const void*
                         const int* doc_hist, int batch, int max_len, int L, int H, int hd, int gh,
                         void* stream);
 
+/* The same tree-block step for lockstep batches (the launch for 3..16 rows;
+ * also replaces step_gates_kernel + step_scan_kernel, fused_step.py:26-88,
+ * decoding.py:477-486): the gate readouts of one level, all heads and gates
+ * at once, run on the tensor cores with relu^2(A + B_hist[t - 2^l]) rounded
+ * to bf16 as the mma operand, then one thread per channel runs the level
+ * recurrence.  w_gates: bf16 (L * np, gh), row l*np + g*H + h = W_g[l, h]
+ * (g = admit, forget, transmit; rows 3H..np-1 zero; np a multiple of 16,
+ * at most 48); pre: fp32 scratch (batch, L, np), zero before the first
+ * call and left zero after each call.  gh a multiple of 32, hd <= 64.
+ * Writes what dh_decode_tree_step writes. */
+DH_API int dh_decode_tree_step_tc(const void* a_in, const void* b_hist, const void* w_gates,
+                                  int np, const float* bi, const float* bf, const float* br,
+                                  const int64_t* t_buf, float* pre, void* rg_hist,
+                                  const void* v0, void* v_ring, void* y, const int* doc_hist,
+                                  int batch, int max_len, int L, int H, int hd, int gh,
+                                  void* stream);
+
 /* x += y . W^T (W: d_out x k, bf16; y bf16 (batch, k)): linear_out and
  * linear_down with the residual add (decoding.py:487-488, 434-435).  x_copy
  * (nullable) receives a copy of the updated x (the input of dh_decode_ffn). */

@@ -62,8 +62,12 @@ def test_decoder_matches_forward_small_seed0(small_s0):
     _compare(*small_s0)
 
 
-def test_decoder_batched(small_nd):
-    _compare(*small_nd, batch=3, seed=5)
+@pytest.mark.parametrize("batch", [3, 9])
+def test_decoder_batched(small_nd, batch):
+    """From 3 rows the GEMVs and the tree gates run on the tensor cores
+    (one 8-column mma tile up to 8 rows, two from 9)."""
+    dec = _compare(*small_nd, batch=batch, seed=5)[0]
+    assert dec.tree_tc and not dec.ffn_fused
 
 
 def test_prefill_logits_match_forward(small_nd):

@@ -41,12 +41,15 @@ def small():
     return cfg, model.eval(), sd32
 
 
-@pytest.mark.parametrize("stepwise", [False, True])
-def test_multi_document_decode_matches_oracle_forward(small, stepwise):
+@pytest.mark.parametrize("stepwise,batch", [(False, 2), (True, 2), (False, 4)])
+def test_multi_document_decode_matches_oracle_forward(small, stepwise, batch):
+    """batch 4 takes the tensor-core tree step (document mask in the gate
+    operand and in the recurrence)."""
     cfg, model, sd32 = small
     prompt, total = 60, 72
     # separators in the prompt (one pair back to back) and among the fed tokens
-    ids = _ids_with_separators(cfg, 2, total, ((0, 10), (1, 33), (1, 34), (0, 63), (1, 70)), 5)
+    seps = ((0, 10), (1, 33), (1, 34), (0, 63), (1, 70)) + ((3, 5), (3, 66))[:2 * (batch > 2)]
+    ids = _ids_with_separators(cfg, batch, total, seps, 5)
     ref32 = oracle.forward(sd32, cfg, ids)[:, prompt - 1:total - 1]
     ref16 = oracle.forward(cast_sd(sd32, torch.bfloat16), cfg, ids)[:, prompt - 1:total - 1].float()
     dec = FusedGraphedHybridDecoder(model, multi_document=True)
