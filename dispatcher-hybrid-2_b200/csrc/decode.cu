@@ -64,6 +64,7 @@ struct GemvIn {
   const __nv_bfloat16* norm_w;   // nullable: RMSNorm weight applied to x
   int K;
   int batch;
+  int* status;                   // nullable: raised when a bounded wait gives up
 };
 
 // ---- epilogues: rows(u) names the two weight rows of work unit u;
@@ -363,23 +364,27 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvIn in, Epi ep
 }
 
 // ---------------------------------------------------------------- tensor-core GEMV
-// For 3..16 lockstep rows the FMA loops above cost 2*B FMAs per weight pair;
-// here the rows are the N side of mma.sync.m16n8k16 (bf16 in, fp32 out) and
-// a weight element costs 1/(8*16) of an instruction.  A CTA takes 16-row
-// tiles of the weight matrix (8 epilogue units: row pairs), its 8 warps
-// split K, and each warp holds 4 chunks of 32 columns per pass in registers.
+// The lockstep rows are the N side of mma.sync.m16n8k16 (bf16 in, fp32 out):
+// one or two 8-column tiles for up to 8 or 16 rows, so a weight element
+// costs 1/(8*16) of an instruction instead of 2*B FMAs.  A CTA takes 16-row
+// tiles of the weight matrix (8 epilogue units: row pairs) in passes of 1024
+// columns; its 8 consumer warps split a pass into 4 chunks of 32 columns
+// each.  A producer warp streams the tiles with cp.async.bulk row copies into
+// a ring of shared-memory slots (rows padded to 2112 bytes, so the fragment
+// reads are bank-conflict free), completion on an mbarrier per slot.  One CTA
+// per SM keeps up to six 33 KB slots in flight without holding weights in
+// registers, and the producer starts before the predecessor kernel has
+// finished (the weights do not depend on it).
 //
-// Fragments come straight from global memory with 16-byte loads: lane
-// (g, t4) reads columns [32c + 8 t4, +8) of tile rows g and g + 8.  The mma
-// sums over its 16 "logical" k of a k-step; which physical columns they are
-// does not matter as long as the activation fragment uses the same ones, so
-// k-step s of chunk c takes physical columns 32c + 8 t4 + 4s + {0,1} as
-// logical k {2 t4, 2 t4 + 1} and 32c + 8 t4 + 4s + {2,3} as {2 t4 + 8, 2 t4 + 9}
-// in both operands.  The activations sit in shared memory with the same
-// column order and rows padded by 64 bytes (conflict-free 16-byte reads).
+// Fragments are plain 16-byte reads: lane (g, t4) reads columns
+// [32c + 8 t4, +8) of tile rows g and g + 8.  The mma sums over the 16
+// "logical" k of a k-step; which physical columns they are does not matter
+// as long as the activation fragment uses the same ones, so k-step s of
+// chunk c takes physical columns 32c + 8 t4 + 4s + {0,1} as logical k
+// {2 t4, 2 t4 + 1} and 32c + 8 t4 + 4s + {2,3} as {2 t4 + 8, 2 t4 + 9} in
+// both operands.  The activations sit in shared memory in natural column
+// order, rows padded by 64 bytes.
 constexpr int kTcWarps = 8;
-constexpr int kTcChunks = 4;                          // 32-column chunks per warp and pass
-constexpr int kTcPassCols = kTcWarps * kTcChunks * 32;  // 1024 columns per pass
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                                uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -390,134 +395,189 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__host__ __device__ constexpr size_t tc_smem_bytes(int nt, int K) {
-  return (size_t)nt * 8 * (K + 32) * 2 + (size_t)kTcWarps * 16 * 16 * 4 + 16 * 17 * 4;
+constexpr int kBulkRowBytes = 2112;                // 1024 columns + 64 bytes of padding
+constexpr int kBulkSlotBytes = 16 * kBulkRowBytes;  // one (tile, pass)
+constexpr int kBulkMaxSlots = 6;
+constexpr int kBulkThreads = (kTcWarps + 1) * 32;
+
+struct BulkShared {
+  uint64_t full[kBulkMaxSlots], empty[kBulkMaxSlots];
+  int abort;
+};
+
+__host__ __device__ constexpr size_t bulk_xs_bytes(int nt, int K) { return (size_t)nt * 8 * (K + 32) * 2; }
+__host__ __device__ constexpr size_t bulk_fixed_bytes(int nt, int K) {
+  return bulk_xs_bytes(nt, K) + (size_t)kTcWarps * 16 * 16 * 4 + 16 * 17 * 4 + sizeof(BulkShared) + 16;
 }
 
+__device__ __forceinline__ void csync_bulk() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
 template <int NT, class Epi>
-__global__ void __launch_bounds__(kTcWarps * 32, 2) gemv_tc_kernel(GemvIn in, Epi epi) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+__global__ void __launch_bounds__(kBulkThreads, 1)
+    gemv_bulk_kernel(GemvIn in, Epi epi, int nslots, int* status, uint32_t wait_limit) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   const int K = in.K, batch = in.batch, KP = K + 32;
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);            // [NT*8][KP]
-  float* red = reinterpret_cast<float*>(smem_raw + (size_t)NT * 8 * KP * 2);  // [warp][16][16]
+  uint8_t* slots = smem_raw;                                                 // [nslots][16][2112]
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw + (size_t)nslots * kBulkSlotBytes);
+  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + bulk_xs_bytes(NT, K));
   float* tile_out = red + kTcWarps * 16 * 16;                                // [16][17]
-  __shared__ float s_rstd[16];
-  pdl_trigger();
+  BulkShared* sh = reinterpret_cast<BulkShared*>(tile_out + 16 * 17);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t4 = lane & 3;
   const int nunits = epi.units();
   const int ntiles = (nunits + 7) / 8;
   const int nchunks = K / 32;
-  const int npass = (K + kTcPassCols - 1) / kTcPassCols;
-  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int nitems = my_tiles * npass;
-
-  // weight rows of tile rows g and g + 8 (units past the end read the last
-  // unit's rows; their results are dropped)
-  auto tile_rows = [&](int tile, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) {
-    const __nv_bfloat16 *a, *b;
-    epi.rows(min(tile * 8 + (g >> 1), nunits - 1), a, b);
-    r0 = (g & 1) ? b : a;
-    epi.rows(min(tile * 8 + 4 + (g >> 1), nunits - 1), a, b);
-    r1 = (g & 1) ? b : a;
-  };
-  auto load_item = [&](int item, uint4 (&w)[2 * kTcChunks]) {
-    const int tile = blockIdx.x + (item / npass) * gridDim.x, pass = item % npass;
-    const __nv_bfloat16 *r0, *r1;
-    tile_rows(tile, r0, r1);
-#pragma unroll
-    for (int i = 0; i < kTcChunks; ++i) {
-      const int c = pass * (kTcWarps * kTcChunks) + warp * kTcChunks + i;
-      if (c < nchunks) {
-        w[2 * i] = ld_stream16(r0 + c * 32 + 8 * t4);
-        w[2 * i + 1] = ld_stream16(r1 + c * 32 + 8 * t4);
-      }
+  const int npass = (K + 1023) / 1024;
+  const int nitems = (blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0) * npass;
+  if (tid == 0) {
+    for (int i = 0; i < nslots; ++i) {
+      mbar_init(&sh->full[i], 1);
+      mbar_init(&sh->empty[i], kTcWarps);
     }
-  };
-
-  // the first item's weights do not depend on the previous kernel
-  uint4 cur[2 * kTcChunks], nxt[2 * kTcChunks];
-  if (nitems > 0) load_item(0, cur);
-  if (lane == 0) {  // later tiles of this CTA: into L2 while the predecessor drains
-    for (int tile = blockIdx.x + gridDim.x * (1 + warp); tile < ntiles; tile += gridDim.x * kTcWarps)
-      for (int r = 0; r < 16; r += 2) {
-        const __nv_bfloat16 *a, *b;
-        epi.rows(min(tile * 8 + r / 2, nunits - 1), a, b);
-        prefetch_l2(a, (uint32_t)K * 2);
-        if (b != a) prefetch_l2(b, (uint32_t)K * 2);
-      }
+    sh->abort = 0;
+    fence_barrier_init();
   }
-  pdl_wait();
+  __syncthreads();
+  pdl_trigger();
 
-  // activations (RMS-normalised when norm_w is set) as bf16 rows of xs
-  if (in.x_f32) {
-    const float* x = static_cast<const float*>(in.x);
-    if (in.norm_w) {
-      for (int b = warp; b < batch; b += kTcWarps) {
-        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)b * K);
-        float ss = 0.f;
-        for (int i = lane; i < K / 4; i += 32) {
-          const float4 v = xr[i];
-          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        }
-        ss = warp_sum(ss);
-        if (lane == 0) s_rstd[b] = rsqrtf(ss / (float)K + kNormEps);
+  if (warp == kTcWarps) {  // ---------------- producer (one lane)
+    if (lane != 0) return;
+    int issued = 0;
+    for (int item = 0; item < nitems; ++item) {
+      const int slot = item % nslots;
+      if (item >= nslots &&
+          !mbar_wait(&sh->empty[slot], (uint32_t)(((item / nslots) - 1) & 1), status, wait_limit)) {
+        sh->abort = 1;
+        break;
       }
-      __syncthreads();
+      if (*reinterpret_cast<volatile int*>(&sh->abort)) break;
+      const int tile = blockIdx.x + (item / npass) * gridDim.x, pass = item % npass;
+      const int cols = min(1024, K - pass * 1024);
+      uint8_t* dst = slots + (size_t)slot * kBulkSlotBytes;
+      mbar_arrive_expect_tx(&sh->full[slot], (uint32_t)(16 * cols * 2));
+      for (int r = 0; r < 16; ++r) {
+        const __nv_bfloat16 *a, *b;
+        epi.rows(min(tile * 8 + (r >> 1), nunits - 1), a, b);
+        const __nv_bfloat16* row = (r & 1) ? b : a;
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_u32(dst + r * kBulkRowBytes)),
+            "l"(row + pass * 1024), "r"((uint32_t)(cols * 2)), "r"(smem_u32(&sh->full[slot]))
+            : "memory");
+      }
+      ++issued;
     }
+    // no copy may still be in flight into this CTA's memory when it exits
+    for (int sl = 0; sl < nslots; ++sl) {
+      const int n_s = issued / nslots + (sl < issued % nslots ? 1 : 0);
+      if (n_s > 0) mbar_wait(&sh->full[sl], (uint32_t)((n_s - 1) & 1), nullptr, 1u << 20);
+    }
+    return;
+  }
+
+  // ---------------- consumers (8 warps, named barrier 1)
+  const int g = lane >> 2, t4 = lane & 3;
+  pdl_wait();
+  if (in.x_f32) {
+    // warp w takes rows w and w + 8 whole: up to 1024 columns, 8 float4 per lane and row
+    const float* x = static_cast<const float*>(in.x);
     const int k4 = K / 4;
-    for (int i = tid; i < batch * k4; i += blockDim.x) {
-      const int b = i / k4, k = (i - b * k4) * 4;
-      float4 v = reinterpret_cast<const float4*>(x + (size_t)b * K)[k / 4];
-      if (in.norm_w) {
-        const float r = s_rstd[b];
-        const uint2 wv = *reinterpret_cast<const uint2*>(in.norm_w + k);
-        const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.x));
-        const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv.y));
-        v.x = v.x * r * w01.x;
-        v.y = v.y * r * w01.y;
-        v.z = v.z * r * w23.x;
-        v.w = v.w * r * w23.y;
+    float4 v[NT][8];
+    uint2 wn[8];
+#pragma unroll
+    for (int r = 0; r < NT; ++r) {
+      const int b = warp + 8 * r;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = lane + 32 * j;
+        v[r][j] = (b < batch && i < k4) ? reinterpret_cast<const float4*>(x + (size_t)b * K)[i]
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      uint2 pk;
-      pk.x = pack2(v.x, v.y);
-      pk.y = pack2(v.z, v.w);
-      *reinterpret_cast<uint2*>(xs + (size_t)b * KP + k) = pk;
+    }
+    if (in.norm_w) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = lane + 32 * j;
+        wn[j] = i < k4 ? *reinterpret_cast<const uint2*>(in.norm_w + 4 * i) : make_uint2(0, 0);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < NT; ++r) {
+      const int b = warp + 8 * r;
+      float sc = 1.f;
+      if (in.norm_w) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          ss += v[r][j].x * v[r][j].x + v[r][j].y * v[r][j].y + v[r][j].z * v[r][j].z + v[r][j].w * v[r][j].w;
+        sc = rsqrtf(warp_sum(ss) / (float)K + kNormEps);
+      }
+      if (b < batch) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = lane + 32 * j;
+          if (i < k4) {
+            float4 q = v[r][j];
+            if (in.norm_w) {
+              const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wn[j].x));
+              const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wn[j].y));
+              q = make_float4(q.x * sc * w01.x, q.y * sc * w01.y, q.z * sc * w23.x, q.w * sc * w23.y);
+            }
+            uint2 pk;
+            pk.x = pack2(q.x, q.y);
+            pk.y = pack2(q.z, q.w);
+            *reinterpret_cast<uint2*>(xs + (size_t)b * KP + 4 * i) = pk;
+          }
+        }
+      }
     }
   } else {
     const int k8 = K / 8;
-    const uint4* x = static_cast<const uint4*>(in.x);
-    for (int i = tid; i < batch * k8; i += blockDim.x) {
+    const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(in.x);
+    for (int i = tid; i < batch * k8; i += kTcWarps * 32) {
       const int b = i / k8, k = (i - b * k8) * 8;
-      *reinterpret_cast<uint4*>(xs + (size_t)b * KP + k) = x[i];
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(xs + (size_t)b * KP + k)),
+                   "l"(x + (size_t)b * K + k)
+                   : "memory");
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
   }
-  __syncthreads();
+  csync_bulk();
 
   float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
   for (int item = 0; item < nitems; ++item) {
-    if (item + 1 < nitems) load_item(item + 1, nxt);
+    const int slot = item % nslots;
     const int tile = blockIdx.x + (item / npass) * gridDim.x, pass = item % npass;
+    bool ok = !*reinterpret_cast<volatile int*>(&sh->abort);
+    if (ok && !mbar_wait(&sh->full[slot], (uint32_t)((item / nslots) & 1), status, wait_limit)) {
+      sh->abort = 1;
+      ok = false;
+    }
+    if (ok) {
+      const uint8_t* sb = slots + (size_t)slot * kBulkSlotBytes;
 #pragma unroll
-    for (int i = 0; i < kTcChunks; ++i) {
-      const int c = pass * (kTcWarps * kTcChunks) + warp * kTcChunks + i;
-      if (c < nchunks) {
-        uint4 xv[NT];
+      for (int i = 0; i < 4; ++i) {
+        const int cl = warp * 4 + i;  // chunk within the pass
+        const int c = pass * 32 + cl;
+        if (c < nchunks) {
+          const uint4 wa = *reinterpret_cast<const uint4*>(sb + g * kBulkRowBytes + cl * 64 + t4 * 16);
+          const uint4 wb = *reinterpret_cast<const uint4*>(sb + (g + 8) * kBulkRowBytes + cl * 64 + t4 * 16);
+          uint4 xv[NT];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-          xv[nt] = *reinterpret_cast<const uint4*>(xs + (size_t)(nt * 8 + g) * KP + c * 32 + 8 * t4);
-        const uint4 wa = cur[2 * i], wb = cur[2 * i + 1];
+          for (int nt = 0; nt < NT; ++nt)
+            xv[nt] = *reinterpret_cast<const uint4*>(xs + (size_t)(nt * 8 + g) * KP + c * 32 + 8 * t4);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          mma_bf16_16816(acc[nt], wa.x, wb.x, wa.y, wb.y, xv[nt].x, xv[nt].y);
-          mma_bf16_16816(acc[nt], wa.z, wb.z, wa.w, wb.w, xv[nt].z, xv[nt].w);
+          for (int nt = 0; nt < NT; ++nt) {
+            mma_bf16_16816(acc[nt], wa.x, wb.x, wa.y, wb.y, xv[nt].x, xv[nt].y);
+            mma_bf16_16816(acc[nt], wa.z, wb.z, wa.w, wb.w, xv[nt].z, xv[nt].w);
+          }
         }
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sh->empty[slot]);
     if (pass == npass - 1) {
-      // partial tiles of the 8 warps meet in shared memory
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         float* pr = red + (size_t)warp * 256;
@@ -526,7 +586,7 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) gemv_tc_kernel(GemvIn in, Ep
             make_float2(acc[nt][2], acc[nt][3]);
         acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
       }
-      __syncthreads();
+      csync_bulk();
       {
         const int r = tid >> 4, col = tid & 15;
         float s = 0.f;
@@ -534,11 +594,11 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) gemv_tc_kernel(GemvIn in, Ep
         for (int w = 0; w < kTcWarps; ++w) s += red[w * 256 + r * 16 + col];
         tile_out[r * 17 + col] = s;
       }
-      __syncthreads();
+      csync_bulk();
       {
         const int j = tid >> 5, row = (tid >> 4) & 1, b = tid & 15;
         const int u = tile * 8 + j;
-        if (u < nunits && b < batch) {
+        if (u < nunits && b < batch && !*reinterpret_cast<volatile int*>(&sh->abort)) {
           const __nv_bfloat16 *a, *bb;
           const bool has1 = epi.rows(u, a, bb);
           epi.store(u, b, row, tile_out[(2 * j + row) * 17 + b], tile_out[(2 * j + 1 - row) * 17 + b],
@@ -546,27 +606,29 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) gemv_tc_kernel(GemvIn in, Ep
         }
       }
     }
-#pragma unroll
-    for (int i = 0; i < 2 * kTcChunks; ++i) cur[i] = nxt[i];
   }
 }
 
 template <int NT, class Epi>
-int launch_gemv_tc(const GemvIn& in, const Epi& epi, int nunits, cudaStream_t st) {
-  const size_t smem = tc_smem_bytes(NT, in.K);
+int launch_gemv_bulk(const GemvIn& in, const Epi& epi, int nunits, int* status, cudaStream_t st) {
+  constexpr size_t kMaxSmem = 227 * 1024;
+  const size_t fixed = bulk_fixed_bytes(NT, in.K);
+  const int nslots = (int)std::min<size_t>(kBulkMaxSlots, (kMaxSmem - fixed) / kBulkSlotBytes);
+  if (nslots < 2) return set_error(DH_ERR_SHAPE, "gemv: K=%d leaves no room for the weight ring", in.K);
+  const size_t smem = fixed + (size_t)nslots * kBulkSlotBytes;
   static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_dev != dev) {
-    cudaFuncSetAttribute(gemv_tc_kernel<NT, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)tc_smem_bytes(2, 5632));
+    cudaFuncSetAttribute(gemv_bulk_kernel<NT, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kMaxSmem);
     configured_dev = dev;
   }
   const int ntiles = (nunits + 7) / 8;
-  const int per_sm = smem <= 110 * 1024 ? 2 : 1;
-  const int grid = std::min(ntiles, sm_count() * per_sm);
-  return launch_pdl(gemv_tc_kernel<NT, Epi>, dim3(grid), dim3(kTcWarps * 32), smem, st, in, epi)
-             ? set_error(DH_ERR_CUDA, "gemv_tc_kernel launch: %s", cudaGetErrorString(cudaGetLastError()))
+  const int grid = std::min(ntiles, sm_count());
+  return launch_pdl(gemv_bulk_kernel<NT, Epi>, dim3(grid), dim3(kBulkThreads), smem, st, in, epi, nslots,
+                    status, wait_limit())
+             ? set_error(DH_ERR_CUDA, "gemv_bulk_kernel launch: %s", cudaGetErrorString(cudaGetLastError()))
              : DH_OK;
 }
 
@@ -599,12 +661,12 @@ int launch_gemv(GemvIn in, const Epi& epi, int nunits, cudaStream_t st) {
     return set_error(DH_ERR_SHAPE, "gemv: batch chunk %d outside [1, 16]", in.batch);
   if ((size_t)in.batch * in.K * 2 > (size_t)kMaxRows * 2816 * 2 + 8192)
     return set_error(DH_ERR_SHAPE, "gemv: batch*K too large for shared memory");
+  if (in.K % 32 == 0 && aligned16(in.x)) {  // tensor cores, weights through the copy engine
+    if (in.batch <= 8) return launch_gemv_bulk<1>(in, epi, nunits, in.status, st);
+    return launch_gemv_bulk<2>(in, epi, nunits, in.status, st);
+  }
   if (in.batch == 1) return launch_gemv_b<1>(in, epi, nunits, st);
   if (in.batch == 2) return launch_gemv_b<2>(in, epi, nunits, st);
-  if (in.K % 32 == 0 && aligned16(in.x)) {  // tensor cores from three rows on
-    if (in.batch <= 8) return launch_gemv_tc<1>(in, epi, nunits, st);
-    return launch_gemv_tc<2>(in, epi, nunits, st);
-  }
   if (in.batch <= 4) return launch_gemv_b<4>(in, epi, nunits, st);
   if (in.batch <= 8) return launch_gemv_b<8>(in, epi, nunits, st);
   return launch_gemv_b<16>(in, epi, nunits, st);
@@ -917,6 +979,7 @@ __global__ void __launch_bounds__(64) tree_recur_kernel(TreeRecurParams p) {
     if (s >= 0) rg_src = bf2f(p.rg[(((size_t)b * p.max_len + s) * L + c) * H + h]);
   }
   pdl_wait();
+  const __nv_bfloat16 v0 = c < hd ? p.v0[(size_t)b * d + h * hd + c] : __float2bfloat16(0.f);
   if (c < L) {
     const int l = c;
     const long long s = t - (1ll << l);
@@ -938,7 +1001,6 @@ __global__ void __launch_bounds__(64) tree_recur_kernel(TreeRecurParams p) {
   }
   __syncthreads();
   if (c >= hd) return;
-  const __nv_bfloat16 v0 = p.v0[(size_t)b * d + h * hd + c];
   float V = bf2f(v0);
   ringb[(size_t)(t & 1) * d] = v0;  // ring 0 at t
 #pragma unroll
@@ -979,7 +1041,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
   extern __shared__ float sc[];  // [chunk_cap]
   __shared__ float sq[HD];
   __shared__ float sred[4];
-  __shared__ float sacc[4][HD];
+  __shared__ float sacc[16][HD];
   __shared__ int s_last;
   const int h = blockIdx.x, b = blockIdx.y, split = blockIdx.z, nsplit = gridDim.z;
   const int tid = threadIdx.x;
@@ -1005,20 +1067,37 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
   __syncthreads();
   const float scale = rsqrtf((float)HD);
 
+  // scores: a thread takes positions tid, tid + 128, ..., two key rows
+  // (16 loads of 16 bytes) in flight per round
   float mloc = -INFINITY;
-  for (int i = tid; i < cnt; i += 128) {
-    const __nv_bfloat16* kr = p.k + ((size_t)b * p.max_len + s0 + i) * d + h * HD;
-    float s = 0.f;
+  for (int i0 = tid; i0 < cnt; i0 += 256) {
+    uint4 kv[2][HD / 8];
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j) {
-      float f[8];
-      unpack8(reinterpret_cast<const uint4*>(kr)[j], f);
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + 128 * u;
+      if (i < cnt) {
+        const uint4* kr = reinterpret_cast<const uint4*>(p.k + ((size_t)b * p.max_len + s0 + i) * d + h * HD);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) s = fmaf(f[e], sq[j * 8 + e], s);
+        for (int j = 0; j < HD / 8; ++j) kv[u][j] = kr[j];
+      }
     }
-    s *= scale;
-    sc[i] = s;
-    mloc = fmaxf(mloc, s);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + 128 * u;
+      if (i < cnt) {
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < HD / 8; ++j) {
+          float f[8];
+          unpack8(kv[u][j], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) s = fmaf(f[e], sq[j * 8 + e], s);
+        }
+        s *= scale;
+        sc[i] = s;
+        mloc = fmaxf(mloc, s);
+      }
+    }
   }
   const float M = block_reduce_128(mloc, sred, true);
   float lsum = 0.f;
@@ -1028,27 +1107,46 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
     lsum += e;
   }
   const float Lsum = block_reduce_128(lsum, sred, false);  // includes a barrier after sc writes
-  const int c2 = (tid & 31) * 2, prow = tid >> 5;
-  float a0 = 0.f, a1 = 0.f;
-  for (int i = prow; i < cnt; i += 4) {
-    const __nv_bfloat162 vv = *reinterpret_cast<const __nv_bfloat162*>(
-        p.v + ((size_t)b * p.max_len + s0 + i) * d + h * HD + c2);
-    const float2 f = __bfloat1622float2(vv);
-    a0 = fmaf(sc[i], f.x, a0);
-    a1 = fmaf(sc[i], f.y, a1);
-  }
-  sacc[prow][c2] = a0;
-  sacc[prow][c2 + 1] = a1;
-  __syncthreads();
-  if (nsplit == 1) {
-    if (tid < HD) {
-      const float o = sacc[0][tid] + sacc[1][tid] + sacc[2][tid] + sacc[3][tid];
-      p.y[(size_t)b * d + h * HD + tid] = f2bf(cnt > 0 ? o / Lsum : 0.f);
+  // values: thread (row group r, channel group cg) accumulates channels
+  // [8 cg, +8) over positions r, r + 16, ...; four 16-byte rows in flight
+  const int cg = tid & 7, r0 = tid >> 3;
+  float acc8[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc8[e] = 0.f;
+  for (int i0 = r0; i0 < cnt; i0 += 64) {
+    uint4 vv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + 16 * u;
+      if (i < cnt)
+        vv[u] = *reinterpret_cast<const uint4*>(p.v + ((size_t)b * p.max_len + s0 + i) * d + h * HD + cg * 8);
     }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + 16 * u;
+      if (i < cnt) {
+        float f[8];
+        unpack8(vv[u], f);
+        const float w = sc[i];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc8[e] = fmaf(w, f[e], acc8[e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) sacc[r0][cg * 8 + e] = acc8[e];
+  __syncthreads();
+  float o = 0.f;
+  if (tid < HD) {
+#pragma unroll
+    for (int r = 0; r < 16; ++r) o += sacc[r][tid];
+  }
+  if (nsplit == 1) {
+    if (tid < HD) p.y[(size_t)b * d + h * HD + tid] = f2bf(cnt > 0 ? o / Lsum : 0.f);
     return;
   }
   float* mine = p.part + (((size_t)b * H + h) * nsplit + split) * (HD + 2);
-  if (tid < HD) mine[2 + tid] = sacc[0][tid] + sacc[1][tid] + sacc[2][tid] + sacc[3][tid];
+  if (tid < HD) mine[2 + tid] = o;
   if (tid == 0) {
     mine[0] = cnt > 0 ? M : -INFINITY;
     mine[1] = cnt > 0 ? Lsum : 0.f;
@@ -1342,13 +1440,13 @@ extern "C" int dh_decode_embed(const int64_t* tokens, const void* emb, float* x,
 
 extern "C" int dh_decode_mixer_in(const float* x, const void* norm_w, const void* w3, void* v0,
                                   void* a_out, void* b_hist, const int64_t* t_buf, int max_len,
-                                  int batch, int d, void* stream) {
+                                  int batch, int d, int* status, void* stream) {
   DH_REQUIRE(x && norm_w && w3 && v0 && a_out && b_hist && t_buf, DH_ERR_ARG,
              "dh_decode_mixer_in: null pointer");
   DH_REQUIRE(d % 8 == 0 && max_len > 0, DH_ERR_SHAPE, "dh_decode_mixer_in: bad sizes");
   for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
     const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
-    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb};
+    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb, status};
     EpiMixerIn e{BF(w3), d, d, max_len, BFM(v0) + (size_t)b0 * d, BFM(a_out) + (size_t)b0 * d,
                  BFM(b_hist) + (size_t)b0 * max_len * d, t_buf};
     int rc = launch_gemv(in, e, 3 * d / 2, STREAM(stream));
@@ -1430,15 +1528,15 @@ extern "C" int dh_decode_tree_step_tc(const void* a_in, const void* b_hist, cons
 }
 
 extern "C" int dh_decode_linear_residual(const void* y, const void* w, float* x, float* x_copy,
-                                         int batch, int k, int d_out, void* stream) {
+                                         int batch, int k, int d_out, int* status, void* stream) {
   DH_REQUIRE(y && w && x, DH_ERR_ARG, "dh_decode_linear_residual: null pointer");
   DH_REQUIRE(d_out % 2 == 0, DH_ERR_SHAPE, "dh_decode_linear_residual: odd output width");
   for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
     const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
-    GemvIn in{BF(y) + (size_t)b0 * k, 0, nullptr, k, nb};
+    GemvIn in{BF(y) + (size_t)b0 * k, 0, nullptr, k, nb, status};
     EpiResidual e{BF(w), d_out, k, x + (size_t)b0 * d_out,
                   x_copy ? x_copy + (size_t)b0 * d_out : nullptr};
-    int rc = launch_gemv(in, e, d_out / 2, STREAM(stream));
+    const int rc = launch_gemv(in, e, d_out / 2, STREAM(stream));
     if (rc) return rc;
   }
   return DH_OK;
@@ -1488,11 +1586,11 @@ extern "C" int dh_decode_ffn(const float* x_in, const void* norm_w, const void* 
 
 extern "C" int dh_decode_ffn_in(const float* x, const void* norm_w, const void* w_gate,
                                 const void* w_up, void* u, int batch, int d, int ff,
-                                void* stream) {
+                                int* status, void* stream) {
   DH_REQUIRE(x && norm_w && w_gate && w_up && u, DH_ERR_ARG, "dh_decode_ffn_in: null pointer");
   for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
     const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
-    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb};
+    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb, status};
     EpiSwiglu e{BF(w_gate), BF(w_up), ff, d, BFM(u) + (size_t)b0 * ff};
     int rc = launch_gemv(in, e, ff, STREAM(stream));
     if (rc) return rc;
@@ -1503,13 +1601,13 @@ extern "C" int dh_decode_ffn_in(const float* x, const void* norm_w, const void* 
 extern "C" int dh_decode_attn_in(const float* x, const void* norm_w, const void* wqkv,
                                  const float* rope_cos, const float* rope_sin, void* q,
                                  void* k_cache, void* v_cache, const int64_t* t_buf, int max_len,
-                                 int batch, int d, int H, void* stream) {
+                                 int batch, int d, int H, int* status, void* stream) {
   DH_REQUIRE(x && norm_w && wqkv && rope_cos && rope_sin && q && k_cache && v_cache && t_buf,
              DH_ERR_ARG, "dh_decode_attn_in: null pointer");
   DH_REQUIRE(H > 0 && d % H == 0 && (d / H) % 2 == 0, DH_ERR_SHAPE, "dh_decode_attn_in: bad heads");
   for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
     const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
-    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb};
+    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb, status};
     EpiQkvRope e{BF(wqkv), d, d, d / H, max_len, rope_cos, rope_sin,
                  BFM(q) + (size_t)b0 * d, BFM(k_cache) + (size_t)b0 * max_len * d,
                  BFM(v_cache) + (size_t)b0 * max_len * d, t_buf};
@@ -1553,11 +1651,11 @@ extern "C" int dh_decode_attn(const void* q, const void* k_cache, const void* v_
 }
 
 extern "C" int dh_decode_logits(const float* x, const void* norm_w, const void* emb, void* logits,
-                                int batch, int d, int vocab, void* stream) {
+                                int batch, int d, int vocab, int* status, void* stream) {
   DH_REQUIRE(x && norm_w && emb && logits, DH_ERR_ARG, "dh_decode_logits: null pointer");
   for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
     const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
-    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb};
+    GemvIn in{x + (size_t)b0 * d, 1, BF(norm_w), d, nb, status};
     EpiLogits e{BF(emb), vocab, d, BFM(logits) + (size_t)b0 * vocab};
     int rc = launch_gemv(in, e, (vocab + 1) / 2, STREAM(stream));
     if (rc) return rc;

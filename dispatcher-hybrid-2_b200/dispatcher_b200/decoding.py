@@ -226,7 +226,8 @@ class FusedGraphedHybridDecoder:
         for lay, cache in zip(W.layers, self.caches):
             if lay["kind"] == "tree":
                 call("dh_decode_mixer_in", P(self.x), P(lay["norm1"]), P(lay["w3"]), P(self.v0),
-                     P(self.a), P(cache.B_hist), P(self.t_buf), self.max_len, B, d, s)
+                     P(self.a), P(cache.B_hist), P(self.t_buf), self.max_len, B, d,
+                     P(self.status), s)
                 if self.tree_tc:
                     call("dh_decode_tree_step_tc", P(self.a), P(cache.B_hist),
                          P(lay["w_gates_np"]), lay["gates_np"], P(lay["bi"]), P(lay["bf"]),
@@ -242,24 +243,24 @@ class FusedGraphedHybridDecoder:
             else:
                 call("dh_decode_attn_in", P(self.x), P(lay["norm1"]), P(lay["wqkv"]),
                      P(cache.rope_cos), P(cache.rope_sin), P(self.q), P(cache.k), P(cache.v),
-                     P(self.t_buf), self.max_len, B, d, H, s)
+                     P(self.t_buf), self.max_len, B, d, H, P(self.status), s)
                 call("dh_decode_attn", P(self.q), P(cache.k), P(cache.v), P(self.y),
                      P(self.t_buf), P(self.part), P(attn_ctr), self.nsplit, B, self.max_len,
                      H, hd, cfg.attn_window, s)
-            # output projection + residual (also leaves a copy of x for the FFN),
-            # then the whole FFN with its residual in one launch
+            # output projection + residual (for the fused FFN it also leaves a
+            # copy of x, which that kernel reads while it adds into x), then the FFN
             call("dh_decode_linear_residual", P(self.y), P(lay["w_out"]), P(self.x),
-                 P(self.x_copy), B, d, d, s)
+                 P(self.x_copy) if self.ffn_fused else None, B, d, d, P(self.status), s)
             if self.ffn_fused:
                 call("dh_decode_ffn", P(self.x_copy), P(lay["norm2"]), P(lay["w_gate"]),
                      P(lay["w_up"]), P(lay["w_downT"]), P(self.x), B, d, ff, s)
             else:
-                call("dh_decode_ffn_in", P(self.x_copy), P(lay["norm2"]), P(lay["w_gate"]),
-                     P(lay["w_up"]), P(self.u), B, d, ff, s)
+                call("dh_decode_ffn_in", P(self.x), P(lay["norm2"]), P(lay["w_gate"]),
+                     P(lay["w_up"]), P(self.u), B, d, ff, P(self.status), s)
                 call("dh_decode_linear_residual", P(self.u), P(lay["w_down"]), P(self.x),
-                     None, B, ff, d, s)
+                     None, B, ff, d, P(self.status), s)
         call("dh_decode_logits", P(self.x), P(W.norm_out), P(W.lm_head), P(self.logits_out),
-             B, d, V, s)
+             B, d, V, P(self.status), s)
         call("dh_decode_advance", P(self.t_buf), s)
 
     def _capture(self):

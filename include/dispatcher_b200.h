@@ -68,10 +68,15 @@ DH_API int dh_decode_embed(const int64_t* tokens, const void* emb, float* x, int
 
 /* Tree block, mixer input side (decoding.py:473-476): h = RMSNorm(x; norm_w);
  * [v0 | A | B] = h . W3^T with W3 = [W_in; W1x; W1s] (3d x d, bf16);
- * v0, A -> bf16 (batch, d); B -> B_hist[:, t, :]. */
+ * v0, A -> bf16 (batch, d); B -> B_hist[:, t, :].
+ * This and the other GEMV entry points below (linear_residual, ffn_in,
+ * attn_in, logits) run on the tensor cores with the weights streamed by
+ * bulk copies whenever K is a multiple of 32 and the input is 16-byte
+ * aligned; *status (nullable) receives DH_ERR_TIMEOUT if one of their
+ * bounded pipeline waits gives up. */
 DH_API int dh_decode_mixer_in(const float* x, const void* norm_w, const void* w3, void* v0,
                        void* a_out, void* b_hist, const int64_t* t_buf, int max_len, int batch,
-                       int d, void* stream);
+                       int d, int* status, void* stream);
 
 /* Tree block, gate readout + level recurrence for one position; replaces
  * step_gates_kernel + step_scan_kernel (fused_step.py:26-88, launched at
@@ -111,7 +116,7 @@ DH_API int dh_decode_tree_step_tc(const void* a_in, const void* b_hist, const vo
  * linear_down with the residual add (decoding.py:487-488, 434-435).  x_copy
  * (nullable) receives a copy of the updated x (the input of dh_decode_ffn). */
 DH_API int dh_decode_linear_residual(const void* y, const void* w, float* x, float* x_copy,
-                              int batch, int k, int d_out, void* stream);
+                              int batch, int k, int d_out, int* status, void* stream);
 
 /* Whole SwiGLU feed-forward with the residual add, one launch
  * (modeling_dispatcher.py:196-197, decoding.py:434-435, 488):
@@ -125,7 +130,7 @@ DH_API int dh_decode_ffn(const float* x_in, const void* norm_w, const void* w_ga
 /* FFN input side: h = RMSNorm(x; norm_w); u = silu(h . Wg^T) * (h . Wu^T),
  * bf16 (batch, ff) (modeling_dispatcher.py:196-197). */
 DH_API int dh_decode_ffn_in(const float* x, const void* norm_w, const void* w_gate, const void* w_up,
-                     void* u, int batch, int d, int ff, void* stream);
+                     void* u, int batch, int d, int ff, int* status, void* stream);
 
 /* Attention block input side (decoding.py:414-426): h = RMSNorm(x);
  * q,k,v = h . [Wq;Wk;Wv]^T; RoPE at position t on q and k (pairs 2j,2j+1,
@@ -133,7 +138,8 @@ DH_API int dh_decode_ffn_in(const float* x, const void* norm_w, const void* w_ga
  * k, v -> k_cache / v_cache at t. */
 DH_API int dh_decode_attn_in(const float* x, const void* norm_w, const void* wqkv, const float* rope_cos,
                       const float* rope_sin, void* q, void* k_cache, void* v_cache,
-                      const int64_t* t_buf, int max_len, int batch, int d, int H, void* stream);
+                      const int64_t* t_buf, int max_len, int batch, int d, int H, int* status,
+                      void* stream);
 
 /* Sliding-window attention of q at position t over cache positions
  * (t - window, t] (all of [0, t] when window <= 0); softmax in fp32, scale
@@ -159,7 +165,7 @@ DH_API int dh_decode_attn_noalloc(const void* q, const void* k_cache, const void
 
 /* logits = RMSNorm(x; norm_w) . E^T, bf16 (batch, vocab) (decoding.py:442). */
 DH_API int dh_decode_logits(const float* x, const void* norm_w, const void* emb, void* logits,
-                     int batch, int d, int vocab, void* stream);
+                     int batch, int d, int vocab, int* status, void* stream);
 
 /* Document tracking for multi-document decoding (no counterpart in the
  * reference decoder, which refuses separators in the prompt): doc_hist[b, t]
