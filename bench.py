@@ -221,32 +221,43 @@ def run_prefill_e2e(model, ids_host, steps, warmup):
     return ids_host.numel() / dt, ids_pin.numel() * 8, out_pin.numel() * 2
 
 
-def run_decode(model, cfg, batch, ctx, steps, warmup, seed, world):
-    """Device-timed lockstep greedy decode steps after a `ctx`-token prefill;
-    with N > 1 the sampled tokens of every rank are all-gathered each step."""
-    from dispatcher_b200 import FusedGraphedHybridDecoder, sharding
+def run_decode(model, cfg, batch, ctx, steps, warmup, seed, world, select=None,
+               gather_logits=False):
+    """Device-timed lockstep decode after a `ctx`-token prefill.  Each step
+    is one CUDA graph replay (FusedGraphedHybridDecoder.lockstep_loop): the
+    step's kernels, the token choice on the device (greedy unless `select`
+    is given) fed back as the next input, and with N > 1 the NCCL all-gather
+    of every rank's tokens.  `steps` counts timed steps after `warmup`
+    untimed ones (both within max_len); gather_logits adds one all-gather of
+    the last step's logits of every rank after the timed steps, inside the
+    timed region."""
+    from dispatcher_b200 import FusedGraphedHybridDecoder
+    from dispatcher_b200.generation import select_greedy
+    torch.cuda.manual_seed(seed)
     ids = prompt_ids(1, ctx, seed, cfg.vocab_size, cfg.eot_token).expand(batch, ctx).contiguous().cuda()
     dec = FusedGraphedHybridDecoder(model)
-    nxt = dec.prefill(ids)[:, -1].argmax(-1)
+    dec.prefill(ids)
+    loop = dec.lockstep_loop(select or select_greedy)
+    warmup = max(0, min(warmup, cfg.max_len - ctx - 1))
     steps = max(1, min(steps, cfg.max_len - ctx - warmup))
-    def one(tok):
-        out = dec.step(tok).argmax(-1)
-        if world > 1:
-            sharding.gather_rows(out, batch * world)   # every rank sees every row's token
-        return out
     for _ in range(warmup):
-        nxt = one(nxt)
+        loop.step()
+    all_logits = (torch.empty(world * batch, cfg.vocab_size, device="cuda", dtype=torch.bfloat16)
+                  if gather_logits and world > 1 else None)
     torch.cuda.synchronize()
     barrier(world)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(steps):
-        nxt = one(nxt)
+        loop.step()
+    if all_logits is not None:
+        torch.distributed.all_gather_into_tensor(all_logits, dec.logits_out)
     e.record()
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(s.elapsed_time(e), world) / steps
     dec.check_status(sync=True)
+    loop.release()
     return ms, steps, dec.persistent
 
 
@@ -426,7 +437,6 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--decode-steps", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", choices=["prefill", "decode", "gate_bwd"],
                     help="run a small fixed workload for a profiler and exit (no JSON line)")
@@ -474,14 +484,29 @@ def main():
     e2e_v, h2d, d2h = run_prefill_e2e(model, ids_host, args.steps, 2)
     e2e_v = -max_over_ranks(-e2e_v, world) * world
 
+    # configs[2] (b1: greedy, 196 steps from a 3900 prefill), configs[3] (b16:
+    # 16 rows of one 3900 prompt, top-k 50 / T 0.8 sampling, 196 steps) and
+    # configs[4] (sharded: 16 rows per GPU, 128 greedy steps from a 3968
+    # prefill, tokens gathered every step, logits of the last step gathered)
+    from dispatcher_b200.generation import select_top_k
     dec_lines = {}
-    for name, batch, seed in (("b16", 16, 2), ("b1", 1, 1)):
-        dms, dsteps, persistent = run_decode(model, cfg, batch, DECODE_CTX, args.decode_steps,
-                                             args.warmup, seed, world)
-        nbytes = decode_bytes_per_step(cfg, batch, DECODE_CTX)
+    legs = (("b16", 16, DECODE_CTX, 2, select_top_k(50, 0.8), False,
+             "configs[3]: 16 lockstep rows of one 3900-token prompt, top-k 50 / T 0.8 sampling "
+             "(Gumbel-max over the top-k, on the device), 196 steps (to the 4096 context)"),
+            ("b1", 1, DECODE_CTX, 1, None, False,
+             "configs[2]: batch 1, greedy, 196 steps from a 3900-token prompt"),
+            ("sharded", 16, 3968, 3, None, True,
+             "configs[4]: 16 rows per GPU, greedy, 128 steps from a 3968-token prompt, "
+             "tokens all-gathered every step and the last step's logits all-gathered"))
+    for name, batch, ctx, seed, sel, gath, what in legs:
+        n_steps = cfg.max_len - ctx - args.warmup
+        dms, dsteps, persistent = run_decode(model, cfg, batch, ctx, n_steps, args.warmup, seed,
+                                             world, select=sel, gather_logits=gath)
+        nbytes = decode_bytes_per_step(cfg, batch, ctx)
         dec_lines[name] = {
+            "workload": what,
             "value": world * batch * 1000.0 / dms, "unit": "tok/s", "ms_per_step": dms,
-            "steps": dsteps, "batch_per_gpu": batch, "ctx": DECODE_CTX,
+            "steps": dsteps, "warmup": args.warmup, "batch_per_gpu": batch, "ctx": ctx,
             "kernel": "persistent step kernel" if persistent else "per-op kernels in a CUDA graph",
             "roofline": {"bound": "hbm", "achieved": nbytes / (dms * 1e-3) / 1e9,
                          "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -491,7 +516,7 @@ def main():
     # batch-1 decode cost across context lengths (flatness)
     flat = {}
     for ctx in (256, 1024, 2048):
-        fms, _, _ = run_decode(model, cfg, 1, ctx, 32, args.warmup, 1, world)
+        fms, _, _ = run_decode(model, cfg, 1, ctx, 64, args.warmup, 1, world)
         flat[str(ctx)] = round(fms, 4)
     flat[str(DECODE_CTX)] = round(dec_lines["b1"]["ms_per_step"], 4)
     dec_lines["b1_ms_per_step_by_ctx"] = flat

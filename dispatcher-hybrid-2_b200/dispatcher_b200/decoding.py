@@ -335,6 +335,7 @@ class FusedGraphedHybridDecoder:
             self.last_tok.copy_(ids[:, T - 1])
         self.t = T
         self.t_buf.fill_(T)
+        self.logits_out.copy_(out[:, -1])   # the latest logits, as after a step
         self.status_word.arm()
         return out[0] if self._squeeze else out
 
@@ -374,6 +375,86 @@ class FusedGraphedHybridDecoder:
         out = self.logits_out.clone()
         self.status_word.arm()
         return out[0] if self._squeeze else out
+
+    def lockstep_loop(self, select, group=None):
+        """A CUDA graph of one whole lockstep step, token choice included:
+        the step's kernels, then `select(logits) -> (B,) int64` (device ops
+        only: argmax, top-k with Gumbel noise, ...), whose tokens become the
+        next step's input on the device, then (with a process group of more
+        than one rank) an NCCL all-gather of every rank's tokens, all in the
+        same graph.  Call after prefill(); run steps with .step().  The
+        reference's loop (modeling_dispatcher.py:421-442) takes the same
+        decisions on the host between graph replays."""
+        return _LockstepLoop(self, select, group)
+
+
+class _LockstepLoop:
+    def __init__(self, dec, select, group):
+        import torch.distributed as dist
+        if dec.graph is None:
+            raise RuntimeError("call prefill() before lockstep_loop()")
+        self.dec = dec
+        world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.world = world
+        B = dec.batch
+        self.tokens = torch.zeros(world * B, dtype=torch.long, device=dec.device)
+        # first token from the latest logits (the prefill's last position, or
+        # the last step's), outside the graph
+        first = select(dec.logits_out)
+        dec.token_buf.copy_(first)
+        # warm the selection and the collective up outside the capture
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            select(dec.logits_out.clone())
+            if world > 1:
+                dist.all_gather_into_tensor(self.tokens, dec.token_buf.clone(), group=group)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        self.graph = None
+        if isinstance(dec.graph, _DirectStep):
+            # a cooperative step the driver would not capture: issue it
+            # directly, selection and collective after it
+            self._eager = (select, group)
+            return
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            dec._record_step(torch.cuda.current_stream().cuda_stream)
+            tok = select(dec.logits_out)
+            dec.token_buf.copy_(tok)
+            if world > 1:
+                dist.all_gather_into_tensor(self.tokens, tok, group=group)
+            else:
+                self.tokens.copy_(tok)
+        self.graph = g
+
+    def step(self):
+        """One step: feeds the tokens chosen last (the prefill's for the
+        first call); afterwards .tokens holds this step's tokens of every
+        rank (rank-major) and the decoder's logits buffer this step's logits."""
+        dec = self.dec
+        if dec.t >= dec.max_len:
+            raise ValueError(f"context exhausted at max_len {dec.max_len}")
+        if self.graph is None:
+            import torch.distributed as dist
+            select, group = self._eager
+            dec._record_step(torch.cuda.current_stream().cuda_stream)
+            tok = select(dec.logits_out)
+            dec.token_buf.copy_(tok)
+            if self.world > 1:
+                dist.all_gather_into_tensor(self.tokens, tok, group=group)
+            else:
+                self.tokens.copy_(tok)
+        else:
+            self.graph.replay()
+        dec.t += 1
+        dec.status_word.arm()
+        return self.tokens
+
+    def release(self):
+        """Drop the graph (before destroying a process group it holds)."""
+        self.graph = None
+        self._eager = None
 
 
 # the reference's name for the graphed decoder without fused kernels maps to

@@ -27,6 +27,28 @@ def sampling_distribution(logits, temperature=1.0, top_k=None):
     return F.softmax(masked_logits(logits, temperature, top_k), dim=-1)
 
 
+def select_greedy(logits):
+    """Device-side token choice for lockstep_loop: argmax per row."""
+    return logits.argmax(-1)
+
+
+def select_top_k(top_k, temperature=1.0):
+    """Device-side sampling for lockstep_loop: a draw from softmax(top-k
+    logits / T) per row, taken as the Gumbel-max of the k candidates with
+    noise from torch's default CUDA generator (capturable in a CUDA graph,
+    each replay advancing the generator).  The same distribution as the
+    reference's multinomial over the masked softmax
+    (modeling_dispatcher.py:427-433); the draws themselves differ."""
+    inv_t = 1.0 / max(temperature, 1e-6)
+
+    def select(logits):
+        v, i = torch.topk(logits.float(), top_k, dim=-1)
+        u = torch.rand(v.shape, device=v.device).clamp_(min=1e-20)
+        z = v * inv_t - torch.log(-torch.log(u))
+        return i.gather(-1, z.argmax(-1, keepdim=True)).squeeze(-1)
+    return select
+
+
 DECODERS = {"fused": FusedGraphedHybridDecoder, "graphed": FusedGraphedHybridDecoder,
             "eager": FusedGraphedHybridDecoder, "b200": FusedGraphedHybridDecoder}
 

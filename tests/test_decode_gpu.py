@@ -265,3 +265,35 @@ def test_batch_above_16_uses_chunked_kernels(small_nd):
                            torch.cat([ids, nxt[:, None]], 1))[:, -1].float()
     assert max_err(got, ref) < bf16_bound(ref, ref16)
     assert out.shape == (18, 30, cfg.vocab_size)
+
+
+def test_lockstep_loop_matches_stepwise_greedy(small_nd):
+    """The captured loop (step kernels + device argmax fed back + token
+    gather, one graph per step) picks the same tokens as step() + argmax."""
+    from dispatcher_b200.generation import select_greedy, select_top_k
+    cfg, model, _ = small_nd
+    g = torch.Generator().manual_seed(11)
+    ids = torch.randint(0, cfg.vocab_size - 1, (3, 40), generator=g).cuda()
+    dec = FusedGraphedHybridDecoder(model)
+    tok = dec.prefill(ids)[:, -1].argmax(-1)
+    want = [tok]
+    for _ in range(10):
+        tok = dec.step(tok).argmax(-1)
+        want.append(tok)
+    dec2 = FusedGraphedHybridDecoder(model)
+    dec2.prefill(ids)
+    loop = dec2.lockstep_loop(select_greedy)
+    got = [dec2.token_buf.clone()]
+    for _ in range(10):
+        got.append(loop.step().clone())
+    assert dec2.t == dec.t
+    assert torch.equal(torch.stack(got), torch.stack(want))
+    assert torch.equal(dec2.logits_out, dec.logits_out)
+    # sampled choices stay inside each row's top-k set
+    dec3 = FusedGraphedHybridDecoder(model)
+    dec3.prefill(ids)
+    loop = dec3.lockstep_loop(select_top_k(5, 0.8))
+    for _ in range(6):
+        loop.step()
+        top5 = torch.topk(dec3.logits_out.float(), 5, dim=-1).indices
+        assert bool((top5 == dec3.token_buf[:, None]).any(-1).all())
