@@ -4,9 +4,11 @@
 first poll.  Each kernel must then return (never hang), issue no further
 copies or MMAs, leave DH_ERR_TIMEOUT in its status word, and leave the
 context usable: the next call with the default limit is correct.  With the
-limit at 0 nothing asynchronous is ever issued (the producers give up before
-their first copy, the MMA warps are released only by a successful wait), so
-these launches read and write only their own buffers.
+limit at 0 the GEMM and gate producers give up before their first copy and
+the MMA warps are released only by a successful wait; the decode GEMVs'
+producer issues its first ring of bulk copies before any wait and drains
+them (with a fixed bound) before the kernel returns.  So these launches read
+and write only their own buffers and leave nothing in flight.
 """
 
 import pytest
@@ -88,3 +90,32 @@ def test_prefill_raises_on_timeout_and_recovers():
     again = model(ids).logits
     model._engine.check_status(sync=True)
     assert torch.equal(again, good)
+
+
+def test_decode_gemv_gives_up_then_recovers():
+    """The lockstep decode's tensor-core GEMVs (bulk-copy weight ring): a
+    step graph captured with the limit at 0 reports DH_ERR_TIMEOUT through
+    the decoder's status word; a decoder captured with the default limit
+    then gives the same logits as one that never saw a timeout."""
+    from dispatcher_b200 import FusedGraphedHybridDecoder
+    cfg = small_config()
+    model = DispatcherHybridForCausalLM(cfg, seed=1, nondegenerate=True).to("cuda", torch.bfloat16)
+    ids = torch.randint(0, cfg.vocab_size - 1, (4, 40), generator=torch.Generator().manual_seed(2))
+    ids = ids.cuda()
+    ref = FusedGraphedHybridDecoder(model)
+    ref.prefill(ids)
+    want = ref.step(ids[:, -1])
+    ref.check_status(sync=True)
+    bad = FusedGraphedHybridDecoder(model)
+    bad.prefill(ids)
+    bad.check_status(sync=True)
+    with wait_limit(0):
+        bad._capture()          # the step graph bakes in the limit of its launches
+    bad.step(ids[:, -1])
+    with pytest.raises(DispatcherB200Error, match="DH_ERR_TIMEOUT"):
+        bad.check_status(sync=True)
+    good = FusedGraphedHybridDecoder(model)
+    good.prefill(ids)
+    got = good.step(ids[:, -1])
+    good.check_status(sync=True)
+    assert (got.float() - want.float()).abs().max().item() < 1e-2
