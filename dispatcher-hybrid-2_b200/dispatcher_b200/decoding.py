@@ -435,6 +435,7 @@ class _LockstepLoop:
         dec = self.dec
         if dec.t >= dec.max_len:
             raise ValueError(f"context exhausted at max_len {dec.max_len}")
+        dec.check_status()
         if self.graph is None:
             import torch.distributed as dist
             select, group = self._eager
