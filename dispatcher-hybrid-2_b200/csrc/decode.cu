@@ -858,7 +858,8 @@ struct TreeGatesTcParams {
   const int64_t* t_buf;
   const int* doc;  // nullable
   float* pre;      // (batch, L, NP) fp32, zero on entry
-  int batch, max_len, L, NP, gh;
+  const __nv_bfloat16* ring;  // V_ring (batch, S, d): the recurrence's history, prefetched here
+  int batch, max_len, L, NP, gh, S, d;
 };
 
 template <int MT>
@@ -881,6 +882,18 @@ __global__ void __launch_bounds__(256) tree_gates_tc_kernel(TreeGatesTcParams p)
     const size_t r = (size_t)l * NP + mt * 16 + g;
     wa[mt] = live ? ld_stream16(p.w + r * gh + k0) : make_uint4(0, 0, 0, 0);
     wb[mt] = live ? ld_stream16(p.w + (r + 8) * gh + k0) : make_uint4(0, 0, 0, 0);
+  }
+  // rows written by earlier steps that this level needs, into L2 while the
+  // predecessor runs: each lockstep row's B_hist row at t - 2^l (read below)
+  // and its ring slot of level l at t - 2^l (read by the recurrence kernel)
+  if (blockIdx.y == 0 && src >= 0 && tid < 2 * p.batch) {
+    const int b = tid >> 1;
+    if (tid & 1) {
+      const long long slot = ((2ll << l) - 2) + (src & ((2ll << l) - 1));
+      prefetch_l2(p.ring + ((size_t)b * p.S + slot) * p.d, (uint32_t)p.d * 2);
+    } else {
+      prefetch_l2(p.bh + ((size_t)b * p.max_len + src) * gh, (uint32_t)gh * 2);
+    }
   }
   pdl_wait();
   if (tid < 16) {
@@ -1511,7 +1524,8 @@ extern "C" int dh_decode_tree_step_tc(const void* a_in, const void* b_hist, cons
     const int* doc = doc_hist ? doc_hist + (size_t)b0 * max_len : nullptr;
     float* pr = pre + (size_t)b0 * L * np;
     TreeGatesTcParams gp{BF(a_in) + (size_t)b0 * gh, BF(b_hist) + (size_t)b0 * max_len * gh,
-                         BF(w_gates), t_buf, doc, pr, nb, max_len, L, np, gh};
+                         BF(w_gates), t_buf, doc, pr, BF(v_ring) + (size_t)b0 * S * d, nb,
+                         max_len, L, np, gh, S, d};
     const dim3 gg(L, (gh + 255) / 256);
     const int bad = np <= 16   ? launch_pdl(tree_gates_tc_kernel<1>, gg, dim3(256), 0, STREAM(stream), gp)
                     : np <= 32 ? launch_pdl(tree_gates_tc_kernel<2>, gg, dim3(256), 0, STREAM(stream), gp)
