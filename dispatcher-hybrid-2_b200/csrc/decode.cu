@@ -69,12 +69,17 @@ struct GemvIn {
 
 // ---- epilogues: rows(u) names the two weight rows of work unit u;
 //      store() receives, in each lane, the dot product of row `row` of unit u
-//      with batch row b, and the partner row's value for the same b.
+//      with batch row b, and the partner row's value for the same b; bind()
+//      runs once per thread at kernel start and reads what store() needs
+//      from the device (the position t, stable within a step) off the
+//      epilogue's critical path.
 struct EpiMixerIn {  // W3 = [W_in; W1x; W1s], adjacent row pairs
   const __nv_bfloat16* w;
   int d, K, max_len;
   __nv_bfloat16 *v0, *a, *bh;
   const int64_t* t_buf;
+  long long t;
+  __device__ void bind() { t = *t_buf; }
   __device__ int units() const { return 3 * d / 2; }
   __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
     r0 = w + (size_t)(2 * u) * K;
@@ -85,7 +90,7 @@ struct EpiMixerIn {  // W3 = [W_in; W1x; W1s], adjacent row pairs
     const int n = 2 * u + row, seg = n / d, c = n % d;
     if (seg == 0) v0[(size_t)b * d + c] = f2bf(v);
     else if (seg == 1) a[(size_t)b * d + c] = f2bf(v);
-    else bh[((size_t)b * max_len + *t_buf) * d + c] = f2bf(v);
+    else bh[((size_t)b * max_len + t) * d + c] = f2bf(v);
   }
 };
 
@@ -94,6 +99,7 @@ struct EpiResidual {  // x[b, n] += v (and x_copy[b, n] = the new x when x_copy 
   int N, K;
   float* x;
   float* x_copy;
+  __device__ void bind() {}
   __device__ int units() const { return N / 2; }
   __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
     r0 = w + (size_t)(2 * u) * K;
@@ -112,6 +118,7 @@ struct EpiSwiglu {  // unit j = (gate row j, up row j) -> silu(g) * u
   const __nv_bfloat16 *wg, *wu;
   int ff, K;
   __nv_bfloat16* out;
+  __device__ void bind() {}
   __device__ int units() const { return ff; }
   __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
     r0 = wg + (size_t)u * K;
@@ -131,6 +138,8 @@ struct EpiQkvRope {  // [Wq; Wk; Wv], row pairs (2j, 2j+1) rotated for q and k
   const float *cosT, *sinT;
   __nv_bfloat16 *q, *kc, *vc;
   const int64_t* t_buf;
+  long long t;
+  __device__ void bind() { t = *t_buf; }
   __device__ int units() const { return 3 * d / 2; }
   __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
     r0 = w + (size_t)(2 * u) * K;
@@ -139,7 +148,6 @@ struct EpiQkvRope {  // [Wq; Wk; Wv], row pairs (2j, 2j+1) rotated for q and k
   }
   __device__ void store(int u, int b, int row, float v, float other, bool) const {
     const int n = 2 * u + row, seg = n / d, c = n % d;
-    const int64_t t = *t_buf;
     float out = v;
     if (seg < 2) {
       const int j = (c % hd) >> 1;
@@ -157,6 +165,7 @@ struct EpiLogits {  // rows of E, odd vocab handled by a half-empty last unit
   const __nv_bfloat16* w;
   int V, K;
   __nv_bfloat16* out;
+  __device__ void bind() {}
   __device__ int units() const { return (V + 1) / 2; }
   __device__ bool rows(int u, const __nv_bfloat16*& r0, const __nv_bfloat16*& r1) const {
     r0 = w + (size_t)(2 * u) * K;
@@ -171,8 +180,10 @@ struct EpiLogits {  // rows of E, odd vocab handled by a half-empty last unit
 };
 
 template <int MAXB, class Epi>
-__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvIn in, Epi epi) {
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvIn in, Epi epi_in) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  Epi epi = epi_in;
+  epi.bind();
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [batch][K]
   __shared__ float s_rstd[MAXB];
   pdl_trigger();
@@ -414,11 +425,13 @@ __device__ __forceinline__ void csync_bulk() { asm volatile("bar.sync 1, 256;" :
 
 template <int NT, class Epi>
 __global__ void __launch_bounds__(kBulkThreads, 1)
-    gemv_bulk_kernel(GemvIn in, Epi epi, int nslots, int* status, uint32_t wait_limit) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
+    gemv_bulk_kernel(GemvIn in, Epi epi_in, int nslots, int* status, uint32_t wait_limit) {
+  extern __shared__ __align__(128) unsigned char bulk_smem[];
+  Epi epi = epi_in;
+  epi.bind();
   const int K = in.K, batch = in.batch, KP = K + 32;
-  uint8_t* slots = smem_raw;                                                 // [nslots][16][2112]
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw + (size_t)nslots * kBulkSlotBytes);
+  uint8_t* slots = bulk_smem;                                                 // [nslots][16][2112]
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(bulk_smem + (size_t)nslots * kBulkSlotBytes);
   float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + bulk_xs_bytes(NT, K));
   float* tile_out = red + kTcWarps * 16 * 16;                                // [16][17]
   BulkShared* sh = reinterpret_cast<BulkShared*>(tile_out + 16 * 17);
@@ -976,26 +989,25 @@ __global__ void __launch_bounds__(64) tree_recur_kernel(TreeRecurParams p) {
   pdl_trigger();
   const int h = blockIdx.x, b = blockIdx.y, c = threadIdx.x;
   const int L = p.L, H = p.H, hd = p.hd, d = H * hd;
-  const long long t = *p.t_buf;
+  const int t = (int)*p.t_buf;  // < max_len: positions and slots fit 32 bits
   __nv_bfloat16* ringb = p.ring + (size_t)b * p.S * d + h * hd + c;
   float vs[LMAX];
 #pragma unroll
   for (int l = 0; l < LMAX; ++l) {
-    const long long s = t - (1ll << l);
+    const int s = t - (1 << l);
     vs[l] = 0.f;
-    if (l < L && s >= 0 && c < hd)
-      vs[l] = bf2f(ringb[(size_t)(((2ll << l) - 2) + (s & ((2ll << l) - 1))) * d]);
+    if (l < L && s >= 0 && c < hd) vs[l] = bf2f(ringb[(size_t)(((2 << l) - 2) + (s & ((2 << l) - 1))) * d]);
   }
   float rg_src = 0.f;
   if (c < L) {
-    const long long s = t - (1ll << c);
+    const int s = t - (1 << c);
     if (s >= 0) rg_src = bf2f(p.rg[(((size_t)b * p.max_len + s) * L + c) * H + h]);
   }
   pdl_wait();
   const __nv_bfloat16 v0 = c < hd ? p.v0[(size_t)b * d + h * hd + c] : __float2bfloat16(0.f);
   if (c < L) {
     const int l = c;
-    const long long s = t - (1ll << l);
+    const int s = t - (1 << l);
     bool ok = s >= 0;
     if (ok && p.doc) ok = p.doc[(size_t)b * p.max_len + s] == p.doc[(size_t)b * p.max_len + t];
     float* pr = p.pre + ((size_t)b * L + l) * p.NP;
@@ -1020,7 +1032,7 @@ __global__ void __launch_bounds__(64) tree_recur_kernel(TreeRecurParams p) {
   for (int l = 0; l < LMAX; ++l) {
     if (l < L) {
       V = s_f[l] * V + s_c[l] * vs[l];
-      if (l + 1 < L) ringb[(size_t)(((2ll << (l + 1)) - 2) + (t & ((2ll << (l + 1)) - 1))) * d] = f2bf(V);
+      if (l + 1 < L) ringb[(size_t)(((2 << (l + 1)) - 2) + (t & ((2 << (l + 1)) - 1))) * d] = f2bf(V);
     }
   }
   p.y[(size_t)b * d + h * hd + c] = f2bf(V);
@@ -1121,21 +1133,21 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
   }
   const float Lsum = block_reduce_128(lsum, sred, false);  // includes a barrier after sc writes
   // values: thread (row group r, channel group cg) accumulates channels
-  // [8 cg, +8) over positions r, r + 16, ...; four 16-byte rows in flight
+  // [8 cg, +8) over positions r, r + 16, ...; eight 16-byte rows in flight
   const int cg = tid & 7, r0 = tid >> 3;
   float acc8[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc8[e] = 0.f;
-  for (int i0 = r0; i0 < cnt; i0 += 64) {
-    uint4 vv[4];
+  for (int i0 = r0; i0 < cnt; i0 += 128) {
+    uint4 vv[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 8; ++u) {
       const int i = i0 + 16 * u;
       if (i < cnt)
         vv[u] = *reinterpret_cast<const uint4*>(p.v + ((size_t)b * p.max_len + s0 + i) * d + h * HD + cg * 8);
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 8; ++u) {
       const int i = i0 + 16 * u;
       if (i < cnt) {
         float f[8];
