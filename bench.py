@@ -256,7 +256,7 @@ def run_decode(model, cfg, batch, ctx, steps, warmup, seed, world, select=None,
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(s.elapsed_time(e), world) / steps
-    dec.check_status(sync=True)
+    loop.finish()
     loop.release()
     return ms, steps, dec.persistent
 

@@ -1438,6 +1438,61 @@ __global__ void doc_step_kernel(const int64_t* tokens, const int64_t* t_buf, int
   last_tok[b] = tokens[b];
 }
 
+// Greedy token choice on the device: one block per row, the first index of
+// the row's largest logit (torch.argmax's tie rule; the logits are the
+// step's bf16 values), written to the next step's input and to an output
+// vector.
+__global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* logits, int vocab,
+                                                      int64_t* next_tokens, int64_t* out) {
+  __shared__ float s_v[32];
+  __shared__ int s_i[32];
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const __nv_bfloat16* row = logits + (size_t)b * vocab;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = tid; i < vocab; i += 1024) {  // ascending per thread: the first max is kept
+    const float v = bf2f(row[i]);
+    if (v > best) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    s_v[warp] = best;
+    s_i[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = s_v[lane];
+    bi = s_i[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      const int64_t tok = bi == 0x7fffffff ? 0 : bi;  // an all-NaN row picks 0
+      next_tokens[b] = tok;
+      if (out) out[b] = tok;
+    }
+  }
+}
+
 __global__ void advance_kernel(int64_t* t) {
   pdl_trigger();
   pdl_wait();
@@ -1698,6 +1753,16 @@ extern "C" int dh_decode_doc_step(const int64_t* tokens, const int64_t* t_buf, i
   if (launch_pdl(doc_step_kernel, dim3((batch + 127) / 128), dim3(128), 0, STREAM(stream), tokens,
                  t_buf, doc_hist, last_tok, eot, max_len, batch))
     return check_launch("doc_step_kernel");
+  return DH_OK;
+}
+
+extern "C" int dh_decode_argmax(const void* logits, int64_t* next_tokens, int64_t* out, int batch,
+                                int vocab, void* stream) {
+  DH_REQUIRE(logits && next_tokens, DH_ERR_ARG, "dh_decode_argmax: null pointer");
+  DH_REQUIRE(batch >= 1 && vocab >= 1, DH_ERR_SHAPE, "dh_decode_argmax: bad sizes");
+  if (launch_pdl(argmax_kernel, dim3(batch), dim3(1024), 0, STREAM(stream), BF(logits), vocab,
+                 next_tokens, out))
+    return check_launch("argmax_kernel");
   return DH_OK;
 }
 

@@ -388,20 +388,29 @@ class FusedGraphedHybridDecoder:
         return _LockstepLoop(self, select, group)
 
 
+def select_greedy(logits):
+    """Token choice for lockstep_loop: argmax per row (the loop runs it as
+    one device kernel, dh_decode_argmax, that also feeds the next step)."""
+    return logits.argmax(-1)
+
+
 class _LockstepLoop:
+    ARM_EVERY = 16   # steps between read-backs of the (sticky) status word
+
     def __init__(self, dec, select, group):
         import torch.distributed as dist
         if dec.graph is None:
             raise RuntimeError("call prefill() before lockstep_loop()")
-        self.dec = dec
+        self.dec, self.select, self.group = dec, select, group
         world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         self.world = world
         B = dec.batch
         self.tokens = torch.zeros(world * B, dtype=torch.long, device=dec.device)
+        self.local = torch.zeros(B, dtype=torch.long, device=dec.device)
+        self._n = 0
         # first token from the latest logits (the prefill's last position, or
         # the last step's), outside the graph
-        first = select(dec.logits_out)
-        dec.token_buf.copy_(first)
+        dec.token_buf.copy_(select(dec.logits_out))
         # warm the selection and the collective up outside the capture
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -415,18 +424,30 @@ class _LockstepLoop:
         if isinstance(dec.graph, _DirectStep):
             # a cooperative step the driver would not capture: issue it
             # directly, selection and collective after it
-            self._eager = (select, group)
             return
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             dec._record_step(torch.cuda.current_stream().cuda_stream)
-            tok = select(dec.logits_out)
-            dec.token_buf.copy_(tok)
-            if world > 1:
-                dist.all_gather_into_tensor(self.tokens, tok, group=group)
-            else:
-                self.tokens.copy_(tok)
+            self._choose()
         self.graph = g
+
+    def _choose(self):
+        """Token choice, feed-back and gather, on the current stream."""
+        import torch.distributed as dist
+        dec = self.dec
+        if self.select is select_greedy:
+            out = self.tokens if self.world == 1 else self.local
+            _lib.call("dh_decode_argmax", _ptr(dec.logits_out), _ptr(dec.token_buf), _ptr(out),
+                      dec.batch, dec.cfg.vocab_size,
+                      ctypes_void(torch.cuda.current_stream().cuda_stream))
+            tok = out
+        else:
+            tok = self.select(dec.logits_out)
+            dec.token_buf.copy_(tok)
+            if self.world == 1:
+                self.tokens.copy_(tok)
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.tokens, tok, group=self.group)
 
     def step(self):
         """One step: feeds the tokens chosen last (the prefill's for the
@@ -437,25 +458,25 @@ class _LockstepLoop:
             raise ValueError(f"context exhausted at max_len {dec.max_len}")
         dec.check_status()
         if self.graph is None:
-            import torch.distributed as dist
-            select, group = self._eager
             dec._record_step(torch.cuda.current_stream().cuda_stream)
-            tok = select(dec.logits_out)
-            dec.token_buf.copy_(tok)
-            if self.world > 1:
-                dist.all_gather_into_tensor(self.tokens, tok, group=group)
-            else:
-                self.tokens.copy_(tok)
+            self._choose()
         else:
             self.graph.replay()
         dec.t += 1
-        dec.status_word.arm()
+        self._n += 1
+        if self._n % self.ARM_EVERY == 0:
+            dec.status_word.arm()
         return self.tokens
+
+    def finish(self):
+        """Wait for the steps issued so far and raise if any kernel of them
+        reported a failure (the status word is sticky)."""
+        self.dec.status_word.arm()
+        self.dec.check_status(sync=True)
 
     def release(self):
         """Drop the graph (before destroying a process group it holds)."""
         self.graph = None
-        self._eager = None
 
 
 # the reference's name for the graphed decoder without fused kernels maps to

@@ -9,7 +9,7 @@ them run the B200 decoder, since that is the only compute path here.
 import torch
 import torch.nn.functional as F
 
-from .decoding import FusedGraphedHybridDecoder
+from .decoding import FusedGraphedHybridDecoder, select_greedy  # noqa: F401 (re-exported)
 
 def masked_logits(logits, temperature=1.0, top_k=None):
     """fp32 logits over max(T, 1e-6) with every logit below the k-th largest
@@ -27,11 +27,6 @@ def sampling_distribution(logits, temperature=1.0, top_k=None):
     return F.softmax(masked_logits(logits, temperature, top_k), dim=-1)
 
 
-def select_greedy(logits):
-    """Device-side token choice for lockstep_loop: argmax per row."""
-    return logits.argmax(-1)
-
-
 def select_top_k(top_k, temperature=1.0):
     """Device-side sampling for lockstep_loop: a draw from softmax(top-k
     logits / T) per row, taken as the Gumbel-max of the k candidates with
@@ -42,7 +37,8 @@ def select_top_k(top_k, temperature=1.0):
     inv_t = 1.0 / max(temperature, 1e-6)
 
     def select(logits):
-        v, i = torch.topk(logits.float(), top_k, dim=-1)
+        v, i = torch.topk(logits, top_k, dim=-1)   # on the bf16 logits: same set
+        v = v.float()
         u = torch.rand(v.shape, device=v.device).clamp_(min=1e-20)
         z = v * inv_t - torch.log(-torch.log(u))
         return i.gather(-1, z.argmax(-1, keepdim=True)).squeeze(-1)

@@ -174,6 +174,14 @@ DH_API int dh_decode_logits(const float* x, const void* norm_w, const void* emb,
 DH_API int dh_decode_doc_step(const int64_t* tokens, const int64_t* t_buf, int* doc_hist,
                        int64_t* last_tok, int64_t eot, int batch, int max_len, void* stream);
 
+/* Greedy choice of the next tokens on the device (fast_generate's argmax,
+ * modeling_dispatcher.py:433, without a host round trip): per row b, the
+ * first index of the largest of logits[b, :] (bf16 (batch, vocab), torch's
+ * tie rule), written to next_tokens[b] (the next step's token buffer) and,
+ * when out is not null, to out[b]. */
+DH_API int dh_decode_argmax(const void* logits, int64_t* next_tokens, int64_t* out, int batch,
+                            int vocab, void* stream);
+
 /* t_buf[0] += 1 (decoding.py:443). */
 DH_API int dh_decode_advance(int64_t* t_buf, void* stream);
 

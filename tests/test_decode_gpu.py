@@ -297,3 +297,23 @@ def test_lockstep_loop_matches_stepwise_greedy(small_nd):
         loop.step()
         top5 = torch.topk(dec3.logits_out.float(), 5, dim=-1).indices
         assert bool((top5 == dec3.token_buf[:, None]).any(-1).all())
+
+
+def test_device_argmax_matches_torch_with_ties():
+    """dh_decode_argmax: first index of the row maximum, as torch.argmax."""
+    import ctypes
+    from dispatcher_b200._lib import call
+    g = torch.Generator(device="cuda").manual_seed(7)
+    B, V = 5, 50257
+    lg = (torch.randn(B, V, device="cuda", generator=g) * 3).bfloat16()
+    lg[1, 100] = lg[1, 4000] = lg[1].max() + 1       # a tie: the first index wins
+    lg[2, V - 1] = 100.0                             # the last column
+    lg[3, 0] = 100.0                                 # the first column
+    nxt = torch.full((B,), -1, dtype=torch.long, device="cuda")
+    out = torch.full((B,), -1, dtype=torch.long, device="cuda")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    call("dh_decode_argmax", p(lg), p(nxt), p(out), B, V,
+         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    want = lg.argmax(-1)
+    assert torch.equal(nxt, want) and torch.equal(out, want)
+    assert int(want[1]) == 100
