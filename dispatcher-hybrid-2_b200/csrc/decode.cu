@@ -1402,6 +1402,192 @@ __global__ void __launch_bounds__(kFfnWarps * 32) ffn_kernel(FfnParams p) {
   }
 }
 
+// ---------------------------------------------------------------- fused FFN, bulk copies
+// The whole FFN for 1-2 lockstep rows with the weights through the copy
+// engine: CTA c takes tiles of 8 u elements (16 rows: gate and up row of each
+// element, the tensor-core GEMV tile above) and, as the next ring item of
+// each tile, the 8 matching rows of Wd^T.  A producer warp issues every copy
+// it can before the dependency wait; the consumers stage RMSNorm(x_in),
+// form u = silu(gate) * up (rounded to bf16) per tile, fold u into this
+// CTA's down-projection partials (registers, 4 output columns per thread),
+// and add the partials into x once at the end (vector reductions).
+template <int MAXB>
+__global__ void __launch_bounds__(kBulkThreads, 1)
+    ffn_bulk_kernel(FfnParams p, int nslots, int* status, uint32_t wait_limit) {
+  extern __shared__ __align__(128) unsigned char ffn_smem[];
+  const int d = p.d, batch = p.batch, KP = d + 32, ff = p.ff;
+  uint8_t* slots = ffn_smem;                                                     // [nslots][16][2112]
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(ffn_smem + (size_t)nslots * kBulkSlotBytes);
+  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + bulk_xs_bytes(1, d));
+  float* tile_out = red + kTcWarps * 16 * 16;   // [16][17]
+  float* us = tile_out + 16 * 17;               // [MAXB][8]
+  BulkShared* sh = reinterpret_cast<BulkShared*>(us + MAXB * 8);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ntiles = (ff + 7) / 8;
+  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int nitems = 2 * my_tiles;  // (gate/up tile, Wd^T rows) per tile
+  if (tid == 0) {
+    for (int i = 0; i < nslots; ++i) {
+      mbar_init(&sh->full[i], 1);
+      mbar_init(&sh->empty[i], kTcWarps);
+    }
+    sh->abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  if (warp == kTcWarps) {  // ---------------- producer (one lane)
+    if (lane != 0) return;
+    int issued = 0;
+    for (int item = 0; item < nitems; ++item) {
+      const int slot = item % nslots;
+      if (item >= nslots &&
+          !mbar_wait(&sh->empty[slot], (uint32_t)(((item / nslots) - 1) & 1), status, wait_limit)) {
+        sh->abort = 1;
+        break;
+      }
+      if (*reinterpret_cast<volatile int*>(&sh->abort)) break;
+      const int tile = blockIdx.x + (item >> 1) * gridDim.x;
+      uint8_t* dst = slots + (size_t)slot * kBulkSlotBytes;
+      const int nrows = (item & 1) ? 8 : 16;
+      mbar_arrive_expect_tx(&sh->full[slot], (uint32_t)(nrows * d * 2));
+      for (int r = 0; r < nrows; ++r) {
+        const __nv_bfloat16* row;
+        if (item & 1) {
+          row = p.wdT + (size_t)min(tile * 8 + r, ff - 1) * d;
+        } else {
+          const int u = min(tile * 8 + (r >> 1), ff - 1);
+          row = ((r & 1) ? p.wu : p.wg) + (size_t)u * d;
+        }
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_u32(dst + r * kBulkRowBytes)),
+            "l"(row), "r"((uint32_t)(d * 2)), "r"(smem_u32(&sh->full[slot]))
+            : "memory");
+      }
+      ++issued;
+    }
+    for (int sl = 0; sl < nslots; ++sl) {  // nothing in flight into this CTA when it exits
+      const int n_s = issued / nslots + (sl < issued % nslots ? 1 : 0);
+      if (n_s > 0) mbar_wait(&sh->full[sl], (uint32_t)((n_s - 1) & 1), nullptr, 1u << 20);
+    }
+    return;
+  }
+
+  // ---------------- consumers (8 warps, named barrier 1)
+  const int g = lane >> 2, t4 = lane & 3;
+  pdl_wait();
+  {  // RMSNorm(x_in) rows as bf16 (warp b takes row b: up to 1024 columns)
+    const int k4 = d / 4;
+    if (warp < batch) {
+      const float* xr = p.x_in + (size_t)warp * d;
+      float4 v[8];
+      uint2 wn[8];
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = lane + 32 * j;
+        v[j] = i < k4 ? reinterpret_cast<const float4*>(xr)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        wn[j] = i < k4 ? *reinterpret_cast<const uint2*>(p.norm_w + 4 * i) : make_uint2(0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+      const float sc = rsqrtf(warp_sum(ss) / (float)d + kNormEps);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = lane + 32 * j;
+        if (i < k4) {
+          const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wn[j].x));
+          const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wn[j].y));
+          uint2 pk;
+          pk.x = pack2(v[j].x * sc * w01.x, v[j].y * sc * w01.y);
+          pk.y = pack2(v[j].z * sc * w23.x, v[j].w * sc * w23.y);
+          *reinterpret_cast<uint2*>(xs + (size_t)warp * KP + 4 * i) = pk;
+        }
+      }
+    }
+  }
+  csync_bulk();
+
+  const int o = 4 * tid;  // this thread's 4 output columns of the down projection
+  float dacc[MAXB][4];
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) dacc[b][0] = dacc[b][1] = dacc[b][2] = dacc[b][3] = 0.f;
+  const int nchunks = d / 32;
+  for (int item = 0; item < nitems; ++item) {
+    const int slot = item % nslots;
+    const int tile = blockIdx.x + (item >> 1) * gridDim.x;
+    bool ok = !*reinterpret_cast<volatile int*>(&sh->abort);
+    if (ok && !mbar_wait(&sh->full[slot], (uint32_t)((item / nslots) & 1), status, wait_limit)) {
+      sh->abort = 1;
+      ok = false;
+    }
+    const uint8_t* sb = slots + (size_t)slot * kBulkSlotBytes;
+    if ((item & 1) == 0) {  // gate/up tile -> u of its 8 elements
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (ok) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = warp * 4 + i;
+          if (c < nchunks) {
+            const uint4 wa = *reinterpret_cast<const uint4*>(sb + g * kBulkRowBytes + c * 64 + t4 * 16);
+            const uint4 wb = *reinterpret_cast<const uint4*>(sb + (g + 8) * kBulkRowBytes + c * 64 + t4 * 16);
+            const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)g * KP + c * 32 + 8 * t4);
+            mma_bf16_16816(acc, wa.x, wb.x, wa.y, wb.y, xv.x, xv.y);
+            mma_bf16_16816(acc, wa.z, wb.z, wa.w, wb.w, xv.z, xv.w);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->empty[slot]);
+      float* pr = red + (size_t)warp * 256;
+      *reinterpret_cast<float2*>(pr + g * 16 + 2 * t4) = make_float2(acc[0], acc[1]);
+      *reinterpret_cast<float2*>(pr + (g + 8) * 16 + 2 * t4) = make_float2(acc[2], acc[3]);
+      csync_bulk();
+      if (tid < 128) {  // rows 0..15, columns (lockstep rows) 0..7
+        const int r = tid >> 3, col = tid & 7;
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kTcWarps; ++w) s += red[w * 256 + r * 16 + col];
+        tile_out[r * 17 + col] = s;
+      }
+      csync_bulk();
+      if (tid < 8 * MAXB) {  // tile row 2j = gate of element j, 2j + 1 = its up row
+        const int j = tid / MAXB, b = tid - j * MAXB;
+        const float gt = tile_out[(2 * j) * 17 + b], up = tile_out[(2 * j + 1) * 17 + b];
+        const bool live = b < batch && tile * 8 + j < ff;
+        us[b * 8 + j] = live ? bf2f(f2bf(gt / (1.0f + expf(-gt)) * up)) : 0.f;  // u in bf16
+      }
+      csync_bulk();
+    } else {  // Wd^T rows of the same 8 elements: this CTA's share of x += u . Wd^T
+      if (ok && o < d) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint2 w2 = *reinterpret_cast<const uint2*>(sb + j * kBulkRowBytes + o * 2);
+          const float2 wa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w2.x));
+          const float2 wb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w2.y));
+#pragma unroll
+          for (int b = 0; b < MAXB; ++b) {
+            const float uv = us[b * 8 + j];
+            dacc[b][0] = fmaf(wa.x, uv, dacc[b][0]);
+            dacc[b][1] = fmaf(wa.y, uv, dacc[b][1]);
+            dacc[b][2] = fmaf(wb.x, uv, dacc[b][2]);
+            dacc[b][3] = fmaf(wb.y, uv, dacc[b][3]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->empty[slot]);
+    }
+  }
+  if (my_tiles > 0 && o < d && !*reinterpret_cast<volatile int*>(&sh->abort)) {
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b)
+      if (b < batch) red_add_v4(p.x + (size_t)b * d + o, dacc[b][0], dacc[b][1], dacc[b][2], dacc[b][3]);
+  }
+}
+
 // ---------------------------------------------------------------- small ones
 __global__ void embed_kernel(const int64_t* tokens, const __nv_bfloat16* emb, float* x, int d,
                              int vocab, int* status) {
@@ -1623,9 +1809,31 @@ extern "C" int dh_decode_linear_residual(const void* y, const void* w, float* x,
   return DH_OK;
 }
 
+template <int MAXB>
+int launch_ffn_bulk(const FfnParams& prm, int* status, cudaStream_t st) {
+  constexpr size_t kMaxSmem = 227 * 1024;
+  const size_t fixed = bulk_xs_bytes(1, prm.d) + (size_t)kTcWarps * 16 * 16 * 4 + 16 * 17 * 4 +
+                       MAXB * 8 * 4 + sizeof(BulkShared) + 16;
+  const int nslots = (int)std::min<size_t>(kBulkMaxSlots, (kMaxSmem - fixed) / kBulkSlotBytes);
+  const size_t smem = fixed + (size_t)nslots * kBulkSlotBytes;
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaFuncSetAttribute(ffn_bulk_kernel<MAXB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kMaxSmem);
+    configured_dev = dev;
+  }
+  const int grid = std::min((prm.ff + 7) / 8, sm_count());
+  if (launch_pdl(ffn_bulk_kernel<MAXB>, dim3(grid), dim3(kBulkThreads), smem, st, prm, nslots, status,
+                 wait_limit()))
+    return check_launch("ffn_bulk_kernel");
+  return DH_OK;
+}
+
 extern "C" int dh_decode_ffn(const float* x_in, const void* norm_w, const void* w_gate,
                              const void* w_up, const void* w_down_t, float* x, int batch, int d,
-                             int ff, void* stream) {
+                             int ff, int* status, void* stream) {
   DH_REQUIRE(x_in && norm_w && w_gate && w_up && w_down_t && x, DH_ERR_ARG,
              "dh_decode_ffn: null pointer");
   DH_REQUIRE(d % 8 == 0 && d <= 2048 && ff >= 1 && batch >= 1, DH_ERR_SHAPE,
@@ -1645,6 +1853,14 @@ extern "C" int dh_decode_ffn(const float* x_in, const void* norm_w, const void* 
   }
   for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
     const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    if (nb <= 2 && d <= 1024 && d % 32 == 0) {  // tensor cores, weights by bulk copies
+      FfnParams prm{x_in + (size_t)b0 * d, BF(norm_w), BF(w_gate), BF(w_up), BF(w_down_t),
+                    x + (size_t)b0 * d, d, ff, nb, 0};
+      const int rc = nb == 1 ? launch_ffn_bulk<1>(prm, status, STREAM(stream))
+                             : launch_ffn_bulk<2>(prm, status, STREAM(stream));
+      if (rc) return rc;
+      continue;
+    }
     const int maxb = nb == 1 ? 1 : (nb <= 4 ? 4 : 16);
     // one wave of CTAs at small batches; more u elements per CTA (fewer
     // atomic row updates) at large batches

@@ -253,7 +253,7 @@ class FusedGraphedHybridDecoder:
                  P(self.x_copy) if self.ffn_fused else None, B, d, d, P(self.status), s)
             if self.ffn_fused:
                 call("dh_decode_ffn", P(self.x_copy), P(lay["norm2"]), P(lay["w_gate"]),
-                     P(lay["w_up"]), P(lay["w_downT"]), P(self.x), B, d, ff, s)
+                     P(lay["w_up"]), P(lay["w_downT"]), P(self.x), B, d, ff, P(self.status), s)
             else:
                 call("dh_decode_ffn_in", P(self.x), P(lay["norm2"]), P(lay["w_gate"]),
                      P(lay["w_up"]), P(self.u), B, d, ff, P(self.status), s)
