@@ -1414,11 +1414,12 @@ __global__ void __launch_bounds__(kFfnWarps * 32) ffn_kernel(FfnParams p) {
 template <int MAXB>
 __global__ void __launch_bounds__(kBulkThreads, 1)
     ffn_bulk_kernel(FfnParams p, int nslots, int* status, uint32_t wait_limit) {
+  constexpr int NT = MAXB > 8 ? 2 : 1;  // 8-column mma tiles of lockstep rows
   extern __shared__ __align__(128) unsigned char ffn_smem[];
   const int d = p.d, batch = p.batch, KP = d + 32, ff = p.ff;
   uint8_t* slots = ffn_smem;                                                     // [nslots][16][2112]
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(ffn_smem + (size_t)nslots * kBulkSlotBytes);
-  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + bulk_xs_bytes(1, d));
+  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + bulk_xs_bytes(NT, d));
   float* tile_out = red + kTcWarps * 16 * 16;   // [16][17]
   float* us = tile_out + 16 * 17;               // [MAXB][8]
   BulkShared* sh = reinterpret_cast<BulkShared*>(us + MAXB * 8);
@@ -1478,10 +1479,10 @@ __global__ void __launch_bounds__(kBulkThreads, 1)
   // ---------------- consumers (8 warps, named barrier 1)
   const int g = lane >> 2, t4 = lane & 3;
   pdl_wait();
-  {  // RMSNorm(x_in) rows as bf16 (warp b takes row b: up to 1024 columns)
+  for (int rb = warp; rb < batch; rb += kTcWarps) {  // RMSNorm(x_in) rows as bf16, warp per row
     const int k4 = d / 4;
-    if (warp < batch) {
-      const float* xr = p.x_in + (size_t)warp * d;
+    {
+      const float* xr = p.x_in + (size_t)rb * d;
       float4 v[8];
       uint2 wn[8];
       float ss = 0.f;
@@ -1503,7 +1504,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1)
           uint2 pk;
           pk.x = pack2(v[j].x * sc * w01.x, v[j].y * sc * w01.y);
           pk.y = pack2(v[j].z * sc * w23.x, v[j].w * sc * w23.y);
-          *reinterpret_cast<uint2*>(xs + (size_t)warp * KP + 4 * i) = pk;
+          *reinterpret_cast<uint2*>(xs + (size_t)rb * KP + 4 * i) = pk;
         }
       }
     }
@@ -1525,7 +1526,9 @@ __global__ void __launch_bounds__(kBulkThreads, 1)
     }
     const uint8_t* sb = slots + (size_t)slot * kBulkSlotBytes;
     if ((item & 1) == 0) {  // gate/up tile -> u of its 8 elements
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      float acc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
       if (ok) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -1533,20 +1536,26 @@ __global__ void __launch_bounds__(kBulkThreads, 1)
           if (c < nchunks) {
             const uint4 wa = *reinterpret_cast<const uint4*>(sb + g * kBulkRowBytes + c * 64 + t4 * 16);
             const uint4 wb = *reinterpret_cast<const uint4*>(sb + (g + 8) * kBulkRowBytes + c * 64 + t4 * 16);
-            const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)g * KP + c * 32 + 8 * t4);
-            mma_bf16_16816(acc, wa.x, wb.x, wa.y, wb.y, xv.x, xv.y);
-            mma_bf16_16816(acc, wa.z, wb.z, wa.w, wb.w, xv.z, xv.w);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)(nt * 8 + g) * KP + c * 32 + 8 * t4);
+              mma_bf16_16816(acc[nt], wa.x, wb.x, wa.y, wb.y, xv.x, xv.y);
+              mma_bf16_16816(acc[nt], wa.z, wb.z, wa.w, wb.w, xv.z, xv.w);
+            }
           }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh->empty[slot]);
       float* pr = red + (size_t)warp * 256;
-      *reinterpret_cast<float2*>(pr + g * 16 + 2 * t4) = make_float2(acc[0], acc[1]);
-      *reinterpret_cast<float2*>(pr + (g + 8) * 16 + 2 * t4) = make_float2(acc[2], acc[3]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        *reinterpret_cast<float2*>(pr + g * 16 + nt * 8 + 2 * t4) = make_float2(acc[nt][0], acc[nt][1]);
+        *reinterpret_cast<float2*>(pr + (g + 8) * 16 + nt * 8 + 2 * t4) = make_float2(acc[nt][2], acc[nt][3]);
+      }
       csync_bulk();
-      if (tid < 128) {  // rows 0..15, columns (lockstep rows) 0..7
-        const int r = tid >> 3, col = tid & 7;
+      {  // rows 0..15, columns (lockstep rows) 0..15
+        const int r = tid >> 4, col = tid & 15;
         float s = 0.f;
 #pragma unroll
         for (int w = 0; w < kTcWarps; ++w) s += red[w * 256 + r * 16 + col];
@@ -1812,8 +1821,8 @@ extern "C" int dh_decode_linear_residual(const void* y, const void* w, float* x,
 template <int MAXB>
 int launch_ffn_bulk(const FfnParams& prm, int* status, cudaStream_t st) {
   constexpr size_t kMaxSmem = 227 * 1024;
-  const size_t fixed = bulk_xs_bytes(1, prm.d) + (size_t)kTcWarps * 16 * 16 * 4 + 16 * 17 * 4 +
-                       MAXB * 8 * 4 + sizeof(BulkShared) + 16;
+  const size_t fixed = bulk_xs_bytes(MAXB > 8 ? 2 : 1, prm.d) + (size_t)kTcWarps * 16 * 16 * 4 +
+                       16 * 17 * 4 + MAXB * 8 * 4 + sizeof(BulkShared) + 16;
   const int nslots = (int)std::min<size_t>(kBulkMaxSlots, (kMaxSmem - fixed) / kBulkSlotBytes);
   const size_t smem = fixed + (size_t)nslots * kBulkSlotBytes;
   static thread_local int configured_dev = -1;
@@ -1853,11 +1862,14 @@ extern "C" int dh_decode_ffn(const float* x_in, const void* norm_w, const void* 
   }
   for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
     const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
-    if (nb <= 2 && d <= 1024 && d % 32 == 0) {  // tensor cores, weights by bulk copies
+    if (d <= 1024 && d % 32 == 0) {  // tensor cores, weights by bulk copies
       FfnParams prm{x_in + (size_t)b0 * d, BF(norm_w), BF(w_gate), BF(w_up), BF(w_down_t),
                     x + (size_t)b0 * d, d, ff, nb, 0};
-      const int rc = nb == 1 ? launch_ffn_bulk<1>(prm, status, STREAM(stream))
-                             : launch_ffn_bulk<2>(prm, status, STREAM(stream));
+      const int rc = nb == 1   ? launch_ffn_bulk<1>(prm, status, STREAM(stream))
+                     : nb == 2 ? launch_ffn_bulk<2>(prm, status, STREAM(stream))
+                     : nb <= 4 ? launch_ffn_bulk<4>(prm, status, STREAM(stream))
+                     : nb <= 8 ? launch_ffn_bulk<8>(prm, status, STREAM(stream))
+                               : launch_ffn_bulk<16>(prm, status, STREAM(stream));
       if (rc) return rc;
       continue;
     }

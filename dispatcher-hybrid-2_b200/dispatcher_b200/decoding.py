@@ -142,7 +142,6 @@ class FusedGraphedHybridDecoder:
                        TreeLayerCache(batch, self.max_len, d, L, H, hd, dev, dt)
                        for i in range(cfg.num_layers)]
         f32, bf = torch.float32, torch.bfloat16
-        ff = cfg.dim_feedforward
         self.token_buf = torch.zeros(batch, dtype=torch.long, device=dev)
         # document ids per (row, position) and each row's last token, used
         # only when the decoder tracks documents
@@ -157,7 +156,6 @@ class FusedGraphedHybridDecoder:
         self.a = torch.zeros(batch, d, device=dev, dtype=bf)
         self.y = torch.zeros(batch, d, device=dev, dtype=bf)
         self.q = torch.zeros(batch, d, device=dev, dtype=bf)
-        self.u = torch.zeros(batch, ff, device=dev, dtype=bf)
         self.ig = torch.zeros(batch, L, H, device=dev, dtype=f32)
         self.fg = torch.zeros(batch, L, H, device=dev, dtype=f32)
         sm = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -176,11 +174,9 @@ class FusedGraphedHybridDecoder:
         self.persistent = (self.step_kernel == "persistent" and batch <= 2 and d <= 1024
                            and d % 128 == 0 and hd == 64
                            and cfg.levels * (2 * d + 16) <= 32768)
-        # up to 2 rows: one fused FFN launch, which reads the down projection
-        # by rows of its transpose; from 3 rows on the gate/up and the down
-        # projection run as two tensor-core GEMVs (u through HBM, 16 KB a row)
-        self.ffn_fused = batch <= 2
-        if not self.persistent and self.ffn_fused:
+        # the FFN is one launch per layer, which reads the down projection by
+        # rows of its transpose
+        if not self.persistent:
             for lay in self.w.layers:
                 if "w_downT" not in lay:
                     lay["w_downT"] = lay["w_down"].t().contiguous()
@@ -250,15 +246,9 @@ class FusedGraphedHybridDecoder:
             # output projection + residual (for the fused FFN it also leaves a
             # copy of x, which that kernel reads while it adds into x), then the FFN
             call("dh_decode_linear_residual", P(self.y), P(lay["w_out"]), P(self.x),
-                 P(self.x_copy) if self.ffn_fused else None, B, d, d, P(self.status), s)
-            if self.ffn_fused:
-                call("dh_decode_ffn", P(self.x_copy), P(lay["norm2"]), P(lay["w_gate"]),
-                     P(lay["w_up"]), P(lay["w_downT"]), P(self.x), B, d, ff, P(self.status), s)
-            else:
-                call("dh_decode_ffn_in", P(self.x), P(lay["norm2"]), P(lay["w_gate"]),
-                     P(lay["w_up"]), P(self.u), B, d, ff, P(self.status), s)
-                call("dh_decode_linear_residual", P(self.u), P(lay["w_down"]), P(self.x),
-                     None, B, ff, d, P(self.status), s)
+                 P(self.x_copy), B, d, d, P(self.status), s)
+            call("dh_decode_ffn", P(self.x_copy), P(lay["norm2"]), P(lay["w_gate"]),
+                 P(lay["w_up"]), P(lay["w_downT"]), P(self.x), B, d, ff, P(self.status), s)
         call("dh_decode_logits", P(self.x), P(W.norm_out), P(W.lm_head), P(self.logits_out),
              B, d, V, P(self.status), s)
         call("dh_decode_advance", P(self.t_buf), s)

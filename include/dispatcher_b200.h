@@ -124,9 +124,10 @@ DH_API int dh_decode_linear_residual(const void* y, const void* w, float* x, flo
  * to bf16.  x_in: fp32 (batch, d), a copy of x (from dh_decode_linear_residual);
  * w_down_t: Wd transposed, bf16 (ff, d); x fp32 (batch, d) receives the down
  * projection through atomic adds (summation order not fixed).  d <= 2048.
- * Up to 2 rows with d <= 1024 (a multiple of 32): the gate/up tiles on the
- * tensor cores, all weights streamed by bulk copies; *status (nullable)
- * receives DH_ERR_TIMEOUT if a bounded wait of that pipeline gives up. */
+ * With d <= 1024 (a multiple of 32), for every batch: the gate/up tiles on
+ * the tensor cores, all weights streamed by bulk copies, the down projection
+ * folded per CTA before its atomic adds; *status (nullable) receives
+ * DH_ERR_TIMEOUT if a bounded wait of that pipeline gives up. */
 DH_API int dh_decode_ffn(const float* x_in, const void* norm_w, const void* w_gate, const void* w_up,
                   const void* w_down_t, float* x, int batch, int d, int ff, int* status,
                   void* stream);

@@ -65,9 +65,10 @@ def test_decoder_matches_forward_small_seed0(small_s0):
 @pytest.mark.parametrize("batch", [3, 9])
 def test_decoder_batched(small_nd, batch):
     """From 3 rows the GEMVs and the tree gates run on the tensor cores
-    (one 8-column mma tile up to 8 rows, two from 9)."""
+    (one 8-column mma tile up to 8 rows, two from 9); up to 8 rows the FFN
+    is one fused launch, from 9 a gate/up and a down-projection GEMV."""
     dec = _compare(*small_nd, batch=batch, seed=5)[0]
-    assert dec.tree_tc and not dec.ffn_fused
+    assert dec.tree_tc
 
 
 def test_prefill_logits_match_forward(small_nd):
@@ -288,7 +289,9 @@ def test_lockstep_loop_matches_stepwise_greedy(small_nd):
         got.append(loop.step().clone())
     assert dec2.t == dec.t
     assert torch.equal(torch.stack(got), torch.stack(want))
-    assert torch.equal(dec2.logits_out, dec.logits_out)
+    # the FFN adds its CTAs' partial sums with atomics: the fp32 summation
+    # order varies between runs, the bf16 logits by about an ulp
+    assert (dec2.logits_out.float() - dec.logits_out.float()).abs().max().item() < 2e-2
     # sampled choices stay inside each row's top-k set
     dec3 = FusedGraphedHybridDecoder(model)
     dec3.prefill(ids)
