@@ -1080,11 +1080,15 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
   long long s1 = s0 + chunk;
   if (s1 > t + 1) s1 = t + 1;
   const int cnt = s1 > s0 ? (int)(s1 - s0) : 0;
-  // cache rows before t were written by earlier steps: warm them into L2
-  for (int i = tid; i < cnt; i += 128) {
-    if (s0 + i < t) {
-      prefetch_l2(p.k + ((size_t)b * p.max_len + s0 + i) * d + h * HD, HD * 2);
-      prefetch_l2(p.v + ((size_t)b * p.max_len + s0 + i) * d + h * HD, HD * 2);
+  // cache rows before t were written by earlier steps: the blocks of head 0
+  // warm whole rows (every head, 2 KB each) into L2 for the blocks of all
+  // heads (one bulk prefetch per row, not one per 128-byte head slice)
+  if (h == 0) {
+    for (int i = tid; i < cnt; i += 128) {
+      if (s0 + i < t) {
+        prefetch_l2(p.k + ((size_t)b * p.max_len + s0 + i) * d, (uint32_t)d * 2);
+        prefetch_l2(p.v + ((size_t)b * p.max_len + s0 + i) * d, (uint32_t)d * 2);
+      }
     }
   }
   pdl_wait();
@@ -1092,35 +1096,38 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
   __syncthreads();
   const float scale = rsqrtf((float)HD);
 
-  // scores: a thread takes positions tid, tid + 128, ..., two key rows
-  // (16 loads of 16 bytes) in flight per round
+  // scores: eight lanes per key row (its 128 bytes read coalesced), partial
+  // dot products joined by three shuffles, eight rows in flight per thread;
+  // every lane runs the same rounds, so the shuffles see whole warps
+  const int kg = tid & 7, rs = tid >> 3;  // 16 row groups of 8 lanes
+  float qf[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) qf[e] = sq[kg * 8 + e];
   float mloc = -INFINITY;
-  for (int i0 = tid; i0 < cnt; i0 += 256) {
-    uint4 kv[2][HD / 8];
+  for (int base = 0; base < cnt; base += 128) {
+    uint4 kv[8];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int i = i0 + 128 * u;
-      if (i < cnt) {
-        const uint4* kr = reinterpret_cast<const uint4*>(p.k + ((size_t)b * p.max_len + s0 + i) * d + h * HD);
-#pragma unroll
-        for (int j = 0; j < HD / 8; ++j) kv[u][j] = kr[j];
-      }
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + rs + 16 * u;
+      kv[u] = i < cnt ? *reinterpret_cast<const uint4*>(p.k + ((size_t)b * p.max_len + s0 + i) * d +
+                                                         h * HD + kg * 8)
+                      : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int i = i0 + 128 * u;
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + rs + 16 * u;
+      float f[8];
+      unpack8(kv[u], f);
+      float sd = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sd = fmaf(f[e], qf[e], sd);
+      sd += __shfl_xor_sync(0xffffffffu, sd, 1);
+      sd += __shfl_xor_sync(0xffffffffu, sd, 2);
+      sd += __shfl_xor_sync(0xffffffffu, sd, 4);
       if (i < cnt) {
-        float s = 0.f;
-#pragma unroll
-        for (int j = 0; j < HD / 8; ++j) {
-          float f[8];
-          unpack8(kv[u][j], f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) s = fmaf(f[e], sq[j * 8 + e], s);
-        }
-        s *= scale;
-        sc[i] = s;
-        mloc = fmaxf(mloc, s);
+        sd *= scale;
+        if (kg == 0) sc[i] = sd;
+        mloc = fmaxf(mloc, sd);
       }
     }
   }
