@@ -1695,6 +1695,126 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* logit
   }
 }
 
+// Top-k / temperature sampling on the device, one block per row: the k-th
+// largest logit by a two-pass radix select over the bf16 keys, then a draw
+// from softmax(logit / T) restricted to the logits >= that value (the
+// reference's rule, modeling_dispatcher.py:427-432: every logit below the
+// k-th largest masked, ties at it kept) as the Gumbel-max over those
+// candidates.  The uniforms come from a counter-based hash of (seed,
+// position t, row, index): a fresh draw every step with no generator state.
+__device__ __forceinline__ uint32_t bf16_key(__nv_bfloat16 v) {  // order-preserving
+  const uint16_t u = *reinterpret_cast<const uint16_t*>(&v);
+  return (u & 0x8000u) ? (uint32_t)(uint16_t)~u : (uint32_t)(u | 0x8000u);
+}
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {  // splitmix64 finaliser
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+
+// bin of the 256-bin histogram (from the top) that holds the k-th largest
+// key, and the number of keys in the bins above it
+__device__ __forceinline__ void select_bin(const int* hist, int k, int& bin, int& above) {
+  __shared__ int s_bin, s_above;
+  if (threadIdx.x == 0) {
+    int acc = 0, bsel = 0;
+    for (int j = 255; j >= 0; --j) {
+      if (acc + hist[j] >= k) {
+        bsel = j;
+        break;
+      }
+      acc += hist[j];
+    }
+    s_bin = bsel;
+    s_above = acc;
+  }
+  __syncthreads();
+  bin = s_bin;
+  above = s_above;
+}
+
+__global__ void __launch_bounds__(1024) sample_top_k_kernel(const __nv_bfloat16* logits, int vocab,
+                                                            int k, float inv_temp,
+                                                            unsigned long long seed,
+                                                            const int64_t* t_buf,
+                                                            int64_t* next_tokens, int64_t* out) {
+  __shared__ int hist[256];
+  __shared__ float s_v[32];
+  __shared__ int s_i[32];
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const __nv_bfloat16* row = logits + (size_t)b * vocab;
+  const int kk = k < 1 ? 1 : (k > vocab ? vocab : k);
+  // pass 1: high byte of the key
+  for (int j = tid; j < 256; j += 1024) hist[j] = 0;
+  __syncthreads();
+  for (int i = tid; i < vocab; i += 1024) atomicAdd(&hist[bf16_key(row[i]) >> 8], 1);
+  __syncthreads();
+  int hi, above_hi;
+  select_bin(hist, kk, hi, above_hi);
+  __syncthreads();
+  // pass 2: low byte among the keys of that high byte
+  for (int j = tid; j < 256; j += 1024) hist[j] = 0;
+  __syncthreads();
+  for (int i = tid; i < vocab; i += 1024) {
+    const uint32_t key = bf16_key(row[i]);
+    if ((int)(key >> 8) == hi) atomicAdd(&hist[key & 255], 1);
+  }
+  __syncthreads();
+  int lo, above_lo;
+  select_bin(hist, kk - above_hi, lo, above_lo);
+  const uint32_t thr = ((uint32_t)hi << 8) | (uint32_t)lo;  // key of the k-th largest logit
+  // Gumbel-max over the candidates
+  const uint64_t base = mix64(seed ^ mix64((uint64_t)*t_buf * 0x9e3779b97f4a7c15ull + (uint64_t)b));
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = tid; i < vocab; i += 1024) {
+    const __nv_bfloat16 v = row[i];
+    if (bf16_key(v) < thr) continue;
+    const uint64_t h = mix64(base + (uint64_t)i);
+    const float u = ((float)(uint32_t)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);  // in (0, 1)
+    const float z = bf2f(v) * inv_temp - logf(-logf(u));
+    if (z > best) {
+      best = z;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    s_v[warp] = best;
+    s_i[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = s_v[lane];
+    bi = s_i[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      const int64_t tok = bi == 0x7fffffff ? 0 : bi;
+      next_tokens[b] = tok;
+      if (out) out[b] = tok;
+    }
+  }
+}
+
 __global__ void advance_kernel(int64_t* t) {
   pdl_trigger();
   pdl_wait();
@@ -1998,6 +2118,19 @@ extern "C" int dh_decode_argmax(const void* logits, int64_t* next_tokens, int64_
   if (launch_pdl(argmax_kernel, dim3(batch), dim3(1024), 0, STREAM(stream), BF(logits), vocab,
                  next_tokens, out))
     return check_launch("argmax_kernel");
+  return DH_OK;
+}
+
+extern "C" int dh_decode_sample_top_k(const void* logits, int64_t* next_tokens, int64_t* out,
+                                      int batch, int vocab, int top_k, float temperature,
+                                      unsigned long long seed, const int64_t* t_buf, void* stream) {
+  DH_REQUIRE(logits && next_tokens && t_buf, DH_ERR_ARG, "dh_decode_sample_top_k: null pointer");
+  DH_REQUIRE(batch >= 1 && vocab >= 1 && top_k >= 1, DH_ERR_SHAPE,
+             "dh_decode_sample_top_k: bad sizes");
+  const float inv_t = 1.0f / (temperature > 1e-6f ? temperature : 1e-6f);
+  if (launch_pdl(sample_top_k_kernel, dim3(batch), dim3(1024), 0, STREAM(stream), BF(logits), vocab,
+                 top_k, inv_t, seed, t_buf, next_tokens, out))
+    return check_launch("sample_top_k_kernel");
   return DH_OK;
 }
 

@@ -37,7 +37,7 @@ def _ctype(decl):
     base = base.replace("const", "").strip()
     return {"int": ctypes.c_int, "float": ctypes.c_float, "int64_t": ctypes.c_int64,
             "uint32_t": ctypes.c_uint32, "size_t": ctypes.c_size_t,
-            "long long": ctypes.c_longlong}[base]
+            "long long": ctypes.c_longlong, "unsigned long long": ctypes.c_ulonglong}[base]
 
 
 def parse_header(path=HEADER):

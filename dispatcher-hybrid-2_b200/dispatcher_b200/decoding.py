@@ -425,11 +425,17 @@ class _LockstepLoop:
         """Token choice, feed-back and gather, on the current stream."""
         import torch.distributed as dist
         dec = self.dec
+        stream = ctypes_void(torch.cuda.current_stream().cuda_stream)
+        out = self.tokens if self.world == 1 else self.local
         if self.select is select_greedy:
-            out = self.tokens if self.world == 1 else self.local
             _lib.call("dh_decode_argmax", _ptr(dec.logits_out), _ptr(dec.token_buf), _ptr(out),
-                      dec.batch, dec.cfg.vocab_size,
-                      ctypes_void(torch.cuda.current_stream().cuda_stream))
+                      dec.batch, dec.cfg.vocab_size, stream)
+            tok = out
+        elif getattr(self.select, "top_k", None) is not None:   # generation.select_top_k
+            sel = self.select
+            _lib.call("dh_decode_sample_top_k", _ptr(dec.logits_out), _ptr(dec.token_buf),
+                      _ptr(out), dec.batch, dec.cfg.vocab_size, sel.top_k, sel.temperature,
+                      sel.seed, _ptr(dec.t_buf), stream)
             tok = out
         else:
             tok = self.select(dec.logits_out)

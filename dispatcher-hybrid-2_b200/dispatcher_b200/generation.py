@@ -27,21 +27,25 @@ def sampling_distribution(logits, temperature=1.0, top_k=None):
     return F.softmax(masked_logits(logits, temperature, top_k), dim=-1)
 
 
-def select_top_k(top_k, temperature=1.0):
-    """Device-side sampling for lockstep_loop: a draw from softmax(top-k
-    logits / T) per row, taken as the Gumbel-max of the k candidates with
-    noise from torch's default CUDA generator (capturable in a CUDA graph,
-    each replay advancing the generator).  The same distribution as the
-    reference's multinomial over the masked softmax
-    (modeling_dispatcher.py:427-433); the draws themselves differ."""
+def select_top_k(top_k, temperature=1.0, seed=None):
+    """Token choice for lockstep_loop: a draw from softmax(logits / T) over
+    the logits >= the top_k-th largest (ties kept, the reference's mask,
+    modeling_dispatcher.py:427-432), as a Gumbel-max.  Inside the loop's
+    graph it runs as one device kernel (dh_decode_sample_top_k, uniforms
+    from a hash of seed, position, row and index); called directly (the
+    loop's first token) it uses torch's generator.  Same distribution as
+    the reference's multinomial; the draws themselves differ."""
     inv_t = 1.0 / max(temperature, 1e-6)
 
     def select(logits):
-        v, i = torch.topk(logits, top_k, dim=-1)   # on the bf16 logits: same set
-        v = v.float()
-        u = torch.rand(v.shape, device=v.device).clamp_(min=1e-20)
-        z = v * inv_t - torch.log(-torch.log(u))
-        return i.gather(-1, z.argmax(-1, keepdim=True)).squeeze(-1)
+        lf = logits.float()
+        kth = torch.topk(lf, top_k, dim=-1).values[:, -1:]
+        u = torch.rand(lf.shape, device=lf.device).clamp_(min=1e-20)
+        z = torch.where(lf >= kth, lf * inv_t - torch.log(-torch.log(u)),
+                        torch.full_like(lf, float("-inf")))
+        return z.argmax(-1)
+    select.top_k, select.temperature = top_k, temperature
+    select.seed = int(seed if seed is not None else torch.initial_seed()) & (2 ** 64 - 1)
     return select
 
 

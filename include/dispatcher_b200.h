@@ -187,6 +187,18 @@ DH_API int dh_decode_doc_step(const int64_t* tokens, const int64_t* t_buf, int* 
 DH_API int dh_decode_argmax(const void* logits, int64_t* next_tokens, int64_t* out, int batch,
                             int vocab, void* stream);
 
+/* Sampling of the next tokens on the device (fast_generate with do_sample,
+ * top_k and temperature, modeling_dispatcher.py:426-432, without a host round
+ * trip): per row b, a draw from softmax(logits[b] / max(T, 1e-6)) restricted
+ * to the logits >= the top_k-th largest (ties at it kept, as the reference's
+ * mask), taken as the Gumbel-max over those candidates with uniforms from a
+ * counter-based hash of (seed, the position in *t_buf, b, index).  Same
+ * distribution as the reference's multinomial; the draws differ.  Writes
+ * next_tokens[b] and, when out is not null, out[b]. */
+DH_API int dh_decode_sample_top_k(const void* logits, int64_t* next_tokens, int64_t* out, int batch,
+                                  int vocab, int top_k, float temperature, unsigned long long seed,
+                                  const int64_t* t_buf, void* stream);
+
 /* t_buf[0] += 1 (decoding.py:443). */
 DH_API int dh_decode_advance(int64_t* t_buf, void* stream);
 

@@ -292,14 +292,15 @@ def test_lockstep_loop_matches_stepwise_greedy(small_nd):
     # the FFN adds its CTAs' partial sums with atomics: the fp32 summation
     # order varies between runs, the bf16 logits by about an ulp
     assert (dec2.logits_out.float() - dec.logits_out.float()).abs().max().item() < 2e-2
-    # sampled choices stay inside each row's top-k set
+    # sampled choices stay among each row's logits >= its 5th largest
     dec3 = FusedGraphedHybridDecoder(model)
     dec3.prefill(ids)
-    loop = dec3.lockstep_loop(select_top_k(5, 0.8))
+    loop = dec3.lockstep_loop(select_top_k(5, 0.8, seed=3))
     for _ in range(6):
         loop.step()
-        top5 = torch.topk(dec3.logits_out.float(), 5, dim=-1).indices
-        assert bool((top5 == dec3.token_buf[:, None]).any(-1).all())
+        lg = dec3.logits_out.float()
+        kth = torch.topk(lg, 5, dim=-1).values[:, -1]
+        assert bool((lg.gather(1, dec3.token_buf[:, None])[:, 0] >= kth).all())
 
 
 def test_device_argmax_matches_torch_with_ties():
@@ -320,3 +321,45 @@ def test_device_argmax_matches_torch_with_ties():
     want = lg.argmax(-1)
     assert torch.equal(nxt, want) and torch.equal(out, want)
     assert int(want[1]) == 100
+
+
+def _sample(lg, k, temp, seed, t):
+    import ctypes
+    from dispatcher_b200._lib import call
+    B, V = lg.shape
+    nxt = torch.full((B,), -1, dtype=torch.long, device="cuda")
+    tb = torch.tensor([t], dtype=torch.long, device="cuda")
+    p = lambda x: ctypes.c_void_p(x.data_ptr())  # noqa: E731
+    call("dh_decode_sample_top_k", p(lg), p(nxt), None, B, V, k, temp, seed, p(tb),
+         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    return nxt
+
+
+def test_device_top_k_sampling_candidates_and_distribution():
+    """dh_decode_sample_top_k: every draw is a logit >= the k-th largest
+    (ties at the k-th kept, the reference's mask), k = 1 without ties is the
+    argmax, and the frequencies follow softmax(logit / T) over the
+    candidates."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    # coarse values: many ties, also at the k-th largest
+    lg = (torch.randint(-20, 20, (6, 50257), device="cuda", generator=g) * 0.25).bfloat16()
+    for k in (1, 7, 50, 50257):
+        for t in range(3):
+            tok = _sample(lg, k, 0.8, 1234, 100 + t)
+            kth = torch.topk(lg.float(), k, dim=-1).values[:, -1]
+            assert bool((lg.float().gather(1, tok[:, None])[:, 0] >= kth).all()), k
+    lg1 = torch.randn(4, 1000, device="cuda", generator=g).bfloat16()
+    assert torch.equal(_sample(lg1, 1, 0.8, 5, 7), lg1.argmax(-1))
+    # distribution: 64 identical rows x 64 positions = 4096 draws
+    V, k, temp = 16, 8, 0.8
+    base = torch.linspace(-1.0, 1.5, V, device="cuda").bfloat16()
+    rows = base[None].expand(64, V).contiguous()
+    counts = torch.zeros(V, device="cuda")
+    for t in range(64):
+        counts += torch.bincount(_sample(rows, k, temp, 77, t), minlength=V).float()
+    freq = counts / counts.sum()
+    lf = base.float()
+    kth = torch.topk(lf, k).values[-1]
+    want = torch.softmax(torch.where(lf >= kth, lf / temp, torch.full_like(lf, float("-inf"))), 0)
+    assert (freq - want).abs().max().item() < 0.03, (freq, want)
+    assert counts[lf < kth].sum().item() == 0
