@@ -1,10 +1,13 @@
 // Decode-step kernels: one lockstep position for batch <= 16 rows per launch
 // (larger batches are split into chunks of 16 by the entry points).
 //
-// Every weight matrix is streamed from HBM exactly once per step: a warp owns
-// a pair of output rows, keeps the (normalised) activations of all rows of
-// the batch in shared memory, and reduces its per-lane partial sums with a
-// transpose-reduction so that lane l ends up owning (row, batch) = (l / B, l % B).
+// Every weight matrix is streamed from HBM exactly once per step.  The GEMVs
+// and the FFN run on the tensor cores with the weights brought by bulk copies
+// (gemv_bulk_kernel, ffn_bulk_kernel: the lockstep rows are the N side of
+// mma.sync); the CUDA-core forms below them (a warp per pair of output rows,
+// a transpose-reduction over the lockstep rows so that lane l ends up owning
+// (row, batch) = (l / B, l % B)) take the shapes the tensor-core kernels do
+// not, and the tree step for 1-2 rows.
 #include <math.h>
 
 #include <algorithm>
@@ -1410,10 +1413,10 @@ __global__ void __launch_bounds__(kFfnWarps * 32) ffn_kernel(FfnParams p) {
 }
 
 // ---------------------------------------------------------------- fused FFN, bulk copies
-// The whole FFN for 1-2 lockstep rows with the weights through the copy
-// engine: CTA c takes tiles of 8 u elements (16 rows: gate and up row of each
-// element, the tensor-core GEMV tile above) and, as the next ring item of
-// each tile, the 8 matching rows of Wd^T.  A producer warp issues every copy
+// The whole FFN (up to 16 lockstep rows per launch, d <= 1024) with the
+// weights through the copy engine: CTA c takes tiles of 8 u elements (16
+// rows: gate and up row of each element, the tensor-core GEMV tile above)
+// and, as the next ring item of each tile, the 8 matching rows of Wd^T.  A producer warp issues every copy
 // it can before the dependency wait; the consumers stage RMSNorm(x_in),
 // form u = silu(gate) * up (rounded to bf16) per tile, fold u into this
 // CTA's down-projection partials (registers, 4 output columns per thread),
