@@ -119,3 +119,33 @@ def test_decode_gemv_gives_up_then_recovers():
     got = good.step(ids[:, -1])
     good.check_status(sync=True)
     assert (got.float() - want.float()).abs().max().item() < 1e-2
+
+
+def test_persistent_step_gives_up_then_recovers():
+    """The persistent step kernel (step_kernel="persistent"): with the limit at
+    0 every hand-off spin and every ring wait gives up at its first poll, the
+    kernel returns with DH_ERR_TIMEOUT in the status word (raised by the
+    decoder), and a fresh decoder is correct afterwards."""
+    from dispatcher_b200 import FusedGraphedHybridDecoder
+    cfg = small_config()
+    model = DispatcherHybridForCausalLM(cfg, seed=1, nondegenerate=True).to("cuda", torch.bfloat16)
+    ids = torch.randint(0, cfg.vocab_size - 1, (1, 40), generator=torch.Generator().manual_seed(4))
+    ids = ids.cuda()
+    ref = FusedGraphedHybridDecoder(model, step_kernel="persistent")
+    ref.prefill(ids)
+    assert ref.persistent
+    want = ref.step(ids[:, -1])
+    ref.check_status(sync=True)
+    bad = FusedGraphedHybridDecoder(model, step_kernel="persistent")
+    bad.prefill(ids)
+    bad.check_status(sync=True)
+    with wait_limit(0):       # launches read the limit (a captured graph keeps it)
+        bad._capture()
+        bad.step(ids[:, -1])
+    with pytest.raises(DispatcherB200Error, match="DH_ERR_TIMEOUT"):
+        bad.check_status(sync=True)
+    good = FusedGraphedHybridDecoder(model, step_kernel="persistent")
+    good.prefill(ids)
+    got = good.step(ids[:, -1])
+    good.check_status(sync=True)
+    assert (got.float() - want.float()).abs().max().item() < 1e-2
