@@ -428,7 +428,7 @@ __device__ __forceinline__ void csync_bulk() { asm volatile("bar.sync 1, 256;" :
 
 template <int NT, class Epi>
 __global__ void __launch_bounds__(kBulkThreads, 1)
-    gemv_bulk_kernel(GemvIn in, Epi epi_in, int nslots, int* status, uint32_t wait_limit) {
+    gemv_bulk_kernel(GemvIn in, Epi epi_in, int nslots, int wpt, int* status, uint32_t wait_limit) {
   extern __shared__ __align__(128) unsigned char bulk_smem[];
   Epi epi = epi_in;
   epi.bind();
@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < nslots; ++i) {
       mbar_init(&sh->full[i], 1);
-      mbar_init(&sh->empty[i], kTcWarps);
+      mbar_init(&sh->empty[i], wpt ? 1 : kTcWarps);  // warp per tile: the slot's own warp
     }
     sh->abort = 0;
     fence_barrier_init();
@@ -559,6 +559,60 @@ __global__ void __launch_bounds__(kBulkThreads, 1)
   }
   csync_bulk();
 
+  if (wpt) {
+    // warp per tile (one pass, many tiles per CTA): consumer warp w owns ring
+    // slot w and takes items w, w + nslots, ... whole (every chunk of K, two
+    // accumulator chains), so it never waits on its slot more than one fill
+    // ahead; it releases the slot and stores its own results, with no
+    // barrier and no cross-warp reduction per tile
+    if (warp >= nslots) return;
+    for (int item = warp; item < nitems; item += nslots) {
+      const int slot = warp;
+      const int tile = blockIdx.x + item * gridDim.x;
+      bool ok = !*reinterpret_cast<volatile int*>(&sh->abort);
+      if (ok && !mbar_wait(&sh->full[slot], (uint32_t)((item / nslots) & 1), status, wait_limit)) {
+        sh->abort = 1;
+        ok = false;
+      }
+      float ac[2][NT][4];
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) ac[q][nt][0] = ac[q][nt][1] = ac[q][nt][2] = ac[q][nt][3] = 0.f;
+      if (ok) {
+        const uint8_t* sb = slots + (size_t)slot * kBulkSlotBytes;
+#pragma unroll 2
+        for (int c = 0; c < nchunks; ++c) {
+          const uint4 wa = *reinterpret_cast<const uint4*>(sb + g * kBulkRowBytes + c * 64 + t4 * 16);
+          const uint4 wb = *reinterpret_cast<const uint4*>(sb + (g + 8) * kBulkRowBytes + c * 64 + t4 * 16);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)(nt * 8 + g) * KP + c * 32 + 8 * t4);
+            mma_bf16_16816(ac[c & 1][nt], wa.x, wb.x, wa.y, wb.y, xv.x, xv.y);
+            mma_bf16_16816(ac[c & 1][nt], wa.z, wb.z, wa.w, wb.w, xv.z, xv.w);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->empty[slot]);
+      const bool live = ok && !*reinterpret_cast<volatile int*>(&sh->abort);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float v = ac[0][nt][e] + ac[1][nt][e];
+          const float other = __shfl_xor_sync(0xffffffffu, v, 4);  // row g ^ 1, same column
+          const int r = g + (e >> 1) * 8, b = nt * 8 + 2 * t4 + (e & 1);
+          const int u = tile * 8 + (r >> 1);
+          if (live && u < nunits && b < batch) {
+            const __nv_bfloat16 *ra, *rb2;
+            const bool has1 = epi.rows(u, ra, rb2);
+            epi.store(u, b, r & 1, v, other, has1);
+          }
+        }
+    }
+    return;
+  }
   float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
@@ -642,8 +696,10 @@ int launch_gemv_bulk(const GemvIn& in, const Epi& epi, int nunits, int* status, 
   }
   const int ntiles = (nunits + 7) / 8;
   const int grid = std::min(ntiles, sm_count());
+  // warp per tile when every CTA has 8 tiles or more of one pass (the logits)
+  const int wpt = in.K <= 1024 && ntiles >= 8 * grid ? 1 : 0;
   return launch_pdl(gemv_bulk_kernel<NT, Epi>, dim3(grid), dim3(kBulkThreads), smem, st, in, epi, nslots,
-                    status, wait_limit())
+                    wpt, status, wait_limit())
              ? set_error(DH_ERR_CUDA, "gemv_bulk_kernel launch: %s", cudaGetErrorString(cudaGetLastError()))
              : DH_OK;
 }
