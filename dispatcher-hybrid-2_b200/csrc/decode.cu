@@ -1097,6 +1097,238 @@ __global__ void __launch_bounds__(64) tree_recur_kernel(TreeRecurParams p) {
   p.y[(size_t)b * d + h * hd + c] = f2bf(V);
 }
 
+// ---------------------------------------------------------------- W3 GEMV with the gate readouts
+// The tree block's input side and its gate readouts in one launch (1-4
+// lockstep rows).  The W3 GEMV of the bulk-copy kernel above (v0, A, B_hist
+// rows), and for every tile that produces 16 columns k of A, one more ring
+// item: rows k of the transposed gate weights, all (level, gate, head)
+// readouts at once (one bulk copy of 16 x L*NP bf16).  The readouts are sums
+// over k, so the tile adds its share into the fp32 pre-activations:
+//   pre[b, l*NP + g*H + h] += sum_k W_g[l, h, k] * relu(A[b, k] + m B_hist[b, t - 2^l, k])^2
+// with A rounded to bf16 as stored, m the level mask (source position exists
+// and, with document tracking, lies in the same document), fp32 arithmetic
+// as in the (level, head) tree kernel.  The level recurrence then runs in
+// tree_recur_kernel, which reads and clears pre.  The gate weights are read
+// once per step in total; no hidden vector of the gates exists in HBM.
+struct MixerGatesParams {
+  const float* x;
+  const __nv_bfloat16 *norm_w, *w3;
+  __nv_bfloat16 *v0, *a, *bh;
+  const int64_t* t_buf;
+  const __nv_bfloat16* wgT;  // (d, L*NP): row k, column l*NP + g*H + h = W_g[l, h, k]
+  float* pre;                // (batch, L*NP)
+  const int* doc;            // nullable
+  int d, batch, max_len, L, NP, H3;
+};
+
+constexpr int kGateMaxL = 16;
+
+template <int NT>
+__global__ void __launch_bounds__(kBulkThreads, 1)
+    mixer_gates_kernel(MixerGatesParams p, int nslots, int* status, uint32_t wait_limit) {
+  extern __shared__ __align__(128) unsigned char mg_smem[];
+  const int d = p.d, K = d, KP = K + 32, batch = p.batch, LNP = p.L * p.NP;
+  uint8_t* slots = mg_smem;                                                  // [nslots][16][2112]
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(mg_smem + (size_t)nslots * kBulkSlotBytes);
+  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + bulk_xs_bytes(NT, K));
+  float* tile_out = red + kTcWarps * 16 * 16;  // [16][17]
+  float* hv = tile_out + 16 * 17;              // [4][kGateMaxL][16]
+  BulkShared* sh = reinterpret_cast<BulkShared*>(hv + 4 * kGateMaxL * 16);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nunits = 3 * d / 2, ntiles = 3 * d / 16, nchunks = K / 32;
+  const int a_lo = d / 16, a_hi = 2 * d / 16;  // tiles whose rows are A
+  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int t = (int)*p.t_buf;  // advanced only by the last kernel of a step
+  if (tid == 0) {
+    for (int i = 0; i < nslots; ++i) {
+      mbar_init(&sh->full[i], 1);
+      mbar_init(&sh->empty[i], kTcWarps);
+    }
+    sh->abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  if (warp == kTcWarps) {  // ---------------- producer (one lane)
+    if (lane != 0) return;
+    int it = 0;
+    for (int tl = 0; tl < my_tiles && !*reinterpret_cast<volatile int*>(&sh->abort); ++tl) {
+      const int tile = blockIdx.x + tl * gridDim.x;
+      const int nit = (tile >= a_lo && tile < a_hi) ? 2 : 1;
+      for (int q = 0; q < nit; ++q, ++it) {
+        const int slot = it % nslots;
+        if (it >= nslots &&
+            !mbar_wait(&sh->empty[slot], (uint32_t)(((it / nslots) - 1) & 1), status, wait_limit)) {
+          sh->abort = 1;
+          break;
+        }
+        uint8_t* dst = slots + (size_t)slot * kBulkSlotBytes;
+        if (q == 0) {  // 16 rows of W3
+          mbar_arrive_expect_tx(&sh->full[slot], (uint32_t)(16 * K * 2));
+          for (int r = 0; r < 16; ++r)
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_u32(dst + r * kBulkRowBytes)),
+                "l"(p.w3 + (size_t)(tile * 16 + r) * K), "r"((uint32_t)(K * 2)),
+                "r"(smem_u32(&sh->full[slot]))
+                : "memory");
+        } else {  // rows k0..k0+15 of the transposed gate weights, contiguous
+          const uint32_t bytes = (uint32_t)(16 * LNP * 2);
+          mbar_arrive_expect_tx(&sh->full[slot], bytes);
+          asm volatile(
+              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                  smem_u32(dst)),
+              "l"(p.wgT + (size_t)(tile * 16 - d) * LNP), "r"(bytes), "r"(smem_u32(&sh->full[slot]))
+              : "memory");
+        }
+      }
+    }
+    for (int sl = 0; sl < nslots; ++sl) {  // nothing in flight into this CTA when it exits
+      const int n_s = it / nslots + (sl < it % nslots ? 1 : 0);
+      if (n_s > 0) mbar_wait(&sh->full[sl], (uint32_t)((n_s - 1) & 1), nullptr, 1u << 20);
+    }
+    return;
+  }
+
+  // ---------------- consumers (8 warps, named barrier 1)
+  const int g = lane >> 2, t4 = lane & 3;
+  pdl_wait();
+  {  // RMSNorm(x) rows as bf16, warp per row (up to 1024 columns)
+    const int k4 = K / 4;
+    for (int rb = warp; rb < batch; rb += kTcWarps) {
+      const float* xr = p.x + (size_t)rb * K;
+      float4 v[8];
+      uint2 wn[8];
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = lane + 32 * j;
+        v[j] = i < k4 ? reinterpret_cast<const float4*>(xr)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        wn[j] = i < k4 ? *reinterpret_cast<const uint2*>(p.norm_w + 4 * i) : make_uint2(0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+      const float sc = rsqrtf(warp_sum(ss) / (float)K + kNormEps);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = lane + 32 * j;
+        if (i < k4) {
+          const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wn[j].x));
+          const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wn[j].y));
+          uint2 pk;
+          pk.x = pack2(v[j].x * sc * w01.x, v[j].y * sc * w01.y);
+          pk.y = pack2(v[j].z * sc * w23.x, v[j].w * sc * w23.y);
+          *reinterpret_cast<uint2*>(xs + (size_t)rb * KP + 4 * i) = pk;
+        }
+      }
+    }
+  }
+  csync_bulk();
+
+  int it = 0;
+  for (int tl = 0; tl < my_tiles; ++tl) {
+    const int tile = blockIdx.x + tl * gridDim.x;
+    {  // ---- the W3 tile
+      const int slot = it % nslots;
+      bool ok = !*reinterpret_cast<volatile int*>(&sh->abort);
+      if (ok && !mbar_wait(&sh->full[slot], (uint32_t)((it / nslots) & 1), status, wait_limit)) {
+        sh->abort = 1;
+        ok = false;
+      }
+      float acc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+      if (ok) {
+        const uint8_t* sb = slots + (size_t)slot * kBulkSlotBytes;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = warp * 4 + i;
+          if (c < nchunks) {
+            const uint4 wa = *reinterpret_cast<const uint4*>(sb + g * kBulkRowBytes + c * 64 + t4 * 16);
+            const uint4 wb = *reinterpret_cast<const uint4*>(sb + (g + 8) * kBulkRowBytes + c * 64 + t4 * 16);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)(nt * 8 + g) * KP + c * 32 + 8 * t4);
+              mma_bf16_16816(acc[nt], wa.x, wb.x, wa.y, wb.y, xv.x, xv.y);
+              mma_bf16_16816(acc[nt], wa.z, wb.z, wa.w, wb.w, xv.z, xv.w);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->empty[slot]);
+      ++it;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float* pr = red + (size_t)warp * 256;
+        *reinterpret_cast<float2*>(pr + g * 16 + nt * 8 + 2 * t4) = make_float2(acc[nt][0], acc[nt][1]);
+        *reinterpret_cast<float2*>(pr + (g + 8) * 16 + nt * 8 + 2 * t4) = make_float2(acc[nt][2], acc[nt][3]);
+      }
+      csync_bulk();
+      {
+        const int r = tid >> 4, col = tid & 15;
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kTcWarps; ++w) s += red[w * 256 + r * 16 + col];
+        tile_out[r * 17 + col] = s;
+      }
+      csync_bulk();
+      {  // store: rows [0, d) -> v0, [d, 2d) -> A, [2d, 3d) -> B_hist[:, t]
+        const int r = tid >> 4, b = tid & 15;
+        const int n = tile * 16 + r, seg = n / d, c = n - seg * d;
+        if (n < 3 * d && b < batch && !*reinterpret_cast<volatile int*>(&sh->abort)) {
+          const __nv_bfloat16 v = f2bf(tile_out[r * 17 + b]);
+          if (seg == 0) p.v0[(size_t)b * d + c] = v;
+          else if (seg == 1) p.a[(size_t)b * d + c] = v;
+          else p.bh[((size_t)b * p.max_len + t) * d + c] = v;
+        }
+      }
+    }
+    if (tile < a_lo || tile >= a_hi) continue;
+    {  // ---- the gate readouts' share of these 16 columns of A
+      const int k0 = tile * 16 - d;
+      for (int i = tid; i < batch * p.L * 16; i += kTcWarps * 32) {
+        const int b = i / (p.L * 16), rem = i - b * (p.L * 16), l = rem >> 4, kk = rem & 15;
+        const int src = t - (1 << l);
+        bool ok = src >= 0;
+        if (ok && p.doc) ok = p.doc[(size_t)b * p.max_len + src] == p.doc[(size_t)b * p.max_len + t];
+        const float av = bf2f(f2bf(tile_out[kk * 17 + b]));  // A as stored (bf16)
+        const float bs = ok ? bf2f(p.bh[((size_t)b * p.max_len + src) * d + k0 + kk]) : 0.f;
+        const float h = fmaxf(av + bs, 0.f);
+        hv[(b * kGateMaxL + l) * 16 + kk] = h * h;  // relu squared
+      }
+      csync_bulk();
+      const int slot = it % nslots;
+      bool ok = !*reinterpret_cast<volatile int*>(&sh->abort);
+      if (ok && !mbar_wait(&sh->full[slot], (uint32_t)((it / nslots) & 1), status, wait_limit)) {
+        sh->abort = 1;
+        ok = false;
+      }
+      if (ok) {
+        const __nv_bfloat16* wg = reinterpret_cast<const __nv_bfloat16*>(slots + (size_t)slot * kBulkSlotBytes);
+        for (int o = tid; o < LNP; o += kTcWarps * 32) {
+          const int l = o / p.NP;
+          if (o - l * p.NP >= p.H3) continue;  // padding rows of the packed gates
+          float w[16];
+#pragma unroll
+          for (int kk = 0; kk < 16; ++kk) w[kk] = bf2f(wg[(size_t)kk * LNP + o]);
+          for (int b = 0; b < batch; ++b) {
+            const float* hb = hv + (b * kGateMaxL + l) * 16;
+            float s = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < 16; ++kk) s = fmaf(w[kk], hb[kk], s);
+            atomicAdd(p.pre + (size_t)b * LNP + o, s);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->empty[slot]);
+      ++it;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- attention
 struct AttnParams {
   const __nv_bfloat16 *q, *k, *v;
@@ -1980,6 +2212,64 @@ extern "C" int dh_decode_tree_step_tc(const void* a_in, const void* b_hist, cons
                                : launch_pdl(tree_gates_tc_kernel<3>, gg, dim3(256), 0, STREAM(stream), gp);
     if (bad) return check_launch("tree_gates_tc_kernel");
     TreeRecurParams rp{pr, bi, bf, br, t_buf, doc,
+                       BFM(rg_hist) + (size_t)b0 * max_len * L * H,
+                       BF(v0) + (size_t)b0 * d, BFM(v_ring) + (size_t)b0 * S * d,
+                       BFM(y) + (size_t)b0 * d, nb, max_len, L, H, hd, np, S};
+    if (launch_pdl(tree_recur_kernel, dim3(H, nb), dim3(64), 0, STREAM(stream), rp))
+      return check_launch("tree_recur_kernel");
+  }
+  return DH_OK;
+}
+
+extern "C" int dh_decode_mixer_in_gates(const float* x, const void* norm_w, const void* w3, void* v0,
+                                        void* a_out, void* b_hist, const int64_t* t_buf,
+                                        int max_len, int batch, int d, const void* w_gates_t,
+                                        int np, int L, int H, float* pre, const int* doc_hist,
+                                        int* status, void* stream) {
+  DH_REQUIRE(x && norm_w && w3 && v0 && a_out && b_hist && t_buf && w_gates_t && pre, DH_ERR_ARG,
+             "dh_decode_mixer_in_gates: null pointer");
+  DH_REQUIRE(batch >= 1 && batch <= 4 && d % 32 == 0 && d >= 32 && d <= 1024 && L >= 1 &&
+                 L <= kGateMaxL && np % 16 == 0 && np >= 3 * H && 16 * L * np * 2 <= kBulkSlotBytes &&
+                 max_len > 0,
+             DH_ERR_SHAPE, "dh_decode_mixer_in_gates: unsupported sizes (batch %d, d %d, L %d, np %d)",
+             batch, d, L, np);
+  DH_REQUIRE(aligned16(x) && aligned16(w3) && aligned16(w_gates_t), DH_ERR_ARG,
+             "dh_decode_mixer_in_gates: pointers must be 16-byte aligned");
+  constexpr size_t kMaxSmem = 227 * 1024;
+  const size_t fixed = bulk_xs_bytes(1, d) + (size_t)kTcWarps * 16 * 16 * 4 + 16 * 17 * 4 +
+                       4 * kGateMaxL * 16 * 4 + sizeof(BulkShared) + 16;
+  const int nslots = (int)std::min<size_t>(kBulkMaxSlots, (kMaxSmem - fixed) / kBulkSlotBytes);
+  const size_t smem = fixed + (size_t)nslots * kBulkSlotBytes;
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaFuncSetAttribute(mixer_gates_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    configured_dev = dev;
+  }
+  MixerGatesParams p{x, BF(norm_w), BF(w3), BFM(v0), BFM(a_out), BFM(b_hist), t_buf, BF(w_gates_t),
+                     pre, doc_hist, d, batch, max_len, L, np, 3 * H};
+  const int grid = std::min(3 * d / 16, sm_count());
+  if (launch_pdl(mixer_gates_kernel<1>, dim3(grid), dim3(kBulkThreads), smem, STREAM(stream), p, nslots,
+                 status, wait_limit()))
+    return check_launch("mixer_gates_kernel");
+  return DH_OK;
+}
+
+extern "C" int dh_decode_tree_recur(const float* bi, const float* bf, const float* br,
+                                    const int64_t* t_buf, float* pre, int np, void* rg_hist,
+                                    const void* v0, void* v_ring, void* y, const int* doc_hist,
+                                    int batch, int max_len, int L, int H, int hd, void* stream) {
+  DH_REQUIRE(bi && bf && br && t_buf && pre && rg_hist && v0 && v_ring && y, DH_ERR_ARG,
+             "dh_decode_tree_recur: null pointer");
+  DH_REQUIRE(batch >= 1 && L >= 1 && L <= 16 && H >= 1 && hd >= 1 && hd <= 64 && np >= 3 * H,
+             DH_ERR_SHAPE, "dh_decode_tree_recur: unsupported sizes (L=%d H=%d hd=%d np=%d)", L, H,
+             hd, np);
+  const int d = H * hd, S = (1 << (L + 1)) - 2;
+  for (int b0 = 0; b0 < batch; b0 += kMaxRows) {
+    const int nb = batch - b0 < kMaxRows ? batch - b0 : kMaxRows;
+    TreeRecurParams rp{pre + (size_t)b0 * L * np, bi, bf, br, t_buf,
+                       doc_hist ? doc_hist + (size_t)b0 * max_len : nullptr,
                        BFM(rg_hist) + (size_t)b0 * max_len * L * H,
                        BF(v0) + (size_t)b0 * d, BFM(v_ring) + (size_t)b0 * S * d,
                        BFM(y) + (size_t)b0 * d, nb, max_len, L, H, hd, np, S};

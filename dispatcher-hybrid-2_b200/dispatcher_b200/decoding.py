@@ -182,17 +182,24 @@ class FusedGraphedHybridDecoder:
                     lay["w_downT"] = lay["w_down"].t().contiguous()
         # tree blocks of 3..16 rows: tensor-core gate readouts over the packed
         # gate rows (all heads of a level at once), pre-activations in fp32
-        self.tree_tc = (not self.persistent and batch > 2 and 3 * H <= 48 and d % 32 == 0
-                        and hd <= 64)
+        np_ = ((3 * H + 15) // 16) * 16
+        # 1-4 rows: the gate readouts are folded into the W3 GEMV (each tile of
+        # A adds its columns' share), then a recurrence kernel; 3-16 rows
+        # otherwise: the readouts of all heads per level on the tensor cores
+        self.gates_fused = (not self.persistent and batch <= 4 and d % 32 == 0 and d <= 1024
+                            and hd <= 64 and L <= 16 and 16 * L * np_ * 2 <= 33792)
+        self.tree_tc = (not self.persistent and not self.gates_fused and batch > 2
+                        and 3 * H <= 48 and d % 32 == 0 and hd <= 64)
         self.pre = None
-        if self.tree_tc:
+        if self.tree_tc or self.gates_fused:
             from .ops import pack_gate_weights
-            np_ = ((3 * H + 15) // 16) * 16
             self.pre = torch.zeros(batch, L, np_, device=dev, dtype=f32)
             for lay in self.w.layers:
                 if lay["kind"] == "tree" and "w_gates_np" not in lay:
                     lay["w_gates_np"], _, lay["gates_np"] = pack_gate_weights(
                         lay["wi"], lay["wf"], lay["wr"], lay["bi"], lay["bf"], lay["br"])
+                if self.gates_fused and lay["kind"] == "tree" and "w_gates_t" not in lay:
+                    lay["w_gates_t"] = lay["w_gates_np"].t().contiguous()   # (gh, L * np)
         self._step_params = None
         if self.persistent:
             from .step_params import build_step_params
@@ -220,7 +227,15 @@ class FusedGraphedHybridDecoder:
         tree_ctr = self.counters[:H]
         attn_ctr = self.counters[H:]
         for lay, cache in zip(W.layers, self.caches):
-            if lay["kind"] == "tree":
+            if lay["kind"] == "tree" and self.gates_fused:
+                call("dh_decode_mixer_in_gates", P(self.x), P(lay["norm1"]), P(lay["w3"]),
+                     P(self.v0), P(self.a), P(cache.B_hist), P(self.t_buf), self.max_len, B, d,
+                     P(lay["w_gates_t"]), lay["gates_np"], L, H, P(self.pre), P(self.doc_hist),
+                     P(self.status), s)
+                call("dh_decode_tree_recur", P(lay["bi"]), P(lay["bf"]), P(lay["br"]),
+                     P(self.t_buf), P(self.pre), lay["gates_np"], P(cache.rg_hist), P(self.v0),
+                     P(cache.V_ring), P(self.y), P(self.doc_hist), B, self.max_len, L, H, hd, s)
+            elif lay["kind"] == "tree":
                 call("dh_decode_mixer_in", P(self.x), P(lay["norm1"]), P(lay["w3"]), P(self.v0),
                      P(self.a), P(cache.B_hist), P(self.t_buf), self.max_len, B, d,
                      P(self.status), s)

@@ -112,6 +112,32 @@ DH_API int dh_decode_tree_step_tc(const void* a_in, const void* b_hist, const vo
                                   int batch, int max_len, int L, int H, int hd, int gh,
                                   void* stream);
 
+/* Tree block input side with the gate readouts folded in (1..4 rows; the
+ * work of dh_decode_mixer_in plus the readout half of dh_decode_tree_step,
+ * fused_step.py:26-59): the W3 GEMV as dh_decode_mixer_in, and each 16
+ * columns of A it produces add their share of every level's admit / forget /
+ * transmit readouts, sum_k W_g[l, h, k] relu(A[b, k] + m B_hist[b, t - 2^l, k])^2
+ * (m: the level mask, with doc_hist (nullable) also the document mask), into
+ * pre (fp32 (batch, L * np), zero on entry; dh_decode_tree_recur reads and
+ * clears it).  w_gates_t: bf16 (d, L * np), the transpose of the packed
+ * gate rows of dh_decode_tree_step_tc (column l*np + g*H + h).  d a multiple
+ * of 32 and at most 1024; 16 * L * np * 2 bytes at most 33792. */
+DH_API int dh_decode_mixer_in_gates(const float* x, const void* norm_w, const void* w3, void* v0,
+                                    void* a_out, void* b_hist, const int64_t* t_buf, int max_len,
+                                    int batch, int d, const void* w_gates_t, int np, int L, int H,
+                                    float* pre, const int* doc_hist, int* status, void* stream);
+
+/* The level recurrence of a tree block from summed gate pre-activations
+ * (fused_step.py:62-88): sigmoid gates with the biases bi/bf/br (L, H) and
+ * the level / document mask, rg_hist[:, t], every level's ring slot at t and
+ * y (batch, d) bf16; pre (batch, L * np) is read and left zero.  One thread
+ * per channel and row, every level's history fetched before the dependency
+ * wait.  hd <= 64. */
+DH_API int dh_decode_tree_recur(const float* bi, const float* bf, const float* br,
+                                const int64_t* t_buf, float* pre, int np, void* rg_hist,
+                                const void* v0, void* v_ring, void* y, const int* doc_hist,
+                                int batch, int max_len, int L, int H, int hd, void* stream);
+
 /* x += y . W^T (W: d_out x k, bf16; y bf16 (batch, k)): linear_out and
  * linear_down with the residual add (decoding.py:487-488, 434-435).  x_copy
  * (nullable) receives a copy of the updated x (the input of dh_decode_ffn). */

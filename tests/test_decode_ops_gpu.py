@@ -75,3 +75,91 @@ def test_fused_ffn(B, d, ff):
     # sums: a few elements can land one bf16 ulp apart
     err = (x - want).abs().max().item()
     assert err < 1e-2 * (1 + want.abs().max().item()), err
+
+
+def _tree_state(B, d, H, L, T, docs, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    hd = d // H
+    bf16 = torch.bfloat16
+    st = dict(
+        x=torch.randn(B, d, device="cuda", generator=g),
+        norm_w=(1 + 0.1 * torch.randn(d, device="cuda", generator=g)).to(bf16),
+        w3=(torch.randn(3 * d, d, device="cuda", generator=g) * d ** -0.5).to(bf16),
+        wi=(torch.randn(L, H, d, device="cuda", generator=g) * d ** -0.5).to(bf16),
+        wf=(torch.randn(L, H, d, device="cuda", generator=g) * d ** -0.5).to(bf16),
+        wr=(torch.randn(L, H, d, device="cuda", generator=g) * d ** -0.5).to(bf16),
+        bi=0.5 * torch.randn(L, H, device="cuda", generator=g),
+        bf=0.5 * torch.randn(L, H, device="cuda", generator=g),
+        br=0.5 * torch.randn(L, H, device="cuda", generator=g),
+        B_hist=torch.randn(B, T + 1, d, device="cuda", generator=g).to(bf16),
+        rg_hist=torch.rand(B, T + 1, L, H, device="cuda", generator=g).to(bf16),
+        V_ring=torch.randn(B, 2 ** (L + 1) - 2, d, device="cuda", generator=g).to(bf16),
+        t_buf=torch.full((1,), T, dtype=torch.long, device="cuda"),
+        doc=None,
+    )
+    if docs:
+        # a document boundary every ~T/5 positions, different per row
+        sep = (torch.rand(B, T + 1, device="cuda", generator=g) < 5.0 / T).int()
+        st["doc"] = torch.cumsum(sep, 1, dtype=torch.int32) - sep
+    return st, hd
+
+
+@pytest.mark.parametrize("B", [1, 4])
+@pytest.mark.parametrize("H,L,T", [(2, 3, 3), (2, 16, 40000), (16, 16, 33000), (4, 12, 1500)])
+@pytest.mark.parametrize("docs", [False, True])
+def test_mixer_in_gates_matches_separate_launches(B, H, L, T, docs):
+    """dh_decode_mixer_in_gates + dh_decode_tree_recur (W3 GEMV with the
+    gate readouts folded in) against dh_decode_mixer_in + dh_decode_tree_step
+    on the same state: every level live (t >= 2^(L-1)) or some masked (t <
+    2^(L-1)), 2..16 heads (np 16 and 48), up to 16 levels, with and without
+    document masks.  v0 / A / B_hist[:, t] come from the same kind of
+    tensor-core GEMV; the gate pre-activations are fp32 sums in another
+    order, so the sigmoid gates and what follows may differ by one bf16 ulp."""
+    d = 128
+    st, hd = _tree_state(B, d, H, L, T, docs, seed=B * 31 + H * 7 + L)
+    from dispatcher_b200.ops import pack_gate_weights
+    wg_np, _, np_ = pack_gate_weights(st["wi"], st["wf"], st["wr"], st["bi"], st["bf"], st["br"])
+    wg_t = wg_np.t().contiguous()
+    max_len = T + 1
+    outs = []
+    for fused in (False, True):
+        v0 = torch.zeros(B, d, device="cuda", dtype=torch.bfloat16)
+        a = torch.zeros_like(v0)
+        y = torch.zeros_like(v0)
+        bh, rg, vr = st["B_hist"].clone(), st["rg_hist"].clone(), st["V_ring"].clone()
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        s = _stream()
+        if fused:
+            pre = torch.zeros(B, L * np_, device="cuda")
+            call("dh_decode_mixer_in_gates", _p(st["x"]), _p(st["norm_w"]), _p(st["w3"]), _p(v0),
+                 _p(a), _p(bh), _p(st["t_buf"]), max_len, B, d, _p(wg_t), np_, L, H, _p(pre),
+                 _p(st["doc"]), _p(status), s)
+            call("dh_decode_tree_recur", _p(st["bi"]), _p(st["bf"]), _p(st["br"]),
+                 _p(st["t_buf"]), _p(pre), np_, _p(rg), _p(v0), _p(vr), _p(y), _p(st["doc"]),
+                 B, max_len, L, H, hd, s)
+        else:
+            ig = torch.zeros(B, L, H, device="cuda")
+            fg = torch.zeros_like(ig)
+            ctr = torch.zeros(H, dtype=torch.int32, device="cuda")
+            call("dh_decode_mixer_in", _p(st["x"]), _p(st["norm_w"]), _p(st["w3"]), _p(v0),
+                 _p(a), _p(bh), _p(st["t_buf"]), max_len, B, d, _p(status), s)
+            call("dh_decode_tree_step", _p(a), _p(bh), _p(st["wi"]), _p(st["wf"]), _p(st["wr"]),
+                 _p(st["bi"]), _p(st["bf"]), _p(st["br"]), _p(st["t_buf"]), _p(ig), _p(fg),
+                 _p(rg), _p(v0), _p(vr), _p(y), _p(ctr), _p(st["doc"]), B, max_len, L, H, hd, d,
+                 s)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        if fused:
+            assert int(torch.count_nonzero(pre)) == 0      # left zero for the next step
+        outs.append((v0, a, bh, rg, vr, y))
+    (v0s, as_, bhs, rgs, vrs, ys), (v0f, af, bhf, rgf, vrf, yf) = outs
+    for u, v in ((v0s, v0f), (as_, af), (bhs, bhf)):
+        assert torch.allclose(u.float(), v.float(), rtol=2 ** -7, atol=1e-3)
+    assert torch.equal(bhs[:, :T], bhf[:, :T])
+    # one bf16 ulp of values in (0, 1) for the gates, of the output scale after
+    assert (rgs.float() - rgf.float()).abs().max().item() <= 2 ** -8
+    scale = 1 + ys.float().abs().max().item()
+    assert (ys.float() - yf.float()).abs().max().item() <= 2e-2 * scale
+    assert (vrs.float() - vrf.float()).abs().max().item() <= 2e-2 * (1 + vrs.float().abs().max().item())
+    # untouched history rows stay bit-identical
+    assert torch.equal(rgs[:, :T], rgf[:, :T])
