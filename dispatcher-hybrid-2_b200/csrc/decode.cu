@@ -1030,6 +1030,7 @@ __global__ void __launch_bounds__(256) tree_gates_tc_kernel(TreeGatesTcParams p)
 // history value fetched up front (ring slots of earlier positions, written by
 // earlier steps), then the short serial chain (fused_step.py:62-88 semantics,
 // fp32 state, each level's value stored into its ring slot at t).
+
 struct TreeRecurParams {
   float* pre;  // (batch, L, NP): read and cleared
   const float *bi, *bf, *br;
@@ -1042,11 +1043,14 @@ struct TreeRecurParams {
   int batch, max_len, L, H, hd, NP, S;
 };
 
-__global__ void __launch_bounds__(64) tree_recur_kernel(TreeRecurParams p) {
+template <int RPB>
+__global__ void __launch_bounds__(64 * RPB) tree_recur_kernel(TreeRecurParams p) {
   constexpr int LMAX = 16;
-  __shared__ float s_f[LMAX], s_c[LMAX];
+  __shared__ float s_f_all[RPB][LMAX], s_c_all[RPB][LMAX];
   pdl_trigger();
-  const int h = blockIdx.x, b = blockIdx.y, c = threadIdx.x;
+  const int h = blockIdx.x, b = blockIdx.y * blockDim.y + threadIdx.y, c = threadIdx.x;
+  float* s_f = s_f_all[threadIdx.y];
+  float* s_c = s_c_all[threadIdx.y];  // blockDim.y == p.batch: every thread has a row
   const int L = p.L, H = p.H, hd = p.hd, d = H * hd;
   const int t = (int)*p.t_buf;  // < max_len: positions and slots fit 32 bits
   __nv_bfloat16* ringb = p.ring + (size_t)b * p.S * d + h * hd + c;
@@ -1095,6 +1099,16 @@ __global__ void __launch_bounds__(64) tree_recur_kernel(TreeRecurParams p) {
     }
   }
   p.y[(size_t)b * d + h * hd + c] = f2bf(V);
+}
+
+// RPB rows per block: every row of a head in one block for 1-4 lockstep
+// rows (measured faster there), one block per (head, row) above
+constexpr int kRecurRows = 16;
+
+template <int RPB>
+int launch_tree_recur(const TreeRecurParams& rp, int H, int nb, cudaStream_t st) {
+  return RPB == 1 ? launch_pdl(tree_recur_kernel<1>, dim3(H, nb), dim3(64), 0, st, rp)
+                  : launch_pdl(tree_recur_kernel<RPB>, dim3(H, 1), dim3(64, nb), 0, st, rp);
 }
 
 // ---------------------------------------------------------------- W3 GEMV with the gate readouts
@@ -2215,7 +2229,8 @@ extern "C" int dh_decode_tree_step_tc(const void* a_in, const void* b_hist, cons
                        BFM(rg_hist) + (size_t)b0 * max_len * L * H,
                        BF(v0) + (size_t)b0 * d, BFM(v_ring) + (size_t)b0 * S * d,
                        BFM(y) + (size_t)b0 * d, nb, max_len, L, H, hd, np, S};
-    if (launch_pdl(tree_recur_kernel, dim3(H, nb), dim3(64), 0, STREAM(stream), rp))
+    if ((nb <= 4 ? launch_tree_recur<kRecurRows>(rp, H, nb, STREAM(stream))
+                : launch_tree_recur<1>(rp, H, nb, STREAM(stream))))
       return check_launch("tree_recur_kernel");
   }
   return DH_OK;
@@ -2273,7 +2288,8 @@ extern "C" int dh_decode_tree_recur(const float* bi, const float* bf, const floa
                        BFM(rg_hist) + (size_t)b0 * max_len * L * H,
                        BF(v0) + (size_t)b0 * d, BFM(v_ring) + (size_t)b0 * S * d,
                        BFM(y) + (size_t)b0 * d, nb, max_len, L, H, hd, np, S};
-    if (launch_pdl(tree_recur_kernel, dim3(H, nb), dim3(64), 0, STREAM(stream), rp))
+    if ((nb <= 4 ? launch_tree_recur<kRecurRows>(rp, H, nb, STREAM(stream))
+                : launch_tree_recur<1>(rp, H, nb, STREAM(stream))))
       return check_launch("tree_recur_kernel");
   }
   return DH_OK;
