@@ -1146,8 +1146,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1)
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(mg_smem + (size_t)nslots * kBulkSlotBytes);
   float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + bulk_xs_bytes(NT, K));
   float* tile_out = red + kTcWarps * 16 * 16;  // [16][17]
-  float* hv = tile_out + 16 * 17;              // [4][kGateMaxL][16]
-  BulkShared* sh = reinterpret_cast<BulkShared*>(hv + 4 * kGateMaxL * 16);
+  float* hv = tile_out + 16 * 17;              // [8 NT][kGateMaxL][16]
+  BulkShared* sh = reinterpret_cast<BulkShared*>(hv + NT * 8 * kGateMaxL * 16);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nunits = 3 * d / 2, ntiles = 3 * d / 16, nchunks = K / 32;
   const int a_lo = d / 16, a_hi = 2 * d / 16;  // tiles whose rows are A
@@ -2243,7 +2243,7 @@ extern "C" int dh_decode_mixer_in_gates(const float* x, const void* norm_w, cons
                                         int* status, void* stream) {
   DH_REQUIRE(x && norm_w && w3 && v0 && a_out && b_hist && t_buf && w_gates_t && pre, DH_ERR_ARG,
              "dh_decode_mixer_in_gates: null pointer");
-  DH_REQUIRE(batch >= 1 && batch <= 4 && d % 32 == 0 && d >= 32 && d <= 1024 && L >= 1 &&
+  DH_REQUIRE(batch >= 1 && batch <= 8 && d % 32 == 0 && d >= 32 && d <= 1024 && L >= 1 &&
                  L <= kGateMaxL && np % 16 == 0 && np >= 3 * H && 16 * L * np * 2 <= kBulkSlotBytes &&
                  max_len > 0,
              DH_ERR_SHAPE, "dh_decode_mixer_in_gates: unsupported sizes (batch %d, d %d, L %d, np %d)",
@@ -2252,7 +2252,7 @@ extern "C" int dh_decode_mixer_in_gates(const float* x, const void* norm_w, cons
              "dh_decode_mixer_in_gates: pointers must be 16-byte aligned");
   constexpr size_t kMaxSmem = 227 * 1024;
   const size_t fixed = bulk_xs_bytes(1, d) + (size_t)kTcWarps * 16 * 16 * 4 + 16 * 17 * 4 +
-                       4 * kGateMaxL * 16 * 4 + sizeof(BulkShared) + 16;
+                       (size_t)8 * kGateMaxL * 16 * 4 + sizeof(BulkShared) + 16;
   const int nslots = (int)std::min<size_t>(kBulkMaxSlots, (kMaxSmem - fixed) / kBulkSlotBytes);
   const size_t smem = fixed + (size_t)nslots * kBulkSlotBytes;
   static thread_local int configured_dev = -1;
@@ -2265,6 +2265,7 @@ extern "C" int dh_decode_mixer_in_gates(const float* x, const void* norm_w, cons
   MixerGatesParams p{x, BF(norm_w), BF(w3), BFM(v0), BFM(a_out), BFM(b_hist), t_buf, BF(w_gates_t),
                      pre, doc_hist, d, batch, max_len, L, np, 3 * H};
   const int grid = std::min(3 * d / 16, sm_count());
+  // one 8-column mma tile of lockstep rows (up to 8 rows)
   if (launch_pdl(mixer_gates_kernel<1>, dim3(grid), dim3(kBulkThreads), smem, STREAM(stream), p, nslots,
                  status, wait_limit()))
     return check_launch("mixer_gates_kernel");

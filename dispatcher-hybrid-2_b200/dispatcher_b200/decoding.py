@@ -183,10 +183,11 @@ class FusedGraphedHybridDecoder:
         # tree blocks of 3..16 rows: tensor-core gate readouts over the packed
         # gate rows (all heads of a level at once), pre-activations in fp32
         np_ = ((3 * H + 15) // 16) * 16
-        # 1-4 rows: the gate readouts are folded into the W3 GEMV (each tile of
-        # A adds its columns' share), then a recurrence kernel; 3-16 rows
-        # otherwise: the readouts of all heads per level on the tensor cores
-        self.gates_fused = (not self.persistent and batch <= 4 and d % 32 == 0 and d <= 1024
+        # up to 8 rows: the gate readouts are folded into the W3 GEMV (each
+        # tile of A adds its columns' share), then a recurrence kernel; 9-16
+        # rows (or more than 16 levels, d above 1024, from 3 rows): the
+        # readouts of all heads per level as their own tensor-core launch
+        self.gates_fused = (not self.persistent and batch <= 8 and d % 32 == 0 and d <= 1024
                             and hd <= 64 and L <= 16 and 16 * L * np_ * 2 <= 33792)
         self.tree_tc = (not self.persistent and not self.gates_fused and batch > 2
                         and 3 * H <= 48 and d % 32 == 0 and hd <= 64)

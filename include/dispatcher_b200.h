@@ -112,7 +112,7 @@ DH_API int dh_decode_tree_step_tc(const void* a_in, const void* b_hist, const vo
                                   int batch, int max_len, int L, int H, int hd, int gh,
                                   void* stream);
 
-/* Tree block input side with the gate readouts folded in (1..4 rows; the
+/* Tree block input side with the gate readouts folded in (1..8 rows; the
  * work of dh_decode_mixer_in plus the readout half of dh_decode_tree_step,
  * fused_step.py:26-59): the W3 GEMV as dh_decode_mixer_in, and each 16
  * columns of A it produces add their share of every level's admit / forget /

@@ -62,13 +62,14 @@ def test_decoder_matches_forward_small_seed0(small_s0):
     _compare(*small_s0)
 
 
-@pytest.mark.parametrize("batch", [3, 9])
-def test_decoder_batched(small_nd, batch):
-    """3 rows: the tree gate readouts folded into the W3 GEMV (1..4 rows);
-    9 rows: the readouts of all heads per level as a tensor-core GEMM
-    (5..16 rows) and two 8-column mma tiles in every GEMV."""
+@pytest.mark.parametrize("batch,mode", [(3, "fused"), (8, "fused"), (9, "tree_tc")])
+def test_decoder_batched(small_nd, batch, mode):
+    """Up to 8 rows the tree gate readouts are folded into the W3 GEMV (one
+    8-column mma tile of lockstep rows); from 9 rows they are their own
+    tensor-core launch over all heads per level, and every GEMV takes two
+    8-column tiles."""
     dec = _compare(*small_nd, batch=batch, seed=5)[0]
-    assert dec.gates_fused if batch <= 4 else dec.tree_tc
+    assert dec.gates_fused if mode == "fused" else dec.tree_tc
 
 
 def test_prefill_logits_match_forward(small_nd):
