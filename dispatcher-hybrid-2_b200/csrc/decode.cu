@@ -1112,7 +1112,7 @@ int launch_tree_recur(const TreeRecurParams& rp, int H, int nb, cudaStream_t st)
 }
 
 // ---------------------------------------------------------------- W3 GEMV with the gate readouts
-// The tree block's input side and its gate readouts in one launch (1-4
+// The tree block's input side and its gate readouts in one launch (1-8
 // lockstep rows).  The W3 GEMV of the bulk-copy kernel above (v0, A, B_hist
 // rows), and for every tile that produces 16 columns k of A, one more ring
 // item: rows k of the transposed gate weights, all (level, gate, head)
