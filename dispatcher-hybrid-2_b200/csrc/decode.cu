@@ -936,10 +936,14 @@ struct TreeGatesTcParams {
 
 template <int MT>
 __global__ void __launch_bounds__(256) tree_gates_tc_kernel(TreeGatesTcParams p) {
-  __shared__ float red[kTcWarps][MT * 16][17];
+  // the 8 warps' partial tiles meet in one tile through shared-memory adds:
+  // 3 KB of static shared memory, small enough for the CTA to be resident
+  // beside the W3 GEMV it follows and load its gate weights before that ends
+  __shared__ float red[MT * 16][16];
   __shared__ bool s_ok[16];
   pdl_trigger();
   const int l = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < MT * 16 * 16; i += blockDim.x) (&red[0][0])[i] = 0.f;
   const int g = lane >> 2, t4 = lane & 3;
   const int gh = p.gh, NP = p.NP;
   const long long t = *p.t_buf;  // advanced only by the last kernel of a step
@@ -1009,20 +1013,15 @@ __global__ void __launch_bounds__(256) tree_gates_tc_kernel(TreeGatesTcParams p)
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      red[warp][mt * 16 + g][nt * 8 + 2 * t4] = acc[mt][nt][0];
-      red[warp][mt * 16 + g][nt * 8 + 2 * t4 + 1] = acc[mt][nt][1];
-      red[warp][mt * 16 + g + 8][nt * 8 + 2 * t4] = acc[mt][nt][2];
-      red[warp][mt * 16 + g + 8][nt * 8 + 2 * t4 + 1] = acc[mt][nt][3];
+      atomicAdd(&red[mt * 16 + g][nt * 8 + 2 * t4], acc[mt][nt][0]);
+      atomicAdd(&red[mt * 16 + g][nt * 8 + 2 * t4 + 1], acc[mt][nt][1]);
+      atomicAdd(&red[mt * 16 + g + 8][nt * 8 + 2 * t4], acc[mt][nt][2]);
+      atomicAdd(&red[mt * 16 + g + 8][nt * 8 + 2 * t4 + 1], acc[mt][nt][3]);
     }
   __syncthreads();
   for (int i = tid; i < MT * 16 * 16; i += blockDim.x) {
     const int m = i >> 4, n = i & 15;
-    if (n < p.batch) {
-      float s = 0.f;
-#pragma unroll
-      for (int w = 0; w < kTcWarps; ++w) s += red[w][m][n];
-      atomicAdd(p.pre + ((size_t)n * p.L + l) * NP + m, s);
-    }
+    if (n < p.batch) atomicAdd(p.pre + ((size_t)n * p.L + l) * NP + m, red[m][n]);
   }
 }
 
