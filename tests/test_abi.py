@@ -129,3 +129,31 @@ def test_shape_errors_are_reported_before_any_launch():
         batch, T, H, hd, L, n_lv = args
         rc = lib.dh_level_scan(p, 3072, p, p, 1024, batch, T, H, hd, L, n_lv, None, None)
         assert rc == 1 and b"dh_level_scan" in lib.dh_last_error(), args
+
+
+@pytest.mark.parametrize("batch,L,H,np_,d", [
+    (9, 12, 16, 48, 1024),    # the W3 GEMV with the readouts takes one 8-row tile
+    (1, 17, 16, 48, 1024),    # at most 16 levels
+    (1, 16, 32, 96, 1024),    # 16 rows of the transposed gate weights exceed one ring slot
+    (1, 12, 16, 48, 2048),    # d above 1024
+    (1, 12, 16, 40, 1024),    # np not a multiple of 16
+])
+def test_mixer_in_gates_rejects_unsupported_sizes_on_the_host(batch, L, H, np_, d):
+    """dh_decode_mixer_in_gates validates its sizes before any CUDA call:
+    DH_ERR_SHAPE with its name in the message (non-null dummy pointers, never
+    dereferenced)."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    rc = lib.dh_decode_mixer_in_gates(p, p, p, p, p, p, p, 4096, batch, d, p, np_, L, H, p, None,
+                                      None, None)
+    assert rc == 1, rc
+    assert lib.dh_last_error().startswith(b"dh_decode_mixer_in_gates")
+
+
+def test_tree_recur_rejects_unsupported_sizes_on_the_host():
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    for L, H, hd, np_ in ((17, 16, 64, 48), (12, 16, 65, 48), (12, 16, 64, 32)):
+        rc = lib.dh_decode_tree_recur(p, p, p, p, p, np_, p, p, p, p, None, 1, 4096, L, H, hd, None)
+        assert rc == 1, (L, H, hd, np_, rc)
+        assert lib.dh_last_error().startswith(b"dh_decode_tree_recur")
